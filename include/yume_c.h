@@ -1,0 +1,286 @@
+/*
+ * yume_c.h -- C ABI of the B200 backend for YumeLayersCore's operator layer.
+ *
+ * This is the drop-in boundary that replaces the reference's Metal-backed
+ * `GpuSession` operator API (Sources/YumeLayersCore/GpuSessionOps.swift,
+ * GpuSessionNormGrad.swift, GpuTraining.swift, GPUTensor.swift,
+ * MetalEngine.swift).  Plain pointers and sizes only: every `float*` tensor
+ * argument is a CUDA device pointer unless its name says `host`.  All calls
+ * are asynchronous on the context's stream unless documented otherwise and
+ * return a yl_status; none of them aborts or exits the process
+ * (the reference calls precondition/fatalError/exit(70): GpuSessionOps.swift:112,
+ * MetalEngine.swift:73-79, GpuTraining.swift:92-97).
+ *
+ * Layout conventions.  Reference tensors are per-image CHW, `rows` = channels
+ * and `cols` = H*W (GPUTensor.swift:9-14); conv weights are (oc, ic*k*k)
+ * (ConvGPU.swift:18); Linear weights are (oc, ic) with Y = X*W^T + b
+ * (DenoiserMLP.swift:51-54).  Batched entry points take NCHW (the reference
+ * layout with the host batch loop folded in) or NHWC via a yl_layout value.
+ */
+#ifndef YUME_C_H
+#define YUME_C_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum yl_status {
+  YL_OK = 0,
+  YL_ERR_SHAPE = 1,         /* precondition on shapes (reference: precondition crash) */
+  YL_ERR_OOM = 2,           /* allocation failed (reference: fatalError) */
+  YL_ERR_TIMEOUT = 3,       /* a wait hit its deadline (reference: exit(70)) */
+  YL_ERR_CUDA = 4,          /* CUDA runtime/driver error */
+  YL_ERR_NCCL = 5,          /* NCCL error */
+  YL_ERR_DEVICE_ASSERT = 6, /* a kernel reported an error through its error word */
+  YL_ERR_INVALID = 7,       /* bad argument (null pointer, unknown enum) */
+  YL_ERR_UNSUPPORTED = 8    /* valid request this build does not handle */
+} yl_status;
+
+typedef enum yl_layout { YL_LAYOUT_NCHW = 0, YL_LAYOUT_NHWC = 1 } yl_layout;
+
+typedef struct yl_ctx yl_ctx;
+typedef struct yl_tensor yl_tensor;
+typedef struct yl_comm yl_comm;
+typedef struct yl_trainer yl_trainer;
+
+/* Thread-local text of the last non-OK status returned on this thread. */
+const char* yl_last_error_message(void);
+const char* yl_version(void);
+
+/* ------------------------------------------------------------------ runtime
+ * Replaces MetalEngine (MetalEngine.swift:6-419: device, queue, pools) and
+ * GpuSession recording (GpuTraining.swift:4-151).  One context per GPU per
+ * host thread; context calls are not thread-safe (GpuTraining.swift:36-38). */
+yl_status yl_ctx_create(int device, yl_ctx** out);
+yl_status yl_ctx_destroy(yl_ctx* ctx);
+/* Use an external cudaStream_t (NULL restores the context's own stream). */
+yl_status yl_ctx_set_stream(yl_ctx* ctx, void* cuda_stream);
+void* yl_ctx_get_stream(yl_ctx* ctx);
+/* GpuSession.begin() (GpuTraining.swift:17-20): marks the start of a step. */
+yl_status yl_session_begin(yl_ctx* ctx);
+/* GpuSession.commit() (GpuTraining.swift:123-134): records completion, no wait. */
+yl_status yl_session_commit(yl_ctx* ctx);
+/* GpuSession.end() (GpuTraining.swift:140-145, wait :72-112): waits for the
+ * session's work with a deadline; YL_ERR_TIMEOUT instead of exit(70).  gpu_ms
+ * (may be NULL) gets the device time between begin and end, bounded by the
+ * wall time the way boundedGpuMs does (GpuWaitPolicy.swift:75-87). */
+yl_status yl_session_end(yl_ctx* ctx, double timeout_s, double* gpu_ms);
+/* Reads and clears the context's device error word (kernels write it when a
+ * bounded wait gives up or a device-side check fails). */
+yl_status yl_ctx_check_device_errors(yl_ctx* ctx);
+
+/* --------------------------------------------------------------- GPUTensor
+ * GPUTensor (GPUTensor.swift:9-143): rows x cols fp32, row-major, owned by
+ * the context's caching pool (MetalEngine.swift:33-82); release returns the
+ * block to the pool once the stream has passed it. */
+yl_status yl_tensor_create(yl_ctx* ctx, int rows, int cols, const float* host_or_null,
+                           yl_tensor** out);
+yl_status yl_tensor_release(yl_tensor* t);
+float* yl_tensor_data(yl_tensor* t);
+int yl_tensor_rows(const yl_tensor* t);
+int yl_tensor_cols(const yl_tensor* t);
+/* setData / toArray (GPUTensor.swift:54-120): synchronous copies. */
+yl_status yl_tensor_upload(yl_tensor* t, const float* host, size_t n);
+yl_status yl_tensor_download(yl_tensor* t, float* host, size_t n);
+/* getValue / setValue (GPUTensor.swift:122-142). */
+yl_status yl_tensor_get_value(yl_tensor* t, size_t index, float* value);
+yl_status yl_tensor_set_value(yl_tensor* t, size_t index, float value);
+/* GpuSession.copy / zeroFill (GpuSessionOps.swift:257-276), stream-ordered. */
+yl_status yl_copy(yl_ctx* ctx, float* dst, const float* src, size_t n);
+yl_status yl_zero_fill(yl_ctx* ctx, float* dst, size_t n);
+
+/* ------------------------------------------------- reference-mode operators
+ * One entry point per GpuSession method, same argument meaning, caller-owned
+ * outputs.  These reproduce the reference kernels' semantics exactly and are
+ * what the reference's own unit tests exercise (TestGroup3.swift:296-537). */
+
+/* matmul(_:_:transA:transB:M:N:K:) (GpuSessionOps.swift:80-108). */
+yl_status yl_matmul(yl_ctx* ctx, const float* A, const float* B, float* C, int M, int N,
+                    int K, int transA, int transB);
+/* im2col (GpuSessionOps.swift:281-300): X (ic, ih, iw) -> (ic*kh*kw, oh*ow). */
+yl_status yl_im2col(yl_ctx* ctx, const float* X, float* cols, int ic, int ih, int iw, int kh,
+                    int kw, int stride, int pad);
+/* col2im (GpuSessionOps.swift:303-333). */
+yl_status yl_col2im(yl_ctx* ctx, const float* cols, float* G, int ic, int ih, int iw, int kh,
+                    int kw, int stride, int pad, int oh, int ow);
+/* gradW(_:_:oc:kk:) (GpuSessionOps.swift:349-359): C = A * B^T, A (oc, K), B (kk, K). */
+yl_status yl_grad_w(yl_ctx* ctx, const float* A, const float* B, float* C, int oc, int kk,
+                    int K);
+/* convBackInputS1 (GpuSessionOps.swift:362-376). */
+yl_status yl_conv_back_input_s1(yl_ctx* ctx, const float* dOut, const float* W, float* dx,
+                                int ic, int oc, int ih, int iw, int k, int pad);
+/* biasRow (GpuSessionOps.swift:389-396): C[r,c] = A[r,c] + b[r]. */
+yl_status yl_bias_row(yl_ctx* ctx, const float* A, const float* b, float* C, int rows, int cols);
+/* biasRowGrad (GpuSessionOps.swift:398-417): out[r] = sum_c G[r,c]. */
+yl_status yl_bias_row_grad(yl_ctx* ctx, const float* G, float* out, int rows, int cols);
+/* addBias (GpuSessionOps.swift:146-153): C[i] = A[i] + bias[i % cols]. */
+yl_status yl_add_bias(yl_ctx* ctx, const float* A, const float* bias, float* C, int rows,
+                      int cols);
+/* sumCols (GpuSessionOps.swift:205-217): C[j] = sum_i A[i,j]. */
+yl_status yl_sum_cols(yl_ctx* ctx, const float* A, float* C, int rows, int cols);
+/* groupNorm(_:groups:) (GpuSessionOps.swift:121-131): affine-free, var >= 1e-5. */
+yl_status yl_group_norm(yl_ctx* ctx, const float* A, float* C, int rows, int cols, int groups);
+/* encodeGroupNormGrad (GpuSessionNormGrad.swift:10-24). */
+yl_status yl_group_norm_grad(yl_ctx* ctx, const float* x, const float* dy, float* out, int rows,
+                             int cols, int groups);
+
+typedef enum yl_unary_op {
+  YL_RELU = 0, YL_SIGMOID = 1, YL_TANH = 2, YL_TANH_GRAD = 3, YL_EXP = 4, YL_EXP_HALF = 5,
+  YL_SILU = 6
+} yl_unary_op;
+/* relu / sigmoid / tanh / tanhGrad / exp / expHalf (GpuSessionOps.swift:186-202,
+ * 419-442, 463-478) and SiLU (src/vae.py:11). */
+yl_status yl_unary(yl_ctx* ctx, int op, const float* A, float* C, size_t n);
+
+typedef enum yl_binary_op {
+  YL_ADD = 0, YL_SUB = 1, YL_MUL = 2, YL_RELU_GRAD = 3, YL_SIGMOID_GRAD = 4, YL_SILU_GRAD = 5
+} yl_binary_op;
+/* add / sub / mul / reluGrad / sigmoidGrad (GpuSessionOps.swift:111-172, 427-451)
+ * and the SiLU derivative. */
+yl_status yl_binary(yl_ctx* ctx, int op, const float* A, const float* B, float* C, size_t n);
+/* smul / addConst / fma / addInPlace (GpuSessionOps.swift:176, 481, 492, 453). */
+yl_status yl_smul(yl_ctx* ctx, float s, const float* A, float* C, size_t n);
+yl_status yl_add_const(yl_ctx* ctx, const float* A, float s, float* C, size_t n);
+yl_status yl_fma(yl_ctx* ctx, const float* A, const float* B, const float* D, float* C,
+                 size_t n);
+yl_status yl_add_in_place(yl_ctx* ctx, float* A, const float* B, size_t n);
+/* upsample2x / downsample2x (GpuSessionOps.swift:336-387), (c,h,w) <-> (c,2h,2w). */
+yl_status yl_upsample2x(yl_ctx* ctx, const float* X, float* Y, int c, int h, int w);
+yl_status yl_downsample2x(yl_ctx* ctx, const float* X, float* Y, int c, int h, int w);
+/* split2 / merge2 (GpuSessionOps.swift:502-524). */
+yl_status yl_split2(yl_ctx* ctx, const float* X, float* mu, float* logvar, int c, int plane);
+yl_status yl_merge2(yl_ctx* ctx, const float* mu, const float* logvar, float* X, int c,
+                    int plane);
+/* randn(seed:rows:cols:) (GpuSessionOps.swift:527-535), same (seed, index) hash. */
+yl_status yl_randn(yl_ctx* ctx, float* out, uint32_t seed, size_t n);
+/* encodeMSE (GpuSessionOps.swift:25-42) and kl (:538-547): the sum is written
+ * to the device scalar out_dev (read it after yl_session_end). */
+yl_status yl_mse_sum(yl_ctx* ctx, const float* recon, const float* target, size_t n,
+                     float* out_dev);
+yl_status yl_kl_sum(yl_ctx* ctx, const float* mu, const float* logvar, size_t n, float* out_dev);
+/* encodeL1Grad (GpuSessionOps.swift:134-143): sign(r - t) / n. */
+yl_status yl_l1_grad(yl_ctx* ctx, const float* recon, const float* target, float* out, size_t n);
+/* vaeGrad (GpuSessionOps.swift:550-563). */
+yl_status yl_vae_grad(yl_ctx* ctx, const float* dz, const float* mu, const float* logvar,
+                      const float* eps, float* dmu, float* dlogvar, float betaN,
+                      float betaHalfN, size_t n);
+/* adamUpdate (GpuSessionOps.swift:242-252): b1 .9, b2 .999, eps 1e-8, t >= 1. */
+yl_status yl_adam_update(yl_ctx* ctx, float* param, const float* grad, float* m, float* v,
+                         size_t n, int t, float lr);
+
+/* -------------------------------------------------- B200 batched operators
+ * The same layer semantics on whole batches (the reference loops frames on
+ * the host, TrainConvVAE.swift:168-219), fused the way the hardware wants:
+ * tcgen05 implicit-GEMM convolutions (tf32 operands, fp32 accumulation),
+ * GroupNorm+SiLU in two memory passes, multi-tensor Adam in one launch. */
+
+/* Conv2d geometry.  The input is (n, c, h, w); with up = 1 it is the source
+ * of a nearest x2 upsample cropped to (up_h, up_w) (the decoder's
+ * "upsample2x + conv", ConvGPU.swift:380-399), read without materialising the
+ * upsampled tensor.  Output size: (in + 2*pad - k)/stride + 1 per axis
+ * (ConvGPU.swift:58-59).  Weights are (oc, c, k, k) = the reference's
+ * (oc, ic*k*k) (ConvGPU.swift:18); bias has oc entries. */
+typedef struct yl_conv_desc {
+  int n, c, h, w;
+  int oc, k, stride, pad;
+  int up, up_h, up_w;
+  int layout; /* yl_layout of every activation argument */
+} yl_conv_desc;
+yl_status yl_conv2d_out_shape(const yl_conv_desc* d, int* oh, int* ow);
+/* ConvLayerGPU.forward (ConvGPU.swift:57-64): y = conv(x, w) + b (+ residual). */
+yl_status yl_conv2d_fwd(yl_ctx* ctx, const yl_conv_desc* d, const float* x, const float* w,
+                        const float* b, const float* residual, float* y);
+/* ConvLayerGPU.backward dX (ConvGPU.swift:71-79): convBackInputS1 for stride
+ * 1, matmul(W, dOut, transA) + col2im for stride 2; with up = 1 the result is
+ * the downsample2x (2x2 sum) of the upsampled-input gradient. */
+yl_status yl_conv2d_bwd_data(yl_ctx* ctx, const yl_conv_desc* d, const float* dy, const float* w,
+                             float* dx);
+/* ConvLayerGPU.backward dW/db (ConvGPU.swift:68-69): gradW + biasRowGrad,
+ * summed over the batch.  dw or db may be NULL. */
+yl_status yl_conv2d_bwd_filter(yl_ctx* ctx, const yl_conv_desc* d, const float* x, const float* dy,
+                               float* dw, float* db);
+/* Transposed convolution = the adjoint of the conv `d` describes: x has the
+ * conv's output shape, y its input shape, b has c entries.  Its backward
+ * passes are the conv's forward and its filter gradient with roles swapped
+ * (the reference's stride-2 dX path, ConvGPU.swift:75-78). */
+yl_status yl_conv_transpose2d_fwd(yl_ctx* ctx, const yl_conv_desc* d, const float* x,
+                                  const float* w, const float* b, float* y);
+yl_status yl_conv_transpose2d_bwd_data(yl_ctx* ctx, const yl_conv_desc* d, const float* dy,
+                                       const float* w, float* dx);
+yl_status yl_conv_transpose2d_bwd_filter(yl_ctx* ctx, const yl_conv_desc* d, const float* x,
+                                         const float* dy, float* dw, float* db);
+
+/* GroupNorm + optional SiLU (groupNorm, GpuSessionOps.swift:121-131, and the
+ * activation that follows it).  mode 0: torch.nn.GroupNorm (biased variance
+ * + eps, affine gamma/beta, either may be NULL); mode 1: the reference's rule
+ * var = max(E[x^2] - E[x]^2, 1e-5), no eps (MetalKernelSourcesC.swift:35-38).
+ * Channels per group must be a multiple of 4.  mean_out / rstd_out (n*groups,
+ * optional) receive the statistics for the backward call. */
+yl_status yl_groupnorm_silu_fwd(yl_ctx* ctx, const float* x, int n, int c, int h, int w,
+                                int layout, int groups, float eps, int mode, const float* gamma,
+                                const float* beta, int apply_silu, float* y, float* mean_out,
+                                float* rstd_out);
+/* encodeGroupNormGrad (GpuSessionNormGrad.swift:10-24) with the affine and
+ * SiLU terms: dx (+= addend when not NULL), dgamma/dbeta summed over (n, h, w).
+ * mean/rstd may be NULL (recomputed). */
+yl_status yl_groupnorm_silu_bwd(yl_ctx* ctx, const float* x, const float* dy, int n, int c, int h,
+                                int w, int layout, int groups, float eps, int mode,
+                                const float* gamma, const float* beta, int apply_silu,
+                                const float* mean, const float* rstd, const float* addend,
+                                float* dx, float* dgamma, float* dbeta);
+
+/* LinearGPU (DenoiserMLP.swift:20-71): Y = X W^T + b, X (n, ic), W (oc, ic);
+ * backward dX = dY W, dW = dY^T X, db = sumCols(dY); outputs may be NULL. */
+yl_status yl_linear_fwd(yl_ctx* ctx, const float* X, const float* W, const float* b, float* Y,
+                        int n, int ic, int oc);
+yl_status yl_linear_bwd(yl_ctx* ctx, const float* X, const float* W, const float* dY, float* dX,
+                        float* dW, float* db, int n, int ic, int oc);
+
+/* Sinusoidal embedding of t[n] (device).  variant 0: motionTimeEmbedding
+ * (MotionPlanner.swift:155-165: interleaved sin/cos, base 1000, t clamped to
+ * [0,1]); variant 1: timestep_embedding (src/diffusion.py:6-10: [cos | sin],
+ * base 10000). */
+yl_status yl_timestep_embedding(yl_ctx* ctx, const float* t, int n, int dim, int variant,
+                                float* out);
+
+/* Multi-tensor Adam in one launch (adamUpdate per tensor, ConvGPU.swift:83-86,
+ * preceded by sanitizeGrads, GradSanitize.swift:18-101): g *= grad_scale;
+ * sanitize != 0 zeroes NaN/Inf; clip_max_norm > 0 scales all gradients by
+ * max_norm/norm when the global L2 norm exceeds it (norm_out_dev, optional,
+ * receives the norm).  Bias correction uses t >= 1. */
+typedef struct yl_adam_tensor {
+  float* param;
+  const float* grad;
+  float* m;
+  float* v;
+  long long n;
+} yl_adam_tensor;
+yl_status yl_adam_multi(yl_ctx* ctx, const yl_adam_tensor* table, int count, float lr, float b1,
+                        float b2, float eps, int t, float grad_scale, float clip_max_norm,
+                        int sanitize, float* norm_out_dev);
+
+/* VAE latent head (ConvVAEGPU encode tail, split2 + expHalf + randn + fma,
+ * GpuSessionOps.swift:472-535): e is (n, 2c, h, w) = [mu | logvar];
+ * z = mu + exp(0.5*clamp(logvar,-10,10)) * eps, eps[img][ch][p] =
+ * randn(trainingNoiseSeed(step, img), ch*h*w + p) (ConvVAEHelpers.swift:33-37). */
+yl_status yl_vae_latent_head_fwd(yl_ctx* ctx, const float* e, int n, int c, int h, int w,
+                                 int layout, int64_t step, float* z);
+/* vaeGrad + merge2 (GpuSessionOps.swift:502-563) with the KL averaged over the
+ * n*c*h*w latent elements (ConvGPU.swift:435-438): de = [dmu | dlogvar]. */
+yl_status yl_vae_latent_head_bwd(yl_ctx* ctx, const float* e, const float* dz, int n, int c, int h,
+                                 int w, int layout, int64_t step, float beta, float* de);
+/* L1 reconstruction + beta * mean KL: drecon = sign(recon - target)/n_recon
+ * (encodeL1Grad, GpuSessionOps.swift:134-143); loss_dev (device scalar) =
+ * mean|recon - target| + beta * KL_sum / (n*c_lat*h_lat*w_lat).  mu_logvar may
+ * be NULL (pure L1). */
+yl_status yl_loss_l1_kl(yl_ctx* ctx, const float* recon, const float* target, size_t n_recon,
+                        const float* mu_logvar, int n, int c_lat, int h_lat, int w_lat, int layout,
+                        float beta, float* drecon, float* loss_dev);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* YUME_C_H */

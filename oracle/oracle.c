@@ -1,0 +1,785 @@
+/*
+ * oracle.c -- CPU restatement of YumeLayersCore's hot-path arithmetic.
+ *
+ * TEST INFRASTRUCTURE ONLY.  This file is the checker for the CUDA backend
+ * (yumelayers_b200/csrc) and the timed CPU baseline; the product path never
+ * links, loads or calls it.  Only tests/, __graft_entry__.smoke() and the
+ * cpu_baseline / reference arm of bench.py may use it.
+ *
+ * Every function below restates one piece of the reference and cites the
+ * reference file:line it follows (paths are relative to the YumeLayers
+ * project root).  The reference's GPU code is Metal Shading Language held in
+ * Swift strings; the per-index loops below are the same arithmetic written in
+ * C.  Layouts are the reference's: per-image CHW with rows = channels and
+ * cols = H*W, conv weights (oc, ic*k*k), Linear weights (oc, ic).
+ *
+ * Parity pins: integer-pattern known-answer tests from the reference's own
+ * tests (Tests/YumeLayersTests/TestGroup3.swift:345-536, TestGroup4.swift:
+ * 116-221) are checked in tests/test_oracle.py; the ops that exist only in
+ * the reference's PyTorch prototype (SiLU, affine GroupNorm, Conv2d,
+ * timestep_embedding) are cross-checked against torch CPU there too.
+ *
+ * Build: see oracle/Makefile (gcc -O3 -march=native -fopenmp -shared).
+ */
+#include <math.h>
+#include <stdint.h>
+#include <stdlib.h>
+#include <string.h>
+#ifdef _OPENMP
+#include <omp.h>
+#endif
+
+#define ORC_API __attribute__((visibility("default")))
+
+ORC_API int orc_num_threads(void) {
+#ifdef _OPENMP
+  return omp_get_max_threads();
+#else
+  return 1;
+#endif
+}
+
+ORC_API void orc_set_num_threads(int n) {
+#ifdef _OPENMP
+  if (n > 0) omp_set_num_threads(n);
+#else
+  (void)n;
+#endif
+}
+
+/* ======================================================================= */
+/* 1. Reference kernels, restated per index (reference layout, fp32).       */
+/* ======================================================================= */
+
+/* matmul_kernel / matmul_tiled_kernel (MetalKernelSourcesA.swift:11-94):
+ * C[r,c] = sum_k op(A)[r,k] * op(B)[k,c]; transA reads A[k*M+r], transB reads
+ * B[c*K+k].  Accumulation order is k ascending, fp32, like the naive kernel. */
+ORC_API void orc_matmul(const float* A, const float* B, float* C, int M, int N,
+                        int K, int transA, int transB) {
+#pragma omp parallel for schedule(static)
+  for (int r = 0; r < M; ++r) {
+    for (int c = 0; c < N; ++c) {
+      float acc = 0.0f;
+      for (int k = 0; k < K; ++k) {
+        float av = transA ? A[(size_t)k * M + r] : A[(size_t)r * K + k];
+        float bv = transB ? B[(size_t)c * K + k] : B[(size_t)k * N + c];
+        acc += av * bv;
+      }
+      C[(size_t)r * N + c] = acc;
+    }
+  }
+}
+
+/* Blocked fp32 GEMM used by the conv composition below, so the CPU baseline is
+ * a fair one: C[M,N] (+)= A[M,K] * B[K,N], row-major, OpenMP over rows.  It is
+ * the same sum as orc_matmul (different association order). */
+static void gemm_nn(const float* A, const float* B, float* C, int M, int N, int K,
+                    int accumulate) {
+#pragma omp parallel for schedule(static)
+  for (int r = 0; r < M; ++r) {
+    float* crow = C + (size_t)r * N;
+    if (!accumulate) memset(crow, 0, sizeof(float) * (size_t)N);
+    for (int k0 = 0; k0 < K; k0 += 256) {
+      int k1 = k0 + 256 < K ? k0 + 256 : K;
+      for (int k = k0; k < k1; ++k) {
+        float a = A[(size_t)r * K + k];
+        if (a == 0.0f) continue;
+        const float* brow = B + (size_t)k * N;
+        for (int c = 0; c < N; ++c) crow[c] += a * brow[c];
+      }
+    }
+  }
+}
+
+/* C[M,N] (+)= A[M,K] * B[N,K]^T (both K-contiguous) -- the gradW shape. */
+static void gemm_nt(const float* A, const float* B, float* C, int M, int N, int K,
+                    int accumulate) {
+#pragma omp parallel for schedule(static)
+  for (int r = 0; r < M * N; ++r) {
+    int i = r / N, j = r % N;
+    const float* a = A + (size_t)i * K;
+    const float* b = B + (size_t)j * K;
+    double acc = 0.0;
+    float part = 0.0f;
+    for (int k = 0; k < K; ++k) {
+      part += a[k] * b[k];
+      if ((k & 1023) == 1023) { acc += part; part = 0.0f; }
+    }
+    acc += part;
+    if (accumulate) C[r] += (float)acc; else C[r] = (float)acc;
+  }
+}
+
+/* im2col3d_kernel (MetalKernelSourcesA.swift:325-352): X (ic, ih, iw) ->
+ * C (ic*kh*kw, oh*ow); out-of-range taps read 0. */
+ORC_API void orc_im2col(const float* X, float* C, int ic, int ih, int iw, int kh,
+                        int kw, int stride, int pad) {
+  int oh = (ih + 2 * pad - kh) / stride + 1;
+  int ow = (iw + 2 * pad - kw) / stride + 1;
+  int rows = ic * kh * kw;
+#pragma omp parallel for schedule(static)
+  for (int col = 0; col < rows; ++col) {
+    int c = col / (kh * kw), r = col % (kh * kw);
+    int ky = r / kw, kx = r % kw;
+    for (int oy = 0; oy < oh; ++oy)
+      for (int ox = 0; ox < ow; ++ox) {
+        int iy = oy * stride + ky - pad, ix = ox * stride + kx - pad;
+        float v = 0.0f;
+        if (iy >= 0 && iy < ih && ix >= 0 && ix < iw) v = X[((size_t)c * ih + iy) * iw + ix];
+        C[(size_t)col * (oh * ow) + oy * ow + ox] = v;
+      }
+  }
+}
+
+/* col2im3d_kernel (MetalKernelSourcesB.swift:28-58): gather of dcols back to
+ * (ic, ih, iw) for any stride; col2im3d_s1_kernel (B:60-85) is its stride-1
+ * special case and gives the same sums. */
+ORC_API void orc_col2im(const float* C, float* G, int ic, int ih, int iw, int kh,
+                        int kw, int stride, int pad, int oh, int ow) {
+#pragma omp parallel for schedule(static)
+  for (int c = 0; c < ic; ++c)
+    for (int y = 0; y < ih; ++y)
+      for (int x = 0; x < iw; ++x) {
+        float acc = 0.0f;
+        for (int ky = 0; ky < kh; ++ky) {
+          int sy = y + pad - ky;
+          if (sy < 0 || sy % stride != 0) continue;
+          int oy = sy / stride;
+          if (oy >= oh) continue;
+          for (int kx = 0; kx < kw; ++kx) {
+            int sx = x + pad - kx;
+            if (sx < 0 || sx % stride != 0) continue;
+            int ox = sx / stride;
+            if (ox >= ow) continue;
+            acc += C[((size_t)c * kh * kw + ky * kw + kx) * (oh * ow) + oy * ow + ox];
+          }
+        }
+        G[((size_t)c * ih + y) * iw + x] = acc;
+      }
+}
+
+/* conv_back_input_s1_kernel (MetalKernelSourcesB.swift:125-159), including the
+ * output-size fix at B:139-143 (bounds on the conv OUTPUT oh/ow). */
+ORC_API void orc_conv_back_input_s1(const float* dOut, const float* W, float* dx,
+                                    int ic, int oc, int ih, int iw, int kh, int kw,
+                                    int pad) {
+  int oh = ih + 2 * pad - kh + 1;
+  int ow = iw + 2 * pad - kw + 1;
+#pragma omp parallel for schedule(static)
+  for (int c = 0; c < ic; ++c)
+    for (int y = 0; y < ih; ++y)
+      for (int x = 0; x < iw; ++x) {
+        float acc = 0.0f;
+        for (int o = 0; o < oc; ++o) {
+          size_t woff = (size_t)o * (ic * kh * kw) + (size_t)c * (kh * kw);
+          for (int ky = 0; ky < kh; ++ky) {
+            int oy = y + pad - ky;
+            if (oy < 0 || oy >= oh) continue;
+            for (int kx = 0; kx < kw; ++kx) {
+              int ox = x + pad - kx;
+              if (ox < 0 || ox >= ow) continue;
+              acc += dOut[(size_t)o * (oh * ow) + oy * ow + ox] * W[woff + ky * kw + kx];
+            }
+          }
+        }
+        dx[((size_t)c * ih + y) * iw + x] = acc;
+      }
+}
+
+/* gradw_plain_kernel (MetalKernelSourcesA.swift:122-137):
+ * C[r,c] = sum_i A[r*K+i] * B[c*K+i]. */
+ORC_API void orc_gradw(const float* A, const float* B, float* C, int oc, int kk, int K) {
+#pragma omp parallel for schedule(static)
+  for (int r = 0; r < oc; ++r)
+    for (int c = 0; c < kk; ++c) {
+      float acc = 0.0f;
+      for (int i = 0; i < K; ++i) acc += A[(size_t)r * K + i] * B[(size_t)c * K + i];
+      C[(size_t)r * kk + c] = acc;
+    }
+}
+
+/* biasrow3d_kernel (MetalKernelSourcesB.swift:112-121): C[r,c] = A[r,c] + b[r]. */
+ORC_API void orc_bias_row(const float* A, const float* b, float* C, int rows, int cols) {
+  for (int r = 0; r < rows; ++r)
+    for (int c = 0; c < cols; ++c) C[(size_t)r * cols + c] = A[(size_t)r * cols + c] + b[r];
+}
+
+/* biasrowgrad_kernel (MetalKernelSourcesB.swift:162-171): out[r] = sum_c G[r,c]. */
+ORC_API void orc_bias_row_grad(const float* G, float* out, int rows, int cols) {
+  for (int r = 0; r < rows; ++r) {
+    float s = 0.0f;
+    for (int c = 0; c < cols; ++c) s += G[(size_t)r * cols + c];
+    out[r] = s;
+  }
+}
+
+/* addbias_kernel (MetalKernelSourcesA.swift:179-187): C[i] = A[i] + bias[i % cols]. */
+ORC_API void orc_add_bias(const float* A, const float* bias, float* C, int n, int cols) {
+  for (int i = 0; i < n; ++i) C[i] = A[i] + bias[i % cols];
+}
+
+/* sumcols_kernel (MetalKernelSourcesA.swift:253-269): C[j] = sum_i A[i*cols+j]. */
+ORC_API void orc_sum_cols(const float* A, float* C, int rows, int cols) {
+  for (int j = 0; j < cols; ++j) {
+    float s = 0.0f;
+    for (int i = 0; i < rows; ++i) s += A[(size_t)i * cols + j];
+    C[j] = s;
+  }
+}
+
+/* upsample3d_kernel (MetalKernelSourcesB.swift:87-97): (c,h,w) -> (c,2h,2w). */
+ORC_API void orc_upsample2x(const float* X, float* Y, int c, int h, int w) {
+  int w2 = 2 * w;
+  for (int ch = 0; ch < c; ++ch)
+    for (int y = 0; y < 2 * h; ++y)
+      for (int x = 0; x < w2; ++x)
+        Y[((size_t)ch * h * 2 + y) * w2 + x] = X[((size_t)ch * h + y / 2) * w + x / 2];
+}
+
+/* downsample3d_kernel (MetalKernelSourcesB.swift:99-110): 2x2 sum. */
+ORC_API void orc_downsample2x(const float* X, float* Y, int c, int h, int w) {
+  int w2 = 2 * w;
+  for (int ch = 0; ch < c; ++ch)
+    for (int y = 0; y < h; ++y)
+      for (int x = 0; x < w; ++x) {
+        size_t base = ((size_t)ch * h * 2 + y * 2) * w2 + x * 2;
+        Y[((size_t)ch * h + y) * w + x] = X[base] + X[base + 1] + X[base + w2] + X[base + w2 + 1];
+      }
+}
+
+/* groupNormCPU (LossFunctions.swift:97-126), the CPU source of truth for
+ * groupnorm_kernel (MetalKernelSourcesC.swift:10-46): affine-free, var clamped
+ * at >= 1e-5, no eps; double accumulation. */
+ORC_API void orc_groupnorm_ref(const float* xs, float* out, int channels, int groups,
+                               int plane) {
+  int gsize = channels / groups;
+  double count = (double)gsize * plane;
+  for (int g = 0; g < groups; ++g) {
+    int c0 = g * gsize;
+    double sum = 0, sq = 0;
+    for (int c = c0; c < c0 + gsize; ++c)
+      for (int p = 0; p < plane; ++p) {
+        double v = xs[(size_t)c * plane + p];
+        sum += v; sq += v * v;
+      }
+    double mean = sum / count;
+    double var = sq / count - mean * mean;
+    if (var < 1e-5) var = 1e-5;
+    double inv = 1.0 / sqrt(var);
+    for (int c = c0; c < c0 + gsize; ++c)
+      for (int p = 0; p < plane; ++p) {
+        size_t idx = (size_t)c * plane + p;
+        out[idx] = (float)((xs[idx] - mean) * inv);
+      }
+  }
+}
+
+/* groupNormGradCPU (LossFunctions.swift:132-176), source of truth for
+ * groupnorm_grad_kernel (MetalKernelSourcesC.swift:51-101). */
+ORC_API void orc_groupnorm_grad_ref(const float* xs, const float* dys, float* out,
+                                    int channels, int groups, int plane) {
+  int gsize = channels / groups;
+  double n = (double)gsize * plane;
+  for (int g = 0; g < groups; ++g) {
+    int c0 = g * gsize;
+    double sum = 0, sq = 0;
+    for (int c = c0; c < c0 + gsize; ++c)
+      for (int p = 0; p < plane; ++p) {
+        double v = xs[(size_t)c * plane + p];
+        sum += v; sq += v * v;
+      }
+    double mean = sum / n;
+    double var = sq / n - mean * mean;
+    if (var < 1e-5) var = 1e-5;
+    double inv = 1.0 / sqrt(var);
+    double sdy = 0, sdyxm = 0;
+    for (int c = c0; c < c0 + gsize; ++c)
+      for (int p = 0; p < plane; ++p) {
+        size_t idx = (size_t)c * plane + p;
+        sdy += dys[idx];
+        sdyxm += dys[idx] * (xs[idx] - mean);
+      }
+    double mdy = sdy / n, mdyxm = sdyxm / n;
+    for (int c = c0; c < c0 + gsize; ++c)
+      for (int p = 0; p < plane; ++p) {
+        size_t idx = (size_t)c * plane + p;
+        double xm = xs[idx] - mean;
+        out[idx] = (float)(inv * (dys[idx] - mdy - xm * mdyxm / var));
+      }
+  }
+}
+
+/* Elementwise kernels.  op codes follow the reference kernel list:
+ *  0 relu (B:191-197)        1 sigmoid (B:208-214)    2 tanh (A:236-242)
+ *  3 tanhgrad (A:244-251)    4 exp (B:273-279)        5 exphalf (B:293-299)
+ *  6 silu (src/vae.py:11, torch nn.SiLU)                                    */
+ORC_API void orc_unary(int op, const float* A, float* C, int n) {
+  for (int i = 0; i < n; ++i) {
+    float a = A[i];
+    switch (op) {
+      case 0: C[i] = a > 0.0f ? a : 0.0f; break;
+      case 1: C[i] = 1.0f / (1.0f + expf(-a)); break;
+      case 2: C[i] = tanhf(a); break;
+      case 3: { float t = tanhf(a); C[i] = 1.0f - t * t; } break;
+      case 4: C[i] = expf(a); break;
+      case 5: { float l = a < -10.0f ? -10.0f : (a > 10.0f ? 10.0f : a); C[i] = expf(0.5f * l); } break;
+      case 6: C[i] = a / (1.0f + expf(-a)); break;
+      default: C[i] = a;
+    }
+  }
+}
+
+/* Binary kernels:
+ *  0 add (A:171-177)   1 sub (A:198-205)   2 mul (A:189-196)
+ *  3 relugrad: Y>0 ? G : 0 (B:199-206)     4 sigmoidgrad: G*s*(1-s) (B:216-224)
+ *  5 silugrad: G * s*(1 + z*(1-s)), s = sigmoid(z)                           */
+ORC_API void orc_binary(int op, const float* A, const float* B, float* C, int n) {
+  for (int i = 0; i < n; ++i) {
+    float a = A[i], b = B[i];
+    switch (op) {
+      case 0: C[i] = a + b; break;
+      case 1: C[i] = a - b; break;
+      case 2: C[i] = a * b; break;
+      case 3: C[i] = a > 0.0f ? b : 0.0f; break;
+      case 4: { float s = 1.0f / (1.0f + expf(-a)); C[i] = b * s * (1.0f - s); } break;
+      case 5: { float s = 1.0f / (1.0f + expf(-a)); C[i] = b * s * (1.0f + a * (1.0f - s)); } break;
+      default: C[i] = a;
+    }
+  }
+}
+
+/* smul_kernel (A:207-214), addconst_kernel (B:281-289), fma_kernel (B:263-271). */
+ORC_API void orc_smul(const float* A, float* C, float s, int n) { for (int i = 0; i < n; ++i) C[i] = A[i] * s; }
+ORC_API void orc_addconst(const float* A, float* C, float s, int n) { for (int i = 0; i < n; ++i) C[i] = A[i] + s; }
+ORC_API void orc_fma(const float* A, const float* B, const float* D, float* C, int n) {
+  for (int i = 0; i < n; ++i) C[i] = A[i] + B[i] * D[i];
+}
+
+/* mse_reduce_kernel (B:236-258): sum of squared differences (double here, as
+ * the reference's test compares it with a Double CPU sum, TestGroup2.swift:115-145). */
+ORC_API double orc_mse_sum(const float* r, const float* t, int n) {
+  double s = 0;
+  for (int i = 0; i < n; ++i) { double d = (double)r[i] - t[i]; s += d * d; }
+  return s;
+}
+
+/* kl_reduce_kernel (B:334-357): 0.5 * sum(mu^2 + exp(lv) - 1 - lv), lv clamped. */
+ORC_API double orc_kl_sum(const float* mu, const float* lv, int n) {
+  double s = 0;
+  for (int i = 0; i < n; ++i) {
+    float l = lv[i] < -10.0f ? -10.0f : (lv[i] > 10.0f ? 10.0f : lv[i]);
+    s += 0.5 * ((double)mu[i] * mu[i] + exp((double)l) - 1.0 - l);
+  }
+  return s;
+}
+
+/* l1grad_kernel (B:453-461): sign(recon - target) * invN. */
+ORC_API void orc_l1grad(const float* r, const float* t, float* out, float invN, int n) {
+  for (int i = 0; i < n; ++i) {
+    float d = r[i] - t[i];
+    out[i] = (d > 0.0f ? 1.0f : (d < 0.0f ? -1.0f : 0.0f)) * invN;
+  }
+}
+
+/* vae_grad_kernel (B:365-380). */
+ORC_API void orc_vae_grad(const float* dz, const float* mu, const float* lv,
+                          const float* eps, float* dmu, float* dlv, float betaN,
+                          float betaHalfN, int n) {
+  for (int i = 0; i < n; ++i) {
+    float l = lv[i] < -10.0f ? -10.0f : (lv[i] > 10.0f ? 10.0f : lv[i]);
+    dmu[i] = dz[i] + betaN * mu[i];
+    dlv[i] = dz[i] * eps[i] * 0.5f * expf(0.5f * l) + betaHalfN * (expf(l) - 1.0f);
+  }
+}
+
+/* split2_kernel / merge2_kernel (B:302-331). */
+ORC_API void orc_split2(const float* X, float* A, float* B, int c, int plane) {
+  memcpy(A, X, sizeof(float) * (size_t)c * plane);
+  memcpy(B, X + (size_t)c * plane, sizeof(float) * (size_t)c * plane);
+}
+ORC_API void orc_merge2(const float* A, const float* B, float* X, int c, int plane) {
+  memcpy(X, A, sizeof(float) * (size_t)c * plane);
+  memcpy(X + (size_t)c * plane, B, sizeof(float) * (size_t)c * plane);
+}
+
+/* yume_hash + randn_kernel (MetalKernelSourcesB.swift:385-402): counter-based
+ * Box-Muller keyed by (seed, index); uint32 wrap-around arithmetic. */
+static inline uint32_t yume_hash(uint32_t x) {
+  x = ((x >> ((x >> 28u) + 4u)) ^ x) * 277803737u;
+  return (x >> 22u) ^ x;
+}
+ORC_API void orc_randn(float* out, uint32_t seed, int n) {
+  for (int i = 0; i < n; ++i) {
+    uint32_t g = (uint32_t)i;
+    uint32_t h1 = yume_hash(g * 747796405u + seed * 2891336453u + 1u);
+    uint32_t h2 = yume_hash(g * 2654435761u + seed * 1013904223u + 0x9E3779B9u);
+    float u1 = (float)(h1 >> 8) / 16777216.0f;
+    if (u1 < 1e-7f) u1 = 1e-7f;
+    float u2 = (float)(h2 >> 8) / 16777216.0f;
+    out[i] = sqrtf(-2.0f * logf(u1)) * cosf(6.28318530718f * u2);
+  }
+}
+ORC_API uint32_t orc_yume_hash(uint32_t x) { return yume_hash(x); }
+
+/* SplitMix64 (ConvVAEHelpers.swift:10-20). */
+ORC_API uint64_t orc_splitmix64_next(uint64_t* state) {
+  *state += 0x9E3779B97F4A7C15ull;
+  uint64_t z = *state;
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  return z ^ (z >> 31);
+}
+
+/* trainingNoiseSeed (ConvVAEHelpers.swift:33-37). */
+ORC_API uint32_t orc_training_noise_seed(int64_t step, int64_t batch_index) {
+  uint64_t a = (uint64_t)step * 0x9E3779B97F4A7C15ull;
+  uint64_t b = (uint64_t)batch_index * 0xC2B2AE3D27D4EB4Full;
+  return (uint32_t)((a ^ (b + 0x165667B19E3779F9ull)) >> 32);
+}
+
+/* adam_kernel (MetalKernelSourcesA.swift:271-287), t clamped to >= 1 as the
+ * caller does (GpuSessionOps.swift:246-248).  b1/b2/eps are parameters here
+ * (the reference hard-codes 0.9/0.999/1e-8, the defaults of the tests). */
+ORC_API void orc_adam(float* p, const float* g, float* m, float* v, int n, int t,
+                      float lr, float b1, float b2, float eps) {
+  if (t < 1) t = 1;
+  float c1 = 1.0f - powf(b1, (float)t), c2 = 1.0f - powf(b2, (float)t);
+  for (int i = 0; i < n; ++i) {
+    float gi = g[i];
+    m[i] = b1 * m[i] + (1.0f - b1) * gi;
+    v[i] = b2 * v[i] + (1.0f - b2) * gi * gi;
+    float mh = m[i] / c1, vh = v[i] / c2;
+    p[i] -= lr * mh / (sqrtf(vh) + eps);
+  }
+}
+
+/* sanitizeGrads (GradSanitize.swift:18-101) on one flat buffer holding all
+ * gradients: g *= preScale; NaN/Inf -> 0 (not counted in the norm); if the
+ * global L2 norm exceeds maxNorm, scale everything by maxNorm/norm.  Returns
+ * the pre-clip norm; *fixed receives the number of non-finite values. */
+ORC_API float orc_sanitize_grads(float* g, long n, float maxNorm, float preScale, long* fixed) {
+  float total = 0.0f;
+  long nf = 0;
+  for (long i = 0; i < n; ++i) {
+    float v = g[i];
+    if (preScale != 1.0f) v *= preScale;
+    if (isnan(v) || isinf(v)) { v = 0.0f; nf++; } else total += v * v;
+    g[i] = v;
+  }
+  float norm = sqrtf(total);
+  if (norm > maxNorm) {
+    float s = maxNorm / norm;
+    for (long i = 0; i < n; ++i) g[i] *= s;
+  }
+  if (fixed) *fixed = nf;
+  return norm;
+}
+
+/* motionTimeEmbedding (MotionPlanner.swift:155-165): t clamped to [0,1]
+ * (non-finite -> 0); emb[i] = sin(t * 1000^(i/d)), emb[i+1] = cos(...) for
+ * even i; computed in double, stored as float. */
+ORC_API void orc_motion_time_embedding(double t, int dim, float* out) {
+  double tt = isfinite(t) ? t : 0.0;
+  if (tt < 0) tt = 0;
+  if (tt > 1) tt = 1;
+  for (int i = 0; i < dim; i += 2) {
+    double w = pow(1000.0, (double)i / (double)dim);
+    out[i] = (float)sin(tt * w);
+    out[i + 1] = (float)cos(tt * w);
+  }
+}
+
+/* timeEmbedding (DenoiserMLP.swift:7-17): integer t, base 10000, interleaved. */
+ORC_API void orc_time_embedding_int(int t, int dim, float* out) {
+  for (int i = 0; i < dim; i += 2) {
+    double w = pow(10000.0, (double)i / (double)dim);
+    out[i] = (float)sin((double)t / w);
+    out[i + 1] = (float)cos((double)t / w);
+  }
+}
+
+/* timestep_embedding (src/diffusion.py:6-10): [cos | sin] halves with
+ * freqs = exp(-ln(max_period) * j / half), fp32 like the torch prototype. */
+ORC_API void orc_timestep_embedding_torch(const float* t, int n, int dim, float max_period,
+                                          float* out) {
+  int half = dim / 2;
+  for (int b = 0; b < n; ++b)
+    for (int j = 0; j < half; ++j) {
+      float f = expf(-logf(max_period) * (float)j / (float)half);
+      float a = t[b] * f;
+      out[(size_t)b * dim + j] = cosf(a);
+      out[(size_t)b * dim + half + j] = sinf(a);
+    }
+}
+
+/* ======================================================================= */
+/* 2. Batched layer math (NCHW = per-image CHW stacked), composed from the  */
+/*    reference kernels the way the reference's layers compose them.       */
+/* ======================================================================= */
+
+/* ConvLayerGPU.forward (ConvGPU.swift:57-64): per image, cols = im2col(x),
+ * y = W * cols + b (biasRow).  Optional nearest-x2 upsample of the input
+ * (the decoder's "up + conv", ConvGPU.swift:393 / Ops:336), cropped to
+ * (ih, iw) when the upsampled size is odd-cropped; optional residual add and
+ * per-(image, channel) bias (time-embedding projection). */
+ORC_API void orc_conv2d_fwd(const float* x, int N, int C, int H, int W,
+                            const float* w, const float* b, int OC, int k, int stride,
+                            int pad, int up, int Hin, int Win, const float* bias2d,
+                            const float* residual, float* y) {
+  /* up: x has spatial (Hs, Ws) = ceil(Hin/2), ceil(Win/2) and is viewed as the
+   * (Hin, Win) nearest upsample; else (H, W) = (Hin, Win). */
+  int ih = up ? Hin : H, iw = up ? Win : W;
+  int oh = (ih + 2 * pad - k) / stride + 1, ow = (iw + 2 * pad - k) / stride + 1;
+  size_t plane_in = (size_t)ih * iw, plane_out = (size_t)oh * ow;
+  float* xin = (float*)malloc(sizeof(float) * C * plane_in);
+  float* cols = (float*)malloc(sizeof(float) * (size_t)C * k * k * plane_out);
+  for (int n = 0; n < N; ++n) {
+    const float* xn = x + (size_t)n * C * H * W;
+    if (up) {
+      for (int c = 0; c < C; ++c)
+        for (int yy = 0; yy < ih; ++yy)
+          for (int xx = 0; xx < iw; ++xx)
+            xin[(size_t)c * plane_in + yy * iw + xx] = xn[((size_t)c * H + yy / 2) * W + xx / 2];
+    } else {
+      memcpy(xin, xn, sizeof(float) * C * plane_in);
+    }
+    orc_im2col(xin, cols, C, ih, iw, k, k, stride, pad);
+    float* yn = y + (size_t)n * OC * plane_out;
+    gemm_nn(w, cols, yn, OC, (int)plane_out, C * k * k, 0);
+#pragma omp parallel for schedule(static)
+    for (int o = 0; o < OC; ++o) {
+      float bb = (b ? b[o] : 0.0f) + (bias2d ? bias2d[(size_t)n * OC + o] : 0.0f);
+      float* row = yn + (size_t)o * plane_out;
+      const float* res = residual ? residual + ((size_t)n * OC + o) * plane_out : NULL;
+      for (size_t p = 0; p < plane_out; ++p) row[p] = row[p] + bb + (res ? res[p] : 0.0f);
+    }
+  }
+  free(xin);
+  free(cols);
+}
+
+/* ConvLayerGPU.backward (ConvGPU.swift:66-81) summed over the batch the way
+ * TrainContext.forwardBackward accumulates per-frame grads
+ * (TrainConvVAE.swift:168-219): dW += gradW(dOut, cols), db += biasRowGrad,
+ * dx = convBackInputS1 (stride 1) or col2im(W^T dOut) (stride 2).  With `up`,
+ * dx is the downsample2x (2x2 sum, Ops:379) of the upsampled-input gradient,
+ * restricted to the cropped size.  Any of dx/dw/db may be NULL.  dw and db
+ * are overwritten; dbias2d (N, OC) receives per-image channel sums. */
+ORC_API void orc_conv2d_bwd(const float* x, int N, int C, int H, int W,
+                            const float* w, int OC, int k, int stride, int pad, int up,
+                            int Hin, int Win, const float* dy, float* dx, float* dw,
+                            float* db, float* dbias2d) {
+  int ih = up ? Hin : H, iw = up ? Win : W;
+  int oh = (ih + 2 * pad - k) / stride + 1, ow = (iw + 2 * pad - k) / stride + 1;
+  size_t plane_in = (size_t)ih * iw, plane_out = (size_t)oh * ow;
+  int kk = C * k * k;
+  float* xin = (float*)malloc(sizeof(float) * C * plane_in);
+  float* cols = (float*)malloc(sizeof(float) * (size_t)kk * plane_out);
+  float* dxin = (float*)malloc(sizeof(float) * C * plane_in);
+  if (dw) memset(dw, 0, sizeof(float) * (size_t)OC * kk);
+  if (db) memset(db, 0, sizeof(float) * OC);
+  for (int n = 0; n < N; ++n) {
+    const float* xn = x + (size_t)n * C * H * W;
+    const float* dyn = dy + (size_t)n * OC * plane_out;
+    if (dw) {
+      if (up) {
+        for (int c = 0; c < C; ++c)
+          for (int yy = 0; yy < ih; ++yy)
+            for (int xx = 0; xx < iw; ++xx)
+              xin[(size_t)c * plane_in + yy * iw + xx] = xn[((size_t)c * H + yy / 2) * W + xx / 2];
+      } else {
+        memcpy(xin, xn, sizeof(float) * C * plane_in);
+      }
+      orc_im2col(xin, cols, C, ih, iw, k, k, stride, pad);
+      gemm_nt(dyn, cols, dw, OC, kk, (int)plane_out, 1);
+    }
+    if (db || dbias2d) {
+      for (int o = 0; o < OC; ++o) {
+        double s = 0;
+        for (size_t p = 0; p < plane_out; ++p) s += dyn[(size_t)o * plane_out + p];
+        if (db) db[o] += (float)s;
+        if (dbias2d) dbias2d[(size_t)n * OC + o] = (float)s;
+      }
+    }
+    if (dx) {
+      if (stride == 1) {
+        orc_conv_back_input_s1(dyn, w, dxin, C, OC, ih, iw, k, k, pad);
+      } else {
+        /* dcols = W^T * dOut (matmul transA, ConvGPU.swift:75), then col2im. */
+        float* dcols = cols;
+#pragma omp parallel for schedule(static)
+        for (int r = 0; r < kk; ++r) {
+          float* row = dcols + (size_t)r * plane_out;
+          memset(row, 0, sizeof(float) * plane_out);
+          for (int o = 0; o < OC; ++o) {
+            float wv = w[(size_t)o * kk + r];
+            const float* drow = dyn + (size_t)o * plane_out;
+            for (size_t p = 0; p < plane_out; ++p) row[p] += wv * drow[p];
+          }
+        }
+        orc_col2im(dcols, dxin, C, ih, iw, k, k, stride, pad, oh, ow);
+      }
+      float* dxn = dx + (size_t)n * C * H * W;
+      if (up) {
+        memset(dxn, 0, sizeof(float) * C * H * W);
+        for (int c = 0; c < C; ++c)
+          for (int yy = 0; yy < ih; ++yy)
+            for (int xx = 0; xx < iw; ++xx)
+              dxn[((size_t)c * H + yy / 2) * W + xx / 2] += dxin[(size_t)c * plane_in + yy * iw + xx];
+      } else {
+        memcpy(dxn, dxin, sizeof(float) * C * plane_in);
+      }
+    }
+  }
+  free(xin);
+  free(cols);
+  free(dxin);
+}
+
+/* GroupNorm with affine gamma/beta and eps (torch.nn.GroupNorm semantics, the
+ * BASELINE op; affine-free clamp variant is orc_groupnorm_ref above), followed
+ * by SiLU when silu != 0.  Per image; double statistics like groupNormCPU
+ * (LossFunctions.swift:97-126).  mean/rstd (N*G) are optional outputs. */
+ORC_API void orc_gn_silu_fwd(const float* x, int N, int C, int HW, int G, float eps,
+                             const float* gamma, const float* beta, int silu, float* y,
+                             float* mean_out, float* rstd_out) {
+  int cg = C / G;
+#pragma omp parallel for collapse(2) schedule(static)
+  for (int n = 0; n < N; ++n)
+    for (int g = 0; g < G; ++g) {
+      const float* xn = x + (size_t)n * C * HW;
+      double s = 0, q = 0, cnt = (double)cg * HW;
+      for (int c = g * cg; c < (g + 1) * cg; ++c)
+        for (int p = 0; p < HW; ++p) { double v = xn[(size_t)c * HW + p]; s += v; q += v * v; }
+      double mean = s / cnt, var = q / cnt - mean * mean;
+      if (var < 0) var = 0;
+      double rstd = 1.0 / sqrt(var + eps);
+      if (mean_out) mean_out[n * G + g] = (float)mean;
+      if (rstd_out) rstd_out[n * G + g] = (float)rstd;
+      for (int c = g * cg; c < (g + 1) * cg; ++c) {
+        double ga = gamma ? gamma[c] : 1.0, be = beta ? beta[c] : 0.0;
+        for (int p = 0; p < HW; ++p) {
+          size_t idx = (size_t)n * C * HW + (size_t)c * HW + p;
+          double a = (x[idx] - mean) * rstd * ga + be;
+          if (silu) a = a / (1.0 + exp(-a));
+          y[idx] = (float)a;
+        }
+      }
+    }
+}
+
+/* Backward of orc_gn_silu_fwd.  dy is the gradient w.r.t. the SiLU output
+ * (or the GN output when silu == 0).  dx = rstd*(dxh - mean(dxh) -
+ * xh*mean(dxh*xh)) with dxh = da*gamma, the affine form of groupNormGradCPU
+ * (LossFunctions.swift:132-176).  dgamma/dbeta are sums over (N, HW);
+ * `addend` (optional) is added to dx (residual fan-in, Ops:453). */
+ORC_API void orc_gn_silu_bwd(const float* x, const float* dy, int N, int C, int HW, int G,
+                             float eps, const float* gamma, const float* beta, int silu,
+                             const float* addend, float* dx, float* dgamma, float* dbeta) {
+  int cg = C / G;
+  double* dg = (double*)calloc((size_t)N * C, sizeof(double));
+  double* dbt = (double*)calloc((size_t)N * C, sizeof(double));
+#pragma omp parallel for collapse(2) schedule(static)
+  for (int n = 0; n < N; ++n)
+    for (int g = 0; g < G; ++g) {
+      const float* xn = x + (size_t)n * C * HW;
+      double s = 0, q = 0, cnt = (double)cg * HW;
+      for (int c = g * cg; c < (g + 1) * cg; ++c)
+        for (int p = 0; p < HW; ++p) { double v = xn[(size_t)c * HW + p]; s += v; q += v * v; }
+      double mean = s / cnt, var = q / cnt - mean * mean;
+      if (var < 0) var = 0;
+      double rstd = 1.0 / sqrt(var + eps);
+      double sd = 0, sdx = 0;
+      for (int c = g * cg; c < (g + 1) * cg; ++c) {
+        double ga = gamma ? gamma[c] : 1.0, be = beta ? beta[c] : 0.0;
+        for (int p = 0; p < HW; ++p) {
+          size_t idx = (size_t)n * C * HW + (size_t)c * HW + p;
+          double xh = (x[idx] - mean) * rstd;
+          double a = xh * ga + be, da = dy[idx];
+          if (silu) { double sg = 1.0 / (1.0 + exp(-a)); da *= sg * (1.0 + a * (1.0 - sg)); }
+          dg[(size_t)n * C + c] += da * xh;
+          dbt[(size_t)n * C + c] += da;
+          double dxh = da * ga;
+          sd += dxh; sdx += dxh * xh;
+        }
+      }
+      double md = sd / cnt, mdx = sdx / cnt;
+      for (int c = g * cg; c < (g + 1) * cg; ++c) {
+        double ga = gamma ? gamma[c] : 1.0, be = beta ? beta[c] : 0.0;
+        for (int p = 0; p < HW; ++p) {
+          size_t idx = (size_t)n * C * HW + (size_t)c * HW + p;
+          double xh = (x[idx] - mean) * rstd;
+          double a = xh * ga + be, da = dy[idx];
+          if (silu) { double sg = 1.0 / (1.0 + exp(-a)); da *= sg * (1.0 + a * (1.0 - sg)); }
+          double v = rstd * (da * ga - md - xh * mdx);
+          if (addend) v += addend[idx];
+          dx[idx] = (float)v;
+        }
+      }
+    }
+  for (int c = 0; c < C; ++c) {
+    double a = 0, b = 0;
+    for (int n = 0; n < N; ++n) { a += dg[(size_t)n * C + c]; b += dbt[(size_t)n * C + c]; }
+    if (dgamma) dgamma[c] = (float)a;
+    if (dbeta) dbeta[c] = (float)b;
+  }
+  free(dg);
+  free(dbt);
+}
+
+/* LinearGPU.forward (DenoiserMLP.swift:51-54): Y = X * W^T + b, X (n, ic),
+ * W (oc, ic); act 1 applies SiLU to the output. */
+ORC_API void orc_linear_fwd(const float* X, const float* Wt, const float* b, float* Y, int n,
+                            int ic, int oc, int act) {
+  for (int r = 0; r < n; ++r)
+    for (int o = 0; o < oc; ++o) {
+      double s = b ? b[o] : 0.0;
+      for (int i = 0; i < ic; ++i) s += (double)X[(size_t)r * ic + i] * Wt[(size_t)o * ic + i];
+      float v = (float)s;
+      if (act == 1) v = v / (1.0f + expf(-v));
+      Y[(size_t)r * oc + o] = v;
+    }
+}
+
+/* LinearGPU.backward (DenoiserMLP.swift:57-64): dX = dY * W, dW = dY^T * X,
+ * db = sumCols(dY).  Any output may be NULL; dW/db are overwritten. */
+ORC_API void orc_linear_bwd(const float* X, const float* Wt, const float* dY, float* dX,
+                            float* dW, float* db, int n, int ic, int oc) {
+  if (dX)
+    for (int r = 0; r < n; ++r)
+      for (int i = 0; i < ic; ++i) {
+        double s = 0;
+        for (int o = 0; o < oc; ++o) s += (double)dY[(size_t)r * oc + o] * Wt[(size_t)o * ic + i];
+        dX[(size_t)r * ic + i] = (float)s;
+      }
+  if (dW)
+    for (int o = 0; o < oc; ++o)
+      for (int i = 0; i < ic; ++i) {
+        double s = 0;
+        for (int r = 0; r < n; ++r) s += (double)dY[(size_t)r * oc + o] * X[(size_t)r * ic + i];
+        dW[(size_t)o * ic + i] = (float)s;
+      }
+  if (db)
+    for (int o = 0; o < oc; ++o) {
+      double s = 0;
+      for (int r = 0; r < n; ++r) s += dY[(size_t)r * oc + o];
+      db[o] = (float)s;
+    }
+}
+
+/* VAE loss head (BASELINE: L1 reconstruction + beta * KL averaged per latent
+ * element, the KL scaling of ConvVAEGPU.backward, ConvGPU.swift:435-438):
+ * returns loss; writes dRecon = sign(r - t)/n_r (l1grad_kernel, B:453-461). */
+ORC_API double orc_l1_kl_loss(const float* recon, const float* target, long nr,
+                              const float* mu, const float* lv, long nl, float beta,
+                              float* drecon) {
+  double l1 = 0;
+  float inv = (float)(1.0 / (double)nr);
+  for (long i = 0; i < nr; ++i) {
+    float d = recon[i] - target[i];
+    l1 += fabs((double)d);
+    if (drecon) drecon[i] = (d > 0.0f ? 1.0f : (d < 0.0f ? -1.0f : 0.0f)) * inv;
+  }
+  double kl = orc_kl_sum(mu, lv, (int)nl);
+  return l1 / (double)nr + (double)beta * kl / (double)nl;
+}

@@ -1,0 +1,466 @@
+// yl_train_ops.cu -- the small, memory-bound training ops: multi-tensor
+// Adam with the gradient sanitize/clip folded in, the VAE latent and loss
+// heads, Linear layers, the timestep embedding and SiLU.
+#include <cmath>
+
+#include "yl_kernels.h"
+#include "yl_norm.h"
+#include "yl_ptx.cuh"
+
+namespace yl {
+
+// ------------------------------------------------------------------ Adam
+// adam_kernel (MetalKernelSourcesA.swift:271-287) ran one launch per
+// parameter tensor with pow() per element, after sanitizeGrads
+// (GradSanitize.swift:18-101) copied every gradient to the CPU and back.
+// Here: one launch computes the global squared norm of the (scaled,
+// sanitized) gradients into a device scalar, and one launch updates all
+// tensors, reading that scalar to apply the clip factor -- no host round trip.
+constexpr int kMaxAdamTensors = 48;
+struct AdamPack {
+  AdamTensor t[kMaxAdamTensors];
+  long long start[kMaxAdamTensors + 1];  // element prefix sums
+  int count;
+};
+
+__device__ __forceinline__ int adam_find(const AdamPack& p, long long i) {
+  int lo = 0, hi = p.count - 1;
+  while (lo < hi) {
+    int mid = (lo + hi + 1) >> 1;
+    if (p.start[mid] <= i) lo = mid; else hi = mid - 1;
+  }
+  return lo;
+}
+
+__device__ __forceinline__ float sanitize_scale(float g, float scale, int sanitize) {
+  float v = g * scale;
+  if (sanitize && !isfinite(v)) v = 0.f;
+  return v;
+}
+
+__global__ void adam_norm_partial_kernel(const __grid_constant__ AdamPack p, float scale,
+                                         int sanitize, double* part) {
+  const long long total = p.start[p.count];
+  double s = 0;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int k = adam_find(p, i);
+    const float v = sanitize_scale(p.t[k].grad[i - p.start[k]], scale, sanitize);
+    s += (double)v * v;
+  }
+  __shared__ double red[32];
+#pragma unroll
+  for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double t = 0;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += red[w];
+    part[blockIdx.x] = t;
+  }
+}
+
+__global__ void adam_norm_final_kernel(const double* part, int nb, float* norm) {
+  if (threadIdx.x == 0) {
+    double s = 0;
+    for (int i = 0; i < nb; ++i) s += part[i];
+    norm[0] = (float)sqrt(s);
+  }
+}
+
+__global__ void adam_update_kernel(const __grid_constant__ AdamPack p, float lr, float b1, float b2,
+                                   float eps, float c1, float c2, float scale, int sanitize,
+                                   float clip, const float* norm) {
+  float clipf = 1.f;
+  if (clip > 0.f && norm) {
+    const float nv = *norm;
+    if (nv > clip) clipf = clip / nv;
+  }
+  const long long total = p.start[p.count];
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int k = adam_find(p, i);
+    const long long j = i - p.start[k];
+    const AdamTensor& t = p.t[k];
+    const float g = sanitize_scale(t.grad[j], scale, sanitize) * clipf;
+    const float m = b1 * t.m[j] + (1.f - b1) * g;
+    const float v = b2 * t.v[j] + (1.f - b2) * g * g;
+    t.m[j] = m;
+    t.v[j] = v;
+    t.param[j] -= lr * (m / c1) / (sqrtf(v / c2) + eps);
+  }
+}
+
+yl_status adam_multi(yl_ctx* ctx, const AdamTensor* tensors, int count, float lr, float b1,
+                     float b2, float eps, int t, float grad_scale, float clip_max_norm,
+                     int sanitize, float* norm_out) {
+  YL_CHECK(count >= 0, YL_ERR_INVALID, "adam_multi: negative tensor count");
+  if (t < 1) t = 1;
+  const float c1 = 1.f - powf(b1, (float)t), c2 = 1.f - powf(b2, (float)t);
+  const int nb = ctx->num_sms * 4;
+  float* norm = norm_out;
+  void* ws = nullptr;
+  const bool need_norm = clip_max_norm > 0.f || norm_out;
+  if (need_norm) {
+    YL_TRY(scratch_get(ctx, nb * sizeof(double) + 256, &ws));
+    if (!norm) norm = (float*)((char*)ws + nb * sizeof(double));
+  }
+  for (int base = 0; base < count; base += kMaxAdamTensors) {
+    AdamPack p;
+    p.count = count - base < kMaxAdamTensors ? count - base : kMaxAdamTensors;
+    p.start[0] = 0;
+    for (int k = 0; k < p.count; ++k) {
+      p.t[k] = tensors[base + k];
+      YL_CHECK(p.t[k].param && p.t[k].grad && p.t[k].m && p.t[k].v, YL_ERR_INVALID,
+               "adam_multi: NULL pointer in tensor %d", base + k);
+      p.start[k + 1] = p.start[k] + p.t[k].n;
+    }
+    if (p.start[p.count] == 0) continue;
+    if (need_norm) {
+      YL_CHECK(count <= kMaxAdamTensors, YL_ERR_UNSUPPORTED,
+               "adam_multi: global-norm clipping supports at most %d tensors per call",
+               kMaxAdamTensors);
+      adam_norm_partial_kernel<<<nb, 256, 0, ctx->stream>>>(p, grad_scale, sanitize, (double*)ws);
+      YL_TRY(check_launch("adam_norm_partial_kernel"));
+      adam_norm_final_kernel<<<1, 32, 0, ctx->stream>>>((double*)ws, nb, norm);
+      YL_TRY(check_launch("adam_norm_final_kernel"));
+    }
+    adam_update_kernel<<<grid_1d(p.start[p.count], 256, ctx->num_sms * 8), 256, 0, ctx->stream>>>(
+        p, lr, b1, b2, eps, c1, c2, grad_scale, sanitize, clip_max_norm, need_norm ? norm : nullptr);
+    YL_TRY(check_launch("adam_update_kernel"));
+  }
+  return YL_OK;
+}
+
+// ------------------------------------------------------------------ Linear
+// LinearGPU (DenoiserMLP.swift:20-71): Y = X W^T + b; dX = dY W; dW = dY^T X;
+// db = sumCols(dY).  Shapes here are tiny (batch <= 64, width <= 512).
+__global__ void linear_fwd_kernel(const float* __restrict__ X, const float* __restrict__ W,
+                                  const float* __restrict__ b, float* __restrict__ Y, int n,
+                                  int ic, int oc) {
+  const int wid = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (wid >= n * oc) return;
+  const int r = wid / oc, o = wid % oc;
+  const float* x = X + (long long)r * ic;
+  const float* w = W + (long long)o * ic;
+  float s = 0.f;
+  for (int i = lane; i < ic; i += 32) s = fmaf(x[i], w[i], s);
+#pragma unroll
+  for (int d = 16; d; d >>= 1) s += __shfl_xor_sync(0xffffffffu, s, d);
+  if (lane == 0) Y[(long long)r * oc + o] = s + (b ? b[o] : 0.f);
+}
+
+__global__ void linear_dx_kernel(const float* __restrict__ W, const float* __restrict__ dY,
+                                 float* __restrict__ dX, int n, int ic, int oc, int acc) {
+  const int idx = blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= n * ic) return;
+  const int r = idx / ic, i = idx % ic;
+  float s = 0.f;
+  for (int o = 0; o < oc; ++o) s = fmaf(dY[(long long)r * oc + o], W[(long long)o * ic + i], s);
+  dX[idx] = acc ? dX[idx] + s : s;
+}
+
+__global__ void linear_dw_kernel(const float* __restrict__ X, const float* __restrict__ dY,
+                                 float* __restrict__ dW, float* __restrict__ db, int n, int ic,
+                                 int oc, int acc) {
+  const int idx = blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx < oc * ic) {
+    const int o = idx / ic, i = idx % ic;
+    float s = 0.f;
+    for (int r = 0; r < n; ++r) s = fmaf(dY[(long long)r * oc + o], X[(long long)r * ic + i], s);
+    dW[idx] = acc ? dW[idx] + s : s;
+  }
+  if (db && idx < oc) {
+    float s = 0.f;
+    for (int r = 0; r < n; ++r) s += dY[(long long)r * oc + idx];
+    db[idx] = acc ? db[idx] + s : s;
+  }
+}
+
+yl_status linear_forward(yl_ctx* ctx, const float* X, const float* W, const float* b, float* Y,
+                         int n, int ic, int oc) {
+  YL_CHECK(X && W && Y, YL_ERR_INVALID, "linear_forward: NULL argument");
+  long long threads = (long long)n * oc * 32;
+  if (threads == 0) return YL_OK;
+  linear_fwd_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, ctx->stream>>>(X, W, b, Y, n, ic,
+                                                                               oc);
+  return check_launch("linear_fwd_kernel");
+}
+
+yl_status linear_backward(yl_ctx* ctx, const float* X, const float* W, const float* dY, float* dX,
+                          float* dW, float* db, int n, int ic, int oc, int accumulate) {
+  YL_CHECK(dY, YL_ERR_INVALID, "linear_backward: dY is NULL");
+  if (dX) {
+    YL_CHECK(W, YL_ERR_INVALID, "linear_backward: W is NULL");
+    linear_dx_kernel<<<(n * ic + 255) / 256, 256, 0, ctx->stream>>>(W, dY, dX, n, ic, oc, 0);
+    YL_TRY(check_launch("linear_dx_kernel"));
+  }
+  if (dW) {
+    YL_CHECK(X, YL_ERR_INVALID, "linear_backward: X is NULL");
+    int m = oc * ic > oc ? oc * ic : oc;
+    linear_dw_kernel<<<(m + 255) / 256, 256, 0, ctx->stream>>>(X, dY, dW, db, n, ic, oc,
+                                                              accumulate);
+    YL_TRY(check_launch("linear_dw_kernel"));
+  } else if (db) {
+    linear_dw_kernel<<<(oc + 255) / 256, 256, 0, ctx->stream>>>(X, dY, nullptr, db, n, 0, oc,
+                                                               accumulate);
+    YL_TRY(check_launch("linear_dw_kernel"));
+  }
+  return YL_OK;
+}
+
+// ------------------------------------------------------------------ embedding / SiLU
+// motionTimeEmbedding (MotionPlanner.swift:155-165) in double, like the
+// reference's host loop; variant 1 is timestep_embedding (src/diffusion.py:6-10).
+__global__ void time_embedding_kernel(const float* __restrict__ t, int n, int dim, int variant,
+                                      float* __restrict__ out) {
+  const int idx = blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= n * (dim / 2)) return;
+  const int b = idx / (dim / 2), j = idx % (dim / 2);
+  if (variant == 0) {
+    double tt = (double)t[b];
+    if (!isfinite(tt)) tt = 0.0;
+    tt = fmin(fmax(tt, 0.0), 1.0);
+    const int i = 2 * j;
+    const double w = pow(1000.0, (double)i / (double)dim);
+    out[(long long)b * dim + i] = (float)sin(tt * w);
+    out[(long long)b * dim + i + 1] = (float)cos(tt * w);
+  } else {
+    const int half = dim / 2;
+    const float f = expf(-logf(10000.f) * (float)j / (float)half);
+    const float a = t[b] * f;
+    out[(long long)b * dim + j] = cosf(a);
+    out[(long long)b * dim + half + j] = sinf(a);
+  }
+}
+
+yl_status time_embedding(yl_ctx* ctx, const float* t, int n, int dim, int variant, float* out) {
+  YL_CHECK(t && out, YL_ERR_INVALID, "time_embedding: NULL argument");
+  YL_CHECK(dim > 0 && dim % 2 == 0, YL_ERR_SHAPE, "time_embedding: dim must be even and > 0");
+  YL_CHECK(variant == 0 || variant == 1, YL_ERR_INVALID, "time_embedding: unknown variant");
+  int total = n * (dim / 2);
+  if (total == 0) return YL_OK;
+  time_embedding_kernel<<<(total + 255) / 256, 256, 0, ctx->stream>>>(t, n, dim, variant, out);
+  return check_launch("time_embedding_kernel");
+}
+
+__global__ void silu_kernel(const float* __restrict__ x, const float* __restrict__ dy,
+                            float* __restrict__ out, long long n, int bwd, int acc) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+       i += (long long)gridDim.x * blockDim.x) {
+    const float a = x[i];
+    const float s = 1.f / (1.f + expf(-a));
+    float r = bwd ? dy[i] * s * (1.f + a * (1.f - s)) : a * s;
+    out[i] = acc ? out[i] + r : r;
+  }
+}
+
+yl_status silu_forward(yl_ctx* ctx, const float* x, float* y, long long n) {
+  silu_kernel<<<grid_1d(n, 256), 256, 0, ctx->stream>>>(x, nullptr, y, n, 0, 0);
+  return check_launch("silu_kernel");
+}
+yl_status silu_backward(yl_ctx* ctx, const float* x, const float* dy, float* dx, long long n,
+                        int accumulate) {
+  silu_kernel<<<grid_1d(n, 256), 256, 0, ctx->stream>>>(x, dy, dx, n, 1, accumulate);
+  return check_launch("silu_kernel");
+}
+
+// ------------------------------------------------------------------ VAE heads
+__device__ __forceinline__ uint32_t yhash(uint32_t x) {
+  x = ((x >> ((x >> 28u) + 4u)) ^ x) * 277803737u;
+  return (x >> 22u) ^ x;
+}
+// randn_kernel (MetalKernelSourcesB.swift:385-402).
+__device__ __forceinline__ float yrandn(uint32_t seed, uint32_t gid) {
+  const uint32_t h1 = yhash(gid * 747796405u + seed * 2891336453u + 1u);
+  const uint32_t h2 = yhash(gid * 2654435761u + seed * 1013904223u + 0x9E3779B9u);
+  const float u1 = fmaxf((float)(h1 >> 8) / 16777216.0f, 1e-7f);
+  const float u2 = (float)(h2 >> 8) / 16777216.0f;
+  return sqrtf(-2.0f * logf(u1)) * cosf(6.28318530718f * u2);
+}
+// trainingNoiseSeed (ConvVAEHelpers.swift:33-37).
+__host__ __device__ __forceinline__ uint32_t noise_seed(int64_t step, int64_t b) {
+  const uint64_t a = (uint64_t)step * 0x9E3779B97F4A7C15ull;
+  const uint64_t bb = (uint64_t)b * 0xC2B2AE3D27D4EB4Full;
+  return (uint32_t)((a ^ (bb + 0x165667B19E3779F9ull)) >> 32);
+}
+
+__global__ void latent_fwd_kernel(const float* __restrict__ e, int lde, int n, long long hw, int c,
+                                  int64_t step, float* __restrict__ z, int ldz) {
+  const long long total = (long long)n * hw * c;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int ch = (int)(i % c);
+    const long long pix = i / c;
+    const int img = (int)(pix / hw);
+    const long long p = pix - (long long)img * hw;
+    const float mu = e[pix * lde + ch];
+    const float lv = fminf(fmaxf(e[pix * lde + c + ch], -10.f), 10.f);
+    const float ep = yrandn(noise_seed(step, img), (uint32_t)(ch * hw + p));
+    z[pix * ldz + ch] = mu + expf(0.5f * lv) * ep;
+  }
+}
+
+__global__ void latent_bwd_kernel(const float* __restrict__ e, int lde,
+                                  const float* __restrict__ dz, int lddz, int n, long long hw,
+                                  int c, int64_t step, float betaN, float betaHalfN,
+                                  float* __restrict__ de, int ldde) {
+  const long long total = (long long)n * hw * c;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int ch = (int)(i % c);
+    const long long pix = i / c;
+    const int img = (int)(pix / hw);
+    const long long p = pix - (long long)img * hw;
+    const float mu = e[pix * lde + ch];
+    const float lv = fminf(fmaxf(e[pix * lde + c + ch], -10.f), 10.f);
+    const float ep = yrandn(noise_seed(step, img), (uint32_t)(ch * hw + p));
+    const float d = dz[pix * lddz + ch];
+    // vae_grad_kernel (MetalKernelSourcesB.swift:365-380)
+    de[pix * ldde + ch] = round_tf32(d + betaN * mu);
+    de[pix * ldde + c + ch] = round_tf32(d * ep * 0.5f * expf(0.5f * lv) + betaHalfN * (expf(lv) - 1.f));
+  }
+}
+
+yl_status latent_head_forward(yl_ctx* ctx, const float* e, int lde, int n, long long hw, int c,
+                              int64_t step, float* z, int ldz) {
+  long long total = (long long)n * hw * c;
+  latent_fwd_kernel<<<grid_1d(total, 256), 256, 0, ctx->stream>>>(e, lde, n, hw, c, step, z, ldz);
+  return check_launch("latent_fwd_kernel");
+}
+
+yl_status latent_head_backward(yl_ctx* ctx, const float* e, int lde, const float* dz, int lddz,
+                               int n, long long hw, int c, int64_t step, float betaN,
+                               float betaHalfN, float* de, int ldde) {
+  long long total = (long long)n * hw * c;
+  latent_bwd_kernel<<<grid_1d(total, 256), 256, 0, ctx->stream>>>(e, lde, dz, lddz, n, hw, c, step,
+                                                                 betaN, betaHalfN, de, ldde);
+  return check_launch("latent_bwd_kernel");
+}
+
+// L1 (l1grad_kernel B:453-461) + KL (kl_reduce_kernel B:334-357) head.
+__global__ void l1_kl_partial_kernel(const float* __restrict__ r, const float* __restrict__ t,
+                                     long long n_pix, int ld, int ch, float inv,
+                                     float* __restrict__ dr, const float* __restrict__ e, int lde,
+                                     long long n_lat, int c_lat, double* part) {
+  double l1 = 0, kl = 0;
+  const long long nr = n_pix * ld;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < nr;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int k = (int)(i % ld);
+    float g = 0.f;
+    if (k < ch) {
+      const float d = r[i] - t[i];
+      l1 += fabs((double)d);
+      g = (d > 0.f ? 1.f : (d < 0.f ? -1.f : 0.f)) * inv;
+    }
+    if (dr) dr[i] = g;
+  }
+  const long long nl = n_lat * c_lat;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < nl;
+       i += (long long)gridDim.x * blockDim.x) {
+    const long long pix = i / c_lat;
+    const int k = (int)(i % c_lat);
+    const float mu = e[pix * lde + k];
+    const float lv = fminf(fmaxf(e[pix * lde + c_lat + k], -10.f), 10.f);
+    kl += 0.5 * ((double)mu * mu + exp((double)lv) - 1.0 - lv);
+  }
+  __shared__ double ra[32], rb[32];
+#pragma unroll
+  for (int o = 16; o; o >>= 1) {
+    l1 += __shfl_xor_sync(0xffffffffu, l1, o);
+    kl += __shfl_xor_sync(0xffffffffu, kl, o);
+  }
+  if ((threadIdx.x & 31) == 0) {
+    ra[threadIdx.x >> 5] = l1;
+    rb[threadIdx.x >> 5] = kl;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double a = 0, b = 0;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) {
+      a += ra[w];
+      b += rb[w];
+    }
+    part[2 * blockIdx.x] = a;
+    part[2 * blockIdx.x + 1] = b;
+  }
+}
+
+__global__ void loss_final_kernel(const double* part, int nb, double sa, double sb, float* out) {
+  if (threadIdx.x == 0) {
+    double a = 0, b = 0;
+    for (int i = 0; i < nb; ++i) {
+      a += part[2 * i];
+      b += part[2 * i + 1];
+    }
+    out[0] = (float)(a * sa + b * sb);
+  }
+}
+
+yl_status l1_kl_head(yl_ctx* ctx, const float* recon, const float* target, long long n_pix, int ld,
+                     int ch, const float* e, int lde, long long n_lat_pix, int c_lat, float beta,
+                     float* drecon, float* loss_out) {
+  const int nb = ctx->num_sms * 2;
+  void* ws = nullptr;
+  YL_TRY(scratch_get(ctx, 2 * nb * sizeof(double), &ws));
+  const double nr = (double)n_pix * ch;
+  const float inv = (float)(1.0 / nr);
+  l1_kl_partial_kernel<<<nb, 256, 0, ctx->stream>>>(recon, target, n_pix, ld, ch, inv, drecon, e,
+                                                    lde, e ? n_lat_pix : 0, c_lat, (double*)ws);
+  YL_TRY(check_launch("l1_kl_partial_kernel"));
+  if (loss_out) {
+    const double nl = (double)n_lat_pix * c_lat;
+    loss_final_kernel<<<1, 32, 0, ctx->stream>>>((double*)ws, nb, 1.0 / nr,
+                                                 nl > 0 ? (double)beta / nl : 0.0, loss_out);
+    YL_TRY(check_launch("loss_final_kernel"));
+  }
+  return YL_OK;
+}
+
+__global__ void mse_partial_kernel(const float* __restrict__ p, const float* __restrict__ t,
+                                   long long n_pix, int ld, int ch, float scale,
+                                   float* __restrict__ dp, double* part) {
+  double s = 0;
+  const long long n = n_pix * ld;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int k = (int)(i % ld);
+    float g = 0.f;
+    if (k < ch) {
+      const float d = p[i] - t[i];
+      s += (double)d * d;
+      g = scale * d;
+    }
+    if (dp) dp[i] = round_tf32(g);
+  }
+  __shared__ double ra[32];
+#pragma unroll
+  for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  if ((threadIdx.x & 31) == 0) ra[threadIdx.x >> 5] = s;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double a = 0;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) a += ra[w];
+    part[2 * blockIdx.x] = a;
+    part[2 * blockIdx.x + 1] = 0.0;
+  }
+}
+
+yl_status mse_head(yl_ctx* ctx, const float* pred, const float* target, long long n_pix, int ld,
+                   int ch, float* dpred, float* loss_out) {
+  const int nb = ctx->num_sms * 2;
+  void* ws = nullptr;
+  YL_TRY(scratch_get(ctx, 2 * nb * sizeof(double), &ws));
+  const double cnt = (double)n_pix * ch;
+  mse_partial_kernel<<<nb, 256, 0, ctx->stream>>>(pred, target, n_pix, ld, ch, (float)(2.0 / cnt),
+                                                  dpred, (double*)ws);
+  YL_TRY(check_launch("mse_partial_kernel"));
+  if (loss_out) {
+    loss_final_kernel<<<1, 32, 0, ctx->stream>>>((double*)ws, nb, 1.0 / cnt, 0.0, loss_out);
+    YL_TRY(check_launch("loss_final_kernel"));
+  }
+  return YL_OK;
+}
+
+}  // namespace yl
