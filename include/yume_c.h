@@ -91,6 +91,10 @@ yl_status yl_tensor_set_value(yl_tensor* t, size_t index, float value);
 /* GpuSession.copy / zeroFill (GpuSessionOps.swift:257-276), stream-ordered. */
 yl_status yl_copy(yl_ctx* ctx, float* dst, const float* src, size_t n);
 yl_status yl_zero_fill(yl_ctx* ctx, float* dst, size_t n);
+/* Host <-> device byte copies on the context's stream; both synchronize
+ * (the staging-buffer upload / toArray paths, GpuSessionOps.swift:8-20). */
+yl_status yl_memcpy_htod(yl_ctx* ctx, void* dst_dev, const void* src_host, size_t bytes);
+yl_status yl_memcpy_dtoh(yl_ctx* ctx, void* dst_host, const void* src_dev, size_t bytes);
 
 /* ------------------------------------------------- reference-mode operators
  * One entry point per GpuSession method, same argument meaning, caller-owned
@@ -279,6 +283,73 @@ yl_status yl_vae_latent_head_bwd(yl_ctx* ctx, const float* e, const float* dz, i
 yl_status yl_loss_l1_kl(yl_ctx* ctx, const float* recon, const float* target, size_t n_recon,
                         const float* mu_logvar, int n, int c_lat, int h_lat, int w_lat, int layout,
                         float beta, float* drecon, float* loss_dev);
+
+/* ------------------------------------------------ data-parallel communicator
+ * NCCL over NVLink/NVSwitch, one rank per GPU.  Rank 0 creates the id; the
+ * caller distributes its bytes (the reference has no multi-GPU path; its
+ * closest relative is the per-frame gradient sum, TrainConvVAE.swift:177-217). */
+#define YL_COMM_ID_BYTES 128
+yl_status yl_comm_get_unique_id(uint8_t* out_id /* YL_COMM_ID_BYTES */);
+yl_status yl_comm_init(yl_ctx* ctx, const uint8_t* id, int rank, int world, yl_comm** out);
+yl_status yl_comm_destroy(yl_comm* comm);
+/* Aborts outstanding collectives (failure handling); destroy afterwards. */
+yl_status yl_comm_abort(yl_comm* comm);
+/* In-place sum over ranks, ordered on `stream` (NULL: the communicator's stream). */
+yl_status yl_allreduce_sum(yl_comm* comm, float* buf, size_t n, void* stream);
+
+/* ------------------------------------------------------- training step
+ * The joint VAE + motion-net step (TrainContext.runStep,
+ * TrainConvVAE.swift:327-362, and runMotionStepPixel, MotionTrainer.swift:
+ * 214-260, re-expressed for the conv VAE and motion U-Net): encoder means of
+ * frames 0 and 16 (no gradient), VAE forward/backward on frame k with
+ * L1 + beta*KL, U-Net on [zA | zB | lerp(zA, zB, t)] predicting mu(frame k)
+ * with MSE, gradient all-reduce overlapped with backward, Adam (0.9, 0.999,
+ * 1e-8).  Nothing is allocated after the first step. */
+typedef struct yl_trainer_config {
+  int batch;            /* frame-pair samples per GPU */
+  int height, width;    /* frame size, multiples of 8 (854 wide frames are padded to 856) */
+  uint64_t seed;        /* parameter initialisation */
+  float lr_vae, lr_motion;
+  float beta_kl;        /* KL weight (1e-6), KL averaged per latent element */
+  float clip_max_norm;  /* > 0: sanitizeGrads semantics (NaN->0 + global L2 clip); 0: off */
+  int train_vae, train_motion;
+  size_t bucket_bytes;  /* all-reduce bucket size; 0 = 25 MB */
+  int profile;          /* time every conv / GroupNorm launch with CUDA events */
+} yl_trainer_config;
+yl_status yl_trainer_create(yl_ctx* ctx, const yl_trainer_config* cfg, yl_comm* comm_or_null,
+                            yl_trainer** out);
+yl_status yl_trainer_destroy(yl_trainer* tr);
+/* frames: device, [3][batch][3][height][width] fp32 in [-1, 1] = frame 0,
+ * frame 16 and frame k of every sample (NCHW); t: device [batch] (k/16);
+ * losses_out (device [2], may be NULL): VAE loss, motion loss (rank mean). */
+yl_status yl_trainer_step(yl_trainer* tr, const float* frames, const float* t, float* losses_out);
+/* The same from host buffers (pinned memory makes the copies asynchronous):
+ * copies in, runs the step, copies the two losses back and synchronizes. */
+yl_status yl_trainer_step_host(yl_trainer* tr, const float* frames_host, const float* t_host,
+                               float* losses_host);
+/* Replace the runtime options (learning rates, which parts train, profiling);
+ * batch and frame size must match creation. */
+yl_status yl_trainer_set_config(yl_trainer* tr, const yl_trainer_config* cfg);
+/* which: 0 = VAE, 1 = motion U-Net.  Flat fp32 buffers on the device;
+ * kind: 0 parameters, 1 gradients, 2 Adam m, 3 Adam v. */
+yl_status yl_trainer_param_count(yl_trainer* tr, int which, size_t* n);
+yl_status yl_trainer_buffer(yl_trainer* tr, int which, int kind, float** dev_ptr);
+/* Parameter table (for checkpoints and tests): conv weights are stored
+ * [oc][k*k][ic rounded up to 4] at `offset`; shape4 = (oc, ic, k, k). */
+yl_status yl_trainer_param_entry(yl_trainer* tr, int which, int index, char* name,
+                                 size_t name_len, size_t* offset, int* shape4);
+/* Re-derive the tf32 weight copies after parameters were written externally. */
+yl_status yl_trainer_prepare_weights(yl_trainer* tr);
+#define YL_KERNEL_CLASSES 5 /* conv fprop, conv dgrad, conv wgrad, GN+SiLU fwd, GN+SiLU bwd */
+typedef struct yl_kernel_stats {
+  double ms[YL_KERNEL_CLASSES];
+  double flops[YL_KERNEL_CLASSES];
+  double bytes[YL_KERNEL_CLASSES];
+  int launches[YL_KERNEL_CLASSES];
+} yl_kernel_stats;
+/* Accumulated CUDA-event times of the profiled steps (cfg.profile = 1). */
+yl_status yl_trainer_kernel_stats(yl_trainer* tr, yl_kernel_stats* out, int reset);
+yl_status yl_trainer_activation_bytes(yl_trainer* tr, size_t* bytes);
 
 #ifdef __cplusplus
 }

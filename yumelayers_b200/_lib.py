@@ -40,6 +40,20 @@ class AdamTensor(C.Structure):
                 ("v", C.c_void_p), ("n", C.c_longlong)]
 
 
+class TrainerConfig(C.Structure):
+    """``yl_trainer_config``."""
+    _fields_ = [("batch", C.c_int), ("height", C.c_int), ("width", C.c_int),
+                ("seed", C.c_uint64), ("lr_vae", C.c_float), ("lr_motion", C.c_float),
+                ("beta_kl", C.c_float), ("clip_max_norm", C.c_float), ("train_vae", C.c_int),
+                ("train_motion", C.c_int), ("bucket_bytes", C.c_size_t), ("profile", C.c_int)]
+
+
+class KernelStats(C.Structure):
+    """``yl_kernel_stats``: conv fprop, conv dgrad, conv wgrad, GN fwd, GN bwd."""
+    _fields_ = [("ms", C.c_double * 5), ("flops", C.c_double * 5), ("bytes", C.c_double * 5),
+                ("launches", C.c_int * 5)]
+
+
 P = C.c_void_p
 I = C.c_int
 F = C.c_float
@@ -70,6 +84,8 @@ SIGNATURES: dict[str, list] = {
     "yl_tensor_set_value": [P, SZ, F],
     "yl_copy": [P, P, P, SZ],
     "yl_zero_fill": [P, P, SZ],
+    "yl_memcpy_htod": [P, P, P, SZ],
+    "yl_memcpy_dtoh": [P, P, P, SZ],
     "yl_matmul": [P, P, P, P, I, I, I, I, I],
     "yl_im2col": [P, P, P, I, I, I, I, I, I, I],
     "yl_col2im": [P, P, P, I, I, I, I, I, I, I, I, I],
@@ -113,6 +129,22 @@ SIGNATURES: dict[str, list] = {
     "yl_vae_latent_head_fwd": [P, P, I, I, I, I, I, I64, P],
     "yl_vae_latent_head_bwd": [P, P, P, I, I, I, I, I, I64, F, P],
     "yl_loss_l1_kl": [P, P, P, SZ, P, I, I, I, I, I, F, P, P],
+    "yl_comm_get_unique_id": [P],
+    "yl_comm_init": [P, P, I, I, C.POINTER(P)],
+    "yl_comm_destroy": [P],
+    "yl_comm_abort": [P],
+    "yl_allreduce_sum": [P, P, SZ, P],
+    "yl_trainer_create": [P, C.POINTER(TrainerConfig), P, C.POINTER(P)],
+    "yl_trainer_destroy": [P],
+    "yl_trainer_step": [P, P, P, P],
+    "yl_trainer_step_host": [P, P, P, P],
+    "yl_trainer_set_config": [P, C.POINTER(TrainerConfig)],
+    "yl_trainer_param_count": [P, I, C.POINTER(SZ)],
+    "yl_trainer_buffer": [P, I, I, C.POINTER(P)],
+    "yl_trainer_param_entry": [P, I, I, C.c_char_p, SZ, C.POINTER(SZ), C.POINTER(I)],
+    "yl_trainer_prepare_weights": [P],
+    "yl_trainer_kernel_stats": [P, C.POINTER(KernelStats), I],
+    "yl_trainer_activation_bytes": [P, C.POINTER(SZ)],
 }
 _RET = {"yl_last_error_message": C.c_char_p, "yl_version": C.c_char_p,
         "yl_ctx_get_stream": P, "yl_tensor_data": P, "yl_tensor_rows": I, "yl_tensor_cols": I}

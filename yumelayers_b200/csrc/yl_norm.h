@@ -38,7 +38,8 @@ yl_status adam_multi(yl_ctx* ctx, const AdamTensor* tensors, int count, float lr
                      float b2, float eps, int t, float grad_scale, float clip_max_norm,
                      int sanitize, float* norm_out);
 
-// Linear: Y = X W^T + b (W is [oc][ic]); backward outputs optional.
+// Linear: Y = X W^T + b (W is [oc][ic]); backward outputs optional; with
+// accumulate != 0 all of dX, dW, db are added to.
 yl_status linear_forward(yl_ctx* ctx, const float* X, const float* W, const float* b, float* Y,
                          int n, int ic, int oc);
 yl_status linear_backward(yl_ctx* ctx, const float* X, const float* W, const float* dY, float* dX,

@@ -253,6 +253,20 @@ yl_status yl_copy(yl_ctx* ctx, float* dst, const float* src, size_t n) {
   return YL_OK;
 }
 
+yl_status yl_memcpy_htod(yl_ctx* ctx, void* dst, const void* src, size_t bytes) {
+  YL_CHECK(ctx && dst && src, YL_ERR_INVALID, "yl_memcpy_htod: NULL argument");
+  YL_CUDA(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, ctx->stream));
+  YL_CUDA(cudaStreamSynchronize(ctx->stream));
+  return YL_OK;
+}
+
+yl_status yl_memcpy_dtoh(yl_ctx* ctx, void* dst, const void* src, size_t bytes) {
+  YL_CHECK(ctx && dst && src, YL_ERR_INVALID, "yl_memcpy_dtoh: NULL argument");
+  YL_CUDA(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, ctx->stream));
+  YL_CUDA(cudaStreamSynchronize(ctx->stream));
+  return YL_OK;
+}
+
 yl_status yl_zero_fill(yl_ctx* ctx, float* dst, size_t n) {
   YL_CHECK(ctx && dst, YL_ERR_INVALID, "yl_zero_fill: NULL argument");
   YL_CUDA(cudaMemsetAsync(dst, 0, n * sizeof(float), ctx->stream));

@@ -192,7 +192,8 @@ yl_status linear_backward(yl_ctx* ctx, const float* X, const float* W, const flo
   YL_CHECK(dY, YL_ERR_INVALID, "linear_backward: dY is NULL");
   if (dX) {
     YL_CHECK(W, YL_ERR_INVALID, "linear_backward: W is NULL");
-    linear_dx_kernel<<<(n * ic + 255) / 256, 256, 0, ctx->stream>>>(W, dY, dX, n, ic, oc, 0);
+    linear_dx_kernel<<<(n * ic + 255) / 256, 256, 0, ctx->stream>>>(W, dY, dX, n, ic, oc,
+                                                                   accumulate);
     YL_TRY(check_launch("linear_dx_kernel"));
   }
   if (dW) {
