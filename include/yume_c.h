@@ -49,6 +49,8 @@ typedef struct yl_trainer yl_trainer;
 /* Thread-local text of the last non-OK status returned on this thread. */
 const char* yl_last_error_message(void);
 const char* yl_version(void);
+/* Number of kernels this library has launched in the process so far. */
+unsigned long long yl_kernel_launch_count(void);
 
 /* ------------------------------------------------------------------ runtime
  * Replaces MetalEngine (MetalEngine.swift:6-419: device, queue, pools) and
@@ -350,6 +352,22 @@ typedef struct yl_kernel_stats {
 /* Accumulated CUDA-event times of the profiled steps (cfg.profile = 1). */
 yl_status yl_trainer_kernel_stats(yl_trainer* tr, yl_kernel_stats* out, int reset);
 yl_status yl_trainer_activation_bytes(yl_trainer* tr, size_t* bytes);
+
+/* ---------------------------------------------------------------- diagnostics
+ * profileConv / runGpuBench (Diagnostics.swift:83-201): device time per launch
+ * of one conv shape's forward, dX and dW kernels on NHWC buffers the call
+ * allocates and frees itself (input n x h x w x c, or its x2 upsample when
+ * up = 1; k x k kernel, pad k/2). */
+typedef struct yl_conv_profile {
+  double fprop_ms, dgrad_ms, wgrad_ms;
+  double flops; /* 2 * MACs of one pass */
+  int wgrad_splits;
+} yl_conv_profile;
+yl_status yl_profile_conv(yl_ctx* ctx, int n, int c, int h, int w, int oc, int k, int stride,
+                          int up, int reps, yl_conv_profile* out);
+/* GroupNorm(32)+SiLU forward and backward on an n x h x w x c NHWC tensor. */
+yl_status yl_profile_groupnorm(yl_ctx* ctx, int n, int c, int h, int w, int reps, double* fwd_ms,
+                               double* bwd_ms);
 
 #ifdef __cplusplus
 }

@@ -70,44 +70,51 @@ ORC_API void orc_matmul(const float* A, const float* B, float* C, int M, int N,
   }
 }
 
-/* Blocked fp32 GEMM used by the conv composition below, so the CPU baseline is
- * a fair one: C[M,N] (+)= A[M,K] * B[K,N], row-major, OpenMP over rows.  It is
- * the same sum as orc_matmul (different association order). */
+/* Cache-blocked fp32 GEMM used by the conv composition below, so the timed
+ * CPU baseline is a fair one: C[M,N] (+)= A[M,K] * B[K,N], row-major.  The
+ * (M-block x N-block) tiles are spread over OpenMP threads; a KB x NB panel
+ * of B stays in L2 while the rows of the tile stream through it.  It is the
+ * same sum as orc_matmul (different association order). */
+enum { GEMM_MB = 32, GEMM_NB = 512, GEMM_KB = 128 };
 static void gemm_nn(const float* A, const float* B, float* C, int M, int N, int K,
                     int accumulate) {
-#pragma omp parallel for schedule(static)
-  for (int r = 0; r < M; ++r) {
-    float* crow = C + (size_t)r * N;
-    if (!accumulate) memset(crow, 0, sizeof(float) * (size_t)N);
-    for (int k0 = 0; k0 < K; k0 += 256) {
-      int k1 = k0 + 256 < K ? k0 + 256 : K;
-      for (int k = k0; k < k1; ++k) {
-        float a = A[(size_t)r * K + k];
-        if (a == 0.0f) continue;
-        const float* brow = B + (size_t)k * N;
-        for (int c = 0; c < N; ++c) crow[c] += a * brow[c];
+  const int mt = (M + GEMM_MB - 1) / GEMM_MB, nt = (N + GEMM_NB - 1) / GEMM_NB;
+#pragma omp parallel for schedule(dynamic, 1) collapse(2)
+  for (int bm = 0; bm < mt; ++bm)
+    for (int bn = 0; bn < nt; ++bn) {
+      const int m0 = bm * GEMM_MB, m1 = m0 + GEMM_MB < M ? m0 + GEMM_MB : M;
+      const int n0 = bn * GEMM_NB, n1 = n0 + GEMM_NB < N ? n0 + GEMM_NB : N;
+      const int nw = n1 - n0;
+      if (!accumulate)
+        for (int r = m0; r < m1; ++r) memset(C + (size_t)r * N + n0, 0, sizeof(float) * nw);
+      for (int k0 = 0; k0 < K; k0 += GEMM_KB) {
+        const int k1 = k0 + GEMM_KB < K ? k0 + GEMM_KB : K;
+        for (int r = m0; r < m1; ++r) {
+          float* crow = C + (size_t)r * N + n0;
+          const float* arow = A + (size_t)r * K;
+          for (int k = k0; k < k1; ++k) {
+            const float a = arow[k];
+            if (a == 0.0f) continue;
+            const float* brow = B + (size_t)k * N + n0;
+#pragma omp simd
+            for (int c = 0; c < nw; ++c) crow[c] += a * brow[c];
+          }
+        }
       }
     }
-  }
 }
 
-/* C[M,N] (+)= A[M,K] * B[N,K]^T (both K-contiguous) -- the gradW shape. */
+/* C[M,N] (+)= A[M,K] * B[N,K]^T (both K-contiguous) -- the gradW shape:
+ * B is transposed once into a K x N panel and the blocked gemm_nn runs. */
 static void gemm_nt(const float* A, const float* B, float* C, int M, int N, int K,
                     int accumulate) {
+  float* bt = (float*)malloc(sizeof(float) * (size_t)K * N);
 #pragma omp parallel for schedule(static)
-  for (int r = 0; r < M * N; ++r) {
-    int i = r / N, j = r % N;
-    const float* a = A + (size_t)i * K;
-    const float* b = B + (size_t)j * K;
-    double acc = 0.0;
-    float part = 0.0f;
-    for (int k = 0; k < K; ++k) {
-      part += a[k] * b[k];
-      if ((k & 1023) == 1023) { acc += part; part = 0.0f; }
-    }
-    acc += part;
-    if (accumulate) C[r] += (float)acc; else C[r] = (float)acc;
-  }
+  for (int k0 = 0; k0 < K; k0 += 64)
+    for (int j = 0; j < N; ++j)
+      for (int k = k0; k < k0 + 64 && k < K; ++k) bt[(size_t)k * N + j] = B[(size_t)j * K + k];
+  gemm_nn(A, bt, C, M, N, K, accumulate);
+  free(bt);
 }
 
 /* im2col3d_kernel (MetalKernelSourcesA.swift:325-352): X (ic, ih, iw) ->
@@ -602,23 +609,17 @@ ORC_API void orc_conv2d_bwd(const float* x, int N, int C, int H, int W,
       }
     }
     if (dx) {
-      if (stride == 1) {
-        orc_conv_back_input_s1(dyn, w, dxin, C, OC, ih, iw, k, k, pad);
-      } else {
-        /* dcols = W^T * dOut (matmul transA, ConvGPU.swift:75), then col2im. */
-        float* dcols = cols;
-#pragma omp parallel for schedule(static)
-        for (int r = 0; r < kk; ++r) {
-          float* row = dcols + (size_t)r * plane_out;
-          memset(row, 0, sizeof(float) * plane_out);
-          for (int o = 0; o < OC; ++o) {
-            float wv = w[(size_t)o * kk + r];
-            const float* drow = dyn + (size_t)o * plane_out;
-            for (size_t p = 0; p < plane_out; ++p) row[p] += wv * drow[p];
-          }
-        }
-        orc_col2im(dcols, dxin, C, ih, iw, k, k, stride, pad, oh, ow);
-      }
+      /* dcols = W^T * dOut (matmul transA, ConvGPU.swift:75), then the col2im
+       * gather (col2im3d / col2im3d_s1, MetalKernelSourcesB.swift:28-85); for
+       * stride 1 this equals conv_back_input_s1 (B:125-159), which the
+       * per-op tests check separately. */
+      float* dcols = cols;
+      float* wt = (float*)malloc(sizeof(float) * (size_t)kk * OC);
+      for (int o = 0; o < OC; ++o)
+        for (int r = 0; r < kk; ++r) wt[(size_t)r * OC + o] = w[(size_t)o * kk + r];
+      gemm_nn(wt, dyn, dcols, kk, (int)plane_out, OC, 0);
+      free(wt);
+      orc_col2im(dcols, dxin, C, ih, iw, k, k, stride, pad, oh, ow);
       float* dxn = dx + (size_t)n * C * H * W;
       if (up) {
         memset(dxn, 0, sizeof(float) * C * H * W);

@@ -1,0 +1,116 @@
+"""The joint VAE + motion-net training step on the GPU against the CPU oracle
+composition of the reference's kernels (oracle/nets.py), from identical
+weights and inputs: per-step losses within 1e-3 relative, and the weights
+after several Adam steps close (tf32 operands on the GPU, fp32 on the CPU).
+"""
+import sys
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+sys.path.insert(0, str(Path(__file__).resolve().parents[1] / "oracle"))
+
+pytestmark = pytest.mark.gpu
+LOSS_TOL = 1e-3
+
+
+def _setup(batch=2, h=32, w=48, seed=3):
+    from yumelayers_b200 import synth
+    from yumelayers_b200.trainer import Trainer, default_config
+    import nets
+    tr = Trainer(default_config(batch=batch, height=h, width=w, seed=seed))
+    vp = nets.Params(tr.param_table(0), tr.download(0))
+    up = nets.Params(tr.param_table(1), tr.download(1))
+    js = nets.JointStep(vp, up, tr.param_count(0), tr.param_count(1))
+    rng = np.random.default_rng(seed)
+    batches = []
+    for s in range(4):
+        frames = np.stack([np.stack([synth.make_frame(100 * s + 10 * b + f, h, w, w)
+                                     for b in range(batch)]) for f in range(3)])
+        t = (rng.integers(1, 16, batch) / 16.0).astype(np.float32)
+        batches.append((np.ascontiguousarray(frames, np.float32), t))
+    return tr, js, batches
+
+
+def _resync(js, tr):
+    """Give the oracle the GPU's current weights (each step then measures the
+    step's own error, not the drift of two trajectories)."""
+    import nets
+    for which, P in ((0, js.vp), (1, js.up)):
+        fresh = nets.Params(P.table, tr.download(which))
+        P.p.update(fresh.p)
+        js.flat[which] = tr.download(which)
+
+
+def test_joint_step_losses_match_oracle_100_steps():
+    """Per-step loss within 1e-3 over 100 training steps: before every step the
+    oracle takes the GPU's weights; both then run the same step on the same
+    frames (the GPU's Adam keeps training the weights between steps)."""
+    tr, js, batches = _setup()
+    worst = 0.0
+    rows = []
+    for step in range(100):
+        frames, t = batches[step % len(batches)]
+        _resync(js, tr)
+        js.step_no = step
+        gpu = tr.step_host(frames, t)
+        cpu = js.step(frames, t)
+        rel = [abs(g - c) / abs(c) for g, c in zip(gpu, cpu)]
+        if max(rel) > worst or step < 3:
+            rows.append(f"step {step + 1}: vae {gpu[0]:.6f}/{cpu[0]:.6f} ({rel[0]:.1e}) "
+                        f"motion {gpu[1]:.6f}/{cpu[1]:.6f} ({rel[1]:.1e})")
+        worst = max(worst, *rel)
+    assert worst < LOSS_TOL, "per-step losses GPU/CPU:\n" + "\n".join(rows)
+    tr.close()
+
+
+def test_free_running_trajectories_stay_close():
+    """Without re-syncing, the two trajectories drift apart only slowly (Adam's
+    first steps move every weight by ~lr with the sign of its gradient, so
+    weights whose gradient is ~0 may step either way on either side)."""
+    tr, js, batches = _setup()
+    worst = 0.0
+    for step in range(6):
+        frames, t = batches[step % len(batches)]
+        gpu = tr.step_host(frames, t)
+        cpu = js.step(frames, t)
+        worst = max(worst, *[abs(g - c) / abs(c) for g, c in zip(gpu, cpu)])
+    assert worst < 5e-3, worst
+    for which in (0, 1):
+        got = tr.download(which)
+        ref = js.flat[which]
+        diff = np.linalg.norm(got - ref) / np.linalg.norm(ref)
+        assert diff < 1e-2, (which, diff)
+    tr.close()
+
+
+def test_vae_gradients_match_oracle():
+    """One VAE step's full gradient vector (before Adam) against the oracle's."""
+    from yumelayers_b200.trainer import Trainer, default_config
+    import nets
+    tr = Trainer(default_config(batch=2, height=32, width=48, seed=5, train_motion=0,
+                                lr_vae=0.0))
+    vp = nets.Params(tr.param_table(0), tr.download(0))
+    ops = nets.Ops()
+    vae = nets.VAE(ops, vp)
+    rng = np.random.default_rng(1)
+    x = np.clip(rng.standard_normal((3, 2, 3, 32, 48)) * 0.5, -1, 1).astype(np.float32)
+    gpu_loss = tr.step_host(x, np.full(2, 0.5, np.float32))
+    g_gpu = tr.download(0, kind=1)
+    loss, g, _ = vae.train_forward_backward(x[2], 1, 1e-6)
+    g_ref = vp.to_flat(g, g_gpu.size)
+    assert abs(gpu_loss[0] - loss) / loss < LOSS_TOL
+    rel = np.linalg.norm(g_gpu - g_ref) / np.linalg.norm(g_ref)
+    assert rel < 1e-2, rel
+    # per-tensor check on the larger tensors (tf32 error compounds through depth)
+    worst = 0.0
+    for e in vp.table:
+        n = int(np.prod([d for d in e.shape if d > 0]))
+        if n < 4096:
+            continue
+        a = np.asarray(vp._get(e, g_gpu))
+        b = np.asarray(vp._get(e, g_ref))
+        worst = max(worst, float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30)))
+    assert worst < 2e-2, worst
+    tr.close()

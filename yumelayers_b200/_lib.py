@@ -147,6 +147,7 @@ SIGNATURES: dict[str, list] = {
     "yl_trainer_activation_bytes": [P, C.POINTER(SZ)],
 }
 _RET = {"yl_last_error_message": C.c_char_p, "yl_version": C.c_char_p,
+        "yl_kernel_launch_count": C.c_ulonglong,
         "yl_ctx_get_stream": P, "yl_tensor_data": P, "yl_tensor_rows": I, "yl_tensor_cols": I}
 NON_STATUS = set(_RET)
 
@@ -171,6 +172,7 @@ def lib() -> C.CDLL:
         getattr(L, name).restype = res
     L.yl_last_error_message.argtypes = []
     L.yl_version.argtypes = []
+    L.yl_kernel_launch_count.argtypes = []
     _lib = L
     return L
 
@@ -185,3 +187,13 @@ def check(status: int) -> None:
 def call(name: str, *args) -> None:
     """Call a status-returning C entry point and raise on failure."""
     check(getattr(lib(), name)(*args))
+
+
+class ConvProfile(C.Structure):
+    """``yl_conv_profile``."""
+    _fields_ = [("fprop_ms", C.c_double), ("dgrad_ms", C.c_double), ("wgrad_ms", C.c_double),
+                ("flops", C.c_double), ("wgrad_splits", C.c_int)]
+
+
+SIGNATURES["yl_profile_conv"] = [P, I, I, I, I, I, I, I, I, I, C.POINTER(ConvProfile)]
+SIGNATURES["yl_profile_groupnorm"] = [P, I, I, I, I, I, C.POINTER(D), C.POINTER(D)]

@@ -1,0 +1,187 @@
+// yl_diag.cu -- kernel-level diagnostics: the B200 counterpart of the
+// reference's profileConv / runGpuBench (Diagnostics.swift:83-201), timing
+// one conv shape's forward, dX and dW kernels (and GroupNorm+SiLU) with CUDA
+// events on NHWC buffers the call allocates itself.
+#include <vector>
+
+#include "yl_kernels.h"
+#include "yl_norm.h"
+#include "yume_c.h"
+
+using namespace yl;
+
+namespace {
+
+__global__ void fill_kernel(float* p, long long n, uint32_t seed, float scale) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+       i += (long long)gridDim.x * blockDim.x) {
+    uint32_t x = (uint32_t)i * 2654435761u ^ seed;
+    x ^= x >> 15;
+    x *= 2246822519u;
+    x ^= x >> 13;
+    p[i] = scale * ((float)(x & 0xFFFFFF) / 8388608.0f - 1.0f);
+  }
+}
+
+struct DevBufs {
+  std::vector<void*> ptrs;
+  ~DevBufs() {
+    for (void* p : ptrs) cudaFree(p);
+  }
+  yl_status get(size_t floats, float** out) {
+    void* p = nullptr;
+    cudaError_t e = cudaMalloc(&p, floats * sizeof(float));
+    if (e != cudaSuccess)
+      return set_error(YL_ERR_OOM, "profile buffer of %zu floats: %s", floats,
+                       cudaGetErrorString(e));
+    ptrs.push_back(p);
+    *out = (float*)p;
+    return YL_OK;
+  }
+};
+
+}  // namespace
+
+extern "C" {
+
+yl_status yl_profile_conv(yl_ctx* ctx, int n, int c, int h, int w, int oc, int k, int stride,
+                          int up, int reps, yl_conv_profile* out) {
+  YL_CHECK(ctx && out && reps >= 1, YL_ERR_INVALID, "yl_profile_conv: bad argument");
+  YL_CHECK(c % 4 == 0 && oc % 4 == 0, YL_ERR_SHAPE, "yl_profile_conv: channels multiple of 4");
+  const int pad = k / 2;
+  const int ih = up ? 2 * h : h, iw = up ? 2 * w : w;
+  const int oh = (ih + 2 * pad - k) / stride + 1, ow = (iw + 2 * pad - k) / stride + 1;
+  DevBufs b;
+  float *x, *wt, *wd, *y, *dy, *dx, *dw;
+  YL_TRY(b.get((size_t)n * h * w * c, &x));
+  YL_TRY(b.get((size_t)oc * k * k * c, &wt));
+  YL_TRY(b.get((size_t)oc * k * k * c, &wd));
+  YL_TRY(b.get((size_t)n * oh * ow * oc, &y));
+  YL_TRY(b.get((size_t)n * oh * ow * oc, &dy));
+  YL_TRY(b.get((size_t)n * ih * iw * c, &dx));
+  YL_TRY(b.get((size_t)oc * k * k * c, &dw));
+  fill_kernel<<<1024, 256, 0, ctx->stream>>>(x, (long long)n * h * w * c, 1, 1.f);
+  fill_kernel<<<1024, 256, 0, ctx->stream>>>(wt, (long long)oc * k * k * c, 2, 0.05f);
+  fill_kernel<<<1024, 256, 0, ctx->stream>>>(wd, (long long)oc * k * k * c, 3, 0.05f);
+  fill_kernel<<<1024, 256, 0, ctx->stream>>>(dy, (long long)n * oh * ow * oc, 4, 1.f);
+  YL_TRY(check_launch("fill_kernel"));
+  ConvGather g;
+  g.src = x;
+  g.img_stride = (long long)h * w * c;
+  g.row_stride = w * c;
+  g.ps = c;
+  g.cin = c;
+  g.hv = ih;
+  g.wv = iw;
+  g.up = up;
+  g.mode = MODE_FPROP;
+  g.ksize = k;
+  g.stride = stride;
+  g.pad = pad;
+  g.oh = oh;
+  g.ow = ow;
+  g.m_total = n * oh * ow;
+  g.k_total = k * k * c;
+  ConvEpilogue e;
+  e.out = y;
+  e.ldo = oc;
+  e.n_total = oc;
+  ConvGather gd;
+  gd.src = dy;
+  gd.img_stride = (long long)oh * ow * oc;
+  gd.row_stride = ow * oc;
+  gd.ps = oc;
+  gd.cin = oc;
+  gd.hv = oh;
+  gd.wv = ow;
+  gd.mode = MODE_DGRAD;
+  gd.ksize = k;
+  gd.stride = stride;
+  gd.pad = pad;
+  gd.oh = ih;
+  gd.ow = iw;
+  gd.m_total = n * ih * iw;
+  gd.k_total = k * k * oc;
+  ConvEpilogue ed;
+  ed.out = dx;
+  ed.ldo = c;
+  ed.n_total = c;
+  const int splits = conv_wgrad_pick_splits(ctx, oc, g.k_total, g.m_total);
+  float* ws;
+  YL_TRY(b.get((size_t)splits * oc * g.k_total, &ws));
+  cudaEvent_t e0, e1;
+  YL_CUDA(cudaEventCreate(&e0));
+  YL_CUDA(cudaEventCreate(&e1));
+  double ms[3] = {0, 0, 0};
+  for (int mode = 0; mode < 3; ++mode) {
+    for (int r = -1; r < reps; ++r) {  // r = -1 is an untimed warm-up
+      if (r == 0) YL_CUDA(cudaEventRecord(e0, ctx->stream));
+      if (mode == 0) YL_TRY(conv_fprop(ctx, g, wt, oc, e));
+      if (mode == 1) YL_TRY(conv_fprop(ctx, gd, wd, c, ed));
+      if (mode == 2) YL_TRY(conv_wgrad_ws(ctx, dy, oc, oc, g, dw, 0, ws, splits));
+    }
+    YL_CUDA(cudaEventRecord(e1, ctx->stream));
+    YL_CUDA(cudaEventSynchronize(e1));
+    float t = 0.f;
+    YL_CUDA(cudaEventElapsedTime(&t, e0, e1));
+    ms[mode] = t / reps;
+  }
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  out->fprop_ms = ms[0];
+  out->dgrad_ms = ms[1];
+  out->wgrad_ms = ms[2];
+  out->flops = 2.0 * n * oh * ow * (double)oc * c * k * k;
+  out->wgrad_splits = splits;
+  return yl_ctx_check_device_errors(ctx);
+}
+
+yl_status yl_profile_groupnorm(yl_ctx* ctx, int n, int c, int h, int w, int reps, double* fwd_ms,
+                               double* bwd_ms) {
+  YL_CHECK(ctx && fwd_ms && bwd_ms && reps >= 1, YL_ERR_INVALID, "yl_profile_groupnorm");
+  const long long e = (long long)n * h * w * c;
+  DevBufs b;
+  float *x, *y, *dy, *dx, *g, *bt, *dg, *db, *m, *r;
+  YL_TRY(b.get(e, &x));
+  YL_TRY(b.get(e, &y));
+  YL_TRY(b.get(e, &dy));
+  YL_TRY(b.get(e, &dx));
+  YL_TRY(b.get(c, &g));
+  YL_TRY(b.get(c, &bt));
+  YL_TRY(b.get(c, &dg));
+  YL_TRY(b.get(c, &db));
+  YL_TRY(b.get((size_t)n * 32, &m));
+  YL_TRY(b.get((size_t)n * 32, &r));
+  fill_kernel<<<1024, 256, 0, ctx->stream>>>(x, e, 5, 1.f);
+  fill_kernel<<<1024, 256, 0, ctx->stream>>>(dy, e, 6, 1.f);
+  fill_kernel<<<4, 256, 0, ctx->stream>>>(g, c, 7, 1.f);
+  fill_kernel<<<4, 256, 0, ctx->stream>>>(bt, c, 8, 0.1f);
+  YL_TRY(check_launch("fill_kernel"));
+  cudaEvent_t e0, e1;
+  YL_CUDA(cudaEventCreate(&e0));
+  YL_CUDA(cudaEventCreate(&e1));
+  double ms[2];
+  for (int mode = 0; mode < 2; ++mode) {
+    for (int rr = -1; rr < reps; ++rr) {
+      if (rr == 0) YL_CUDA(cudaEventRecord(e0, ctx->stream));
+      if (mode == 0)
+        YL_TRY(gn_silu_forward(ctx, x, n, c, 32, (long long)h * w, c, 1e-6f, 0, g, bt, 1, y, c, 1,
+                               m, r));
+      else
+        YL_TRY(gn_silu_backward(ctx, x, dy, c, n, c, 32, (long long)h * w, c, m, r, g, bt, 1, y, c,
+                                dx, c, 1, dg, db, 0));
+    }
+    YL_CUDA(cudaEventRecord(e1, ctx->stream));
+    YL_CUDA(cudaEventSynchronize(e1));
+    float t = 0.f;
+    YL_CUDA(cudaEventElapsedTime(&t, e0, e1));
+    ms[mode] = t / reps;
+  }
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  *fwd_ms = ms[0];
+  *bwd_ms = ms[1];
+  return yl_ctx_check_device_errors(ctx);
+}
+
+}  // extern "C"

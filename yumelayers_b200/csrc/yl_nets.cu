@@ -80,10 +80,11 @@ __global__ void slice_copy_kernel(const float* __restrict__ src, int lds, float*
 }
 
 // Motion-net input (MotionMLP.swift:39-55: concat [zA | zB] and lerp(zA, zB, t)):
-// out[p] = [zA | zB | (1-t) zA + t zB], 32 channels each, t per image.
+// out[p] = [zA | zB | (1-t) zA + t zB], 32 channels each, t per image, rounded
+// to tf32 for the first conv; lerp_out keeps the fp32 lerp the prediction adds.
 __global__ void motion_input_kernel(const float* __restrict__ za, const float* __restrict__ zb,
                                    int ldz, const float* __restrict__ t, long long hw, int n,
-                                   int c, float* __restrict__ out) {
+                                   int c, float* __restrict__ out, float* __restrict__ lerp_out) {
   const long long total = (long long)n * hw * c;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
        i += (long long)gridDim.x * blockDim.x) {
@@ -94,7 +95,9 @@ __global__ void motion_input_kernel(const float* __restrict__ za, const float* _
     float* o = out + p * 3 * c;
     o[k] = round_tf32(a);
     o[c + k] = round_tf32(b);
-    o[2 * c + k] = round_tf32((1.f - tt) * a + tt * b);
+    const float l = (1.f - tt) * a + tt * b;
+    o[2 * c + k] = round_tf32(l);
+    lerp_out[p * c + k] = l;
   }
 }
 
@@ -535,6 +538,7 @@ yl_status VAE::build(yl_ctx* c, int n, int h, int w, uint64_t seed) {
   YL_TRY(params.allocate());
   // activations
   YL_TRY(x_in.make(arena, n, h, w, 4));
+  YL_TRY(x_tgt.make(arena, n, h, w, 4));
   YL_TRY(conv_in.bind(*this));
   YL_TRY(a0.make(arena, n, h, w, 128));
   YL_TRY(e1a.bind(*this, n, h, w));
@@ -760,6 +764,7 @@ yl_status UNet::build(yl_ctx* c, int n, int h, int w, uint64_t seed) {
   YL_TRY(arena.alloc((size_t)n * kTime, &dtmp2));
   for (int i = 0; i < kBlocks; ++i) YL_TRY(arena.alloc((size_t)n * rbs[i]->cout, &pj[i]));
   YL_TRY(inp.make(arena, n, h, w, 3 * kLat));
+  YL_TRY(lerp.make(arena, n, h, w, kLat));
   YL_TRY(conv_in.bind(*this));
   YL_TRY(h0.make(arena, n, h, w, 128));
   YL_TRY(r1a.bind(*this, n, h, w));
@@ -829,9 +834,9 @@ yl_status UNet::forward() {
   YL_TRY(r5a.forward(*this, cat2, pj[8]));
   YL_TRY(r5b.forward(*this, r5a.y, pj[9]));
   YL_TRY(gn_o.forward(*this, r5b.y, ho));
-  // prediction = lerp(zA, zB, t) + net output (MotionMLP.swift:39-55): the lerp is
-  // channels [64, 96) of the input, added in the epilogue
-  return conv_o.forward(*this, ho, pred, inp.p + 2 * kLat, inp.ld);
+  // prediction = lerp(zA, zB, t) + net output (MotionMLP.swift:39-55), the fp32
+  // lerp added in the epilogue
+  return conv_o.forward(*this, ho, pred, lerp.p, lerp.ld);
 }
 
 yl_status UNet::backward() {
@@ -913,13 +918,14 @@ yl_status UNet::backward() {
 yl_status UNet::set_inputs(const float* za, const float* zb, int ldz, const float* tdev) {
   YL_CUDA(cudaMemcpyAsync(t, tdev, N * sizeof(float), cudaMemcpyDeviceToDevice, ctx->stream));
   motion_input_kernel<<<grid_1d((long long)N * H * W * kLat, 256), 256, 0, ctx->stream>>>(
-      za, zb, ldz, t, (long long)H * W, N, kLat, inp.p);
+      za, zb, ldz, t, (long long)H * W, N, kLat, inp.p, lerp.p);
   return check_launch("motion_input_kernel");
 }
 
 // ------------------------------------------------------------------ frames
-yl_status frames_to_nhwc4(yl_ctx* ctx, const float* nchw3, int n, int h, int w, float* out) {
-  return nchw_to_nhwc(ctx, nchw3, out, n, 3, (long long)h * w, 4, 1);
+yl_status frames_to_nhwc4(yl_ctx* ctx, const float* nchw3, int n, int h, int w, float* out,
+                          int round) {
+  return nchw_to_nhwc(ctx, nchw3, out, n, 3, (long long)h * w, 4, round);
 }
 
 yl_status copy_mu(yl_ctx* ctx, const Act& e, float* dst, int c) {

@@ -158,7 +158,7 @@ struct VAE : Net {
   ConvL conv_in, down1, down2, down3, conv_eo, conv_z, up1, up2, up3, conv_do;
   RB e1a, e1b, e2a, e2b, e3a, e3b, d1a, d1b, d2a, d2b, d3a, d3b;
   GNL gn_eo, gn_do;
-  Act x_in, a0, a1, a2, a3, hg, e, z, b0, b1, b2, b3, hd, recon, drecon;
+  Act x_in, x_tgt, a0, a1, a2, a3, hg, e, z, b0, b1, b2, b3, hd, recon, drecon;
   yl_status build(yl_ctx* ctx, int n, int h, int w, uint64_t seed);
   yl_status encode();                 // x_in -> e = [mu | logvar]
   yl_status decode();                 // z -> recon
@@ -178,14 +178,15 @@ struct UNet : Net {
   float *t = nullptr, *emb = nullptr, *th = nullptr, *ta = nullptr, *temb = nullptr, *ts = nullptr;
   float *dts = nullptr, *dtmp = nullptr, *dtmp2 = nullptr;
   float* pj[kBlocks] = {};
-  Act inp, h0, p1, p2, cat1, cat2, ho, pred, dpred, target;
+  Act inp, lerp, h0, p1, p2, cat1, cat2, ho, pred, dpred, target;
   yl_status build(yl_ctx* ctx, int n, int h, int w, uint64_t seed);
   yl_status set_inputs(const float* za, const float* zb, int ldz, const float* t_dev);
   yl_status forward();
   yl_status backward();  // from dpred
 };
 
-yl_status frames_to_nhwc4(yl_ctx* ctx, const float* nchw3, int n, int h, int w, float* out);
+yl_status frames_to_nhwc4(yl_ctx* ctx, const float* nchw3, int n, int h, int w, float* out,
+                          int round);
 yl_status copy_mu(yl_ctx* ctx, const Act& e, float* dst, int c);
 
 }  // namespace yl

@@ -4,6 +4,7 @@
 // GpuSession begin/commit/end recording (GpuTraining.swift:4-151) and
 // GPUTensor (GPUTensor.swift:9-143).  Waits are bounded and return
 // YL_ERR_TIMEOUT where the reference calls exit(70).
+#include <atomic>
 #include <cstdio>
 #include <cstring>
 #include <string>
@@ -25,7 +26,10 @@ yl_status set_error(yl_status st, const char* fmt, ...) {
   return st;
 }
 
+static std::atomic<unsigned long long> g_launches{0};
+
 yl_status check_launch(const char* what) {
+  g_launches.fetch_add(1, std::memory_order_relaxed);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess)
     return set_error(YL_ERR_CUDA, "launch of %s failed: %s", what, cudaGetErrorString(e));
@@ -58,6 +62,8 @@ extern "C" {
 const char* yl_last_error_message(void) { return t_last_error.c_str(); }
 
 const char* yl_version(void) { return "yumelayers_b200 0.1 (sm_100a, tcgen05/TMA)"; }
+
+unsigned long long yl_kernel_launch_count(void) { return g_launches.load(); }
 
 yl_status yl_ctx_create(int device, yl_ctx** out) {
   YL_CHECK(out != nullptr, YL_ERR_INVALID, "yl_ctx_create: out is NULL");

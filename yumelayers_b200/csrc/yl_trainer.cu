@@ -248,17 +248,19 @@ yl_status yl_trainer_step(yl_trainer* tr, const float* frames, const float* t, f
   vae.profiling = unet.profiling = tr->cfg.profile != 0;
   YL_CUDA(cudaMemsetAsync(tr->losses, 0, 2 * sizeof(float), ctx->stream));
   if (train_motion) {  // endpoints: encoder means of frames 0 and 16, no gradient
-    YL_TRY(frames_to_nhwc4(ctx, frames, B, H, W, vae.x_in.p));
+    YL_TRY(frames_to_nhwc4(ctx, frames, B, H, W, vae.x_in.p, 1));
     YL_TRY(vae.encode());
     YL_TRY(copy_mu(ctx, vae.e, tr->za, VAE::kLatent));
-    YL_TRY(frames_to_nhwc4(ctx, frames + set, B, H, W, vae.x_in.p));
+    YL_TRY(frames_to_nhwc4(ctx, frames + set, B, H, W, vae.x_in.p, 1));
     YL_TRY(vae.encode());
     YL_TRY(copy_mu(ctx, vae.e, tr->zb, VAE::kLatent));
   }
-  YL_TRY(frames_to_nhwc4(ctx, frames + 2 * set, B, H, W, vae.x_in.p));
+  YL_TRY(frames_to_nhwc4(ctx, frames + 2 * set, B, H, W, vae.x_in.p, 1));
   if (train_vae) {
+    // the reconstruction target keeps the frame's fp32 values
+    YL_TRY(frames_to_nhwc4(ctx, frames + 2 * set, B, H, W, vae.x_tgt.p, 0));
     YL_TRY(vae.forward_train(tr->step));
-    YL_TRY(l1_kl_head(ctx, vae.recon.p, vae.x_in.p, vae.recon.pixels(), 4, 3, vae.e.p, vae.e.ld,
+    YL_TRY(l1_kl_head(ctx, vae.recon.p, vae.x_tgt.p, vae.recon.pixels(), 4, 3, vae.e.p, vae.e.ld,
                       vae.e.pixels(), VAE::kLatent, tr->cfg.beta_kl, vae.drecon.p, tr->losses));
     if (train_motion) YL_TRY(copy_mu(ctx, vae.e, unet.target.p, VAE::kLatent));
     YL_TRY(vae.backward(tr->step, tr->cfg.beta_kl));

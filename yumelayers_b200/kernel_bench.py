@@ -1,0 +1,69 @@
+"""Per-kernel timing of the conv and GroupNorm kernels on the workload's layer
+shapes (the B200 counterpart of the reference's profileConv, Diagnostics.swift:
+124-201).  Prints one JSON line per shape.
+
+    python -m yumelayers_b200.kernel_bench [--shapes vae|small] [--reps R] [--only NAME]
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes as C
+import json
+import sys
+
+from ._lib import ConvProfile, call
+from .session import Context
+
+# (name, n, c, h, w, oc, k, stride, up): the distinct conv shapes of one batch-8
+# VAE step at 480x856 (up = 1: the input is the half-resolution source).
+VAE_SHAPES = [
+    ("full_128_128", 8, 128, 480, 856, 128, 3, 1, 0),
+    ("full_in_4_128", 8, 4, 480, 856, 128, 3, 1, 0),
+    ("full_out_128_4", 8, 128, 480, 856, 4, 3, 1, 0),
+    ("down1_128_s2", 8, 128, 480, 856, 128, 3, 2, 0),
+    ("half_128_256", 8, 128, 240, 428, 256, 3, 1, 0),
+    ("half_256_256", 8, 256, 240, 428, 256, 3, 1, 0),
+    ("half_skip_128_256", 8, 128, 240, 428, 256, 1, 1, 0),
+    ("quarter_256_256", 8, 256, 120, 214, 256, 3, 1, 0),
+    ("up3_256_128", 8, 256, 240, 428, 128, 3, 1, 1),
+    ("up2_256_256", 8, 256, 120, 214, 256, 3, 1, 1),
+]
+SMALL_SHAPES = [
+    ("small_128_128", 8, 128, 192, 192, 128, 3, 1, 0),
+]
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--shapes", default="vae", choices=["vae", "small"])
+    ap.add_argument("--reps", type=int, default=5)
+    ap.add_argument("--only", default=None)
+    ap.add_argument("--groupnorm", action="store_true")
+    a = ap.parse_args(argv)
+    ctx = Context.shared(0)
+    shapes = VAE_SHAPES if a.shapes == "vae" else SMALL_SHAPES
+    for name, n, c, h, w, oc, k, s, up in shapes:
+        if a.only and a.only != name:
+            continue
+        p = ConvProfile()
+        call("yl_profile_conv", ctx.handle, n, c, h, w, oc, k, s, up, a.reps, C.byref(p))
+        row = {"shape": name, "n": n, "c": c, "h": h, "w": w, "oc": oc, "k": k, "stride": s,
+               "up": up, "gflop": p.flops / 1e9, "wgrad_splits": p.wgrad_splits}
+        for m in ("fprop", "dgrad", "wgrad"):
+            ms = getattr(p, m + "_ms")
+            row[m + "_ms"] = round(ms, 4)
+            row[m + "_tflops"] = round(p.flops / (ms * 1e-3) / 1e12, 1)
+        print(json.dumps(row), flush=True)
+    if a.groupnorm:
+        for (n, c, h, w) in [(8, 128, 480, 856), (8, 256, 240, 428)]:
+            f, b = C.c_double(), C.c_double()
+            call("yl_profile_groupnorm", ctx.handle, n, c, h, w, a.reps, C.byref(f), C.byref(b))
+            e = n * c * h * w * 4
+            print(json.dumps({"groupnorm": [n, c, h, w], "fwd_ms": f.value, "bwd_ms": b.value,
+                              "fwd_gbs": 3 * e / (f.value * 1e-3) / 1e9,
+                              "bwd_gbs": 5 * e / (b.value * 1e-3) / 1e9}), flush=True)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())
