@@ -33,6 +33,13 @@ CASES = [
     ("c256", 1, 256, 256, 16, 18, 3, 1, 1, False, None),
     ("c128_to_384", 1, 128, 384, 15, 27, 3, 1, 1, False, None),
     ("s2_c128", 2, 128, 128, 30, 54, 3, 2, 1, False, None),
+    # TMA phase-view paths: upsample + conv as four 2x2 phase convs, stride-2
+    # via input phase views / output phases, odd extents, and a cropped upsample
+    ("up_c128", 2, 128, 128, 10, 12, 3, 1, 1, True, None),
+    ("up_c256_128", 1, 256, 128, 8, 14, 3, 1, 1, True, None),
+    ("up_crop_c128", 1, 128, 128, 8, 9, 3, 1, 1, True, (15, 17)),
+    ("s2_odd_c128_256", 1, 128, 256, 15, 17, 3, 2, 1, False, None),
+    ("c256_to_128", 1, 256, 128, 30, 54, 3, 1, 1, False, None),
 ]
 
 

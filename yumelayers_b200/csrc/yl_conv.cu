@@ -30,28 +30,9 @@
 #include <algorithm>
 #include <mutex>
 
-#include "yl_kernels.h"
-#include "yl_ptx.cuh"
+#include "yl_conv_common.cuh"
 
 namespace yl {
-
-constexpr int kBM = 128;         // GEMM rows per CTA (UMMA M)
-constexpr int kBK = 32;          // k per stage: 32 fp32 = one 128-byte swizzle row
-constexpr int kThreads = 192;    // 4 gather/epilogue warps + TMA warp + MMA warp
-constexpr int kATileBytes = kBM * 128;
-
-template <int BN>
-struct TileCfg {
-  static constexpr int kBTileBytes = BN * 128;
-  static constexpr int kStageBytes = kATileBytes + kBTileBytes;
-  static constexpr int kStages = (196 * 1024) / kStageBytes > 8 ? 8 : (196 * 1024) / kStageBytes;
-  static constexpr int kTmemCols = BN < 32 ? 32 : BN;
-  static constexpr int kSmemBytes = kStages * kStageBytes + (2 * kStages + 2) * 8 + 1024;
-};
-
-__device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
-  return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
-}
 
 // ------------------------------------------------------------------ fprop / dgrad
 template <int BN>
@@ -441,416 +422,7 @@ __global__ void __launch_bounds__(kThreads, 1) conv_wgrad_kernel(WgradArgs w, in
   }
 }
 
-// ------------------------------------------------------------------ TMA paths
-// Stride-1, non-upsampled convolutions with >= 32-channel chunks: every
-// operand tile is a rectangular box of an NHWC tensor, so one thread issues
-// 4-D TMA loads (out-of-range rows/columns read as zero = the padding) and
-// the gather warps have nothing to do in the mainloop.
-struct TmaConv {
-  int mode;          // MODE_FPROP or MODE_DGRAD (stride 1)
-  int ksize, pad;
-  int cpt;           // 32-channel chunks per tap
-  int nk;            // k-blocks = ksize^2 * cpt
-  int oh, ow, n_img;
-  int tiles_x, tiles_y;  // ceil(ow / 32), ceil(oh / 4)
-};
-
-// Output tile: 4 rows x 32 pixels of one image (128 GEMM rows, row = 32*dy + dx).
-template <int BN>
-__global__ void __launch_bounds__(kThreads, 1)
-    conv_gemm_tma_kernel(const __grid_constant__ CUtensorMap tmap_a,
-                         const __grid_constant__ CUtensorMap tmap_w, TmaConv p, ConvEpilogue e,
-                         int* err) {
-  using Cfg = TileCfg<BN>;
-  constexpr int S = Cfg::kStages;
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = align1024(smem_raw);
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * Cfg::kStageBytes);
-  uint64_t* empty = full + S;
-  uint64_t* accum = empty + S;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
-
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int tx = blockIdx.x % p.tiles_x;
-  const int trest = blockIdx.x / p.tiles_x;
-  const int ty = trest % p.tiles_y;
-  const int img = trest / p.tiles_y;
-  const int ox0 = tx * 32, oy0 = ty * 4, n0 = blockIdx.y * BN;
-
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < S; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1);
-    }
-    mbar_init(accum, 1);
-    fence_barrier_init();
-  }
-  if (warp == 5) {
-    tmem_alloc(tmem_slot, Cfg::kTmemCols);
-    tmem_relinquish();
-  }
-  if (warp == 4 && lane == 0) {
-    tma_prefetch_desc(&tmap_a);
-    tma_prefetch_desc(&tmap_w);
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
-
-  if (warp == 4) {
-    if (lane == 0) {
-      int tap = 0, chunk = 0;
-      for (int kb = 0; kb < p.nk; ++kb) {
-        const int s = kb % S;
-        if (kb >= S && !mbar_wait(&empty[s], ((kb / S) - 1) & 1)) {
-          report_error(err, YL_DEVERR_TIMEOUT);
-          break;
-        }
-        const int ky = tap / p.ksize, kx = tap - ky * p.ksize;
-        int cx, cy;
-        if (p.mode == MODE_FPROP) {
-          cx = ox0 + kx - p.pad;
-          cy = oy0 + ky - p.pad;
-        } else {
-          cx = ox0 + p.pad - kx;
-          cy = oy0 + p.pad - ky;
-        }
-        const uint32_t a_dst = smem_u32(smem + s * Cfg::kStageBytes);
-        mbar_arrive_expect_tx(&full[s], kATileBytes + Cfg::kBTileBytes);
-        tma_load_4d(a_dst, &tmap_a, &full[s], chunk * 32, cx, cy, img);
-        tma_load_2d(a_dst + kATileBytes, &tmap_w, &full[s], kb * kBK, n0);
-        if (++chunk == p.cpt) {
-          chunk = 0;
-          ++tap;
-        }
-      }
-    }
-  } else if (warp == 5) {
-    if (lane == 0) {
-      constexpr uint32_t idesc = idesc_tf32(kBM, BN, 0, 0);
-      for (int kb = 0; kb < p.nk; ++kb) {
-        const int s = kb % S;
-        if (!mbar_wait(&full[s], (kb / S) & 1)) {
-          report_error(err, YL_DEVERR_TIMEOUT);
-          break;
-        }
-        tc_fence_after();
-        const uint32_t a_addr = smem_u32(smem + s * Cfg::kStageBytes);
-        const uint32_t b_addr = a_addr + kATileBytes;
-#pragma unroll
-        for (int kk = 0; kk < kBK / 8; ++kk)
-          umma_tf32(tmem, sw128_desc(a_addr + kk * 32, 16, 1024),
-                    sw128_desc(b_addr + kk * 32, 16, 1024), idesc, (kb | kk) != 0);
-        umma_commit(&empty[s]);
-      }
-      umma_commit(accum);
-    }
-  }
-
-  if (warp < 4) {
-    const bool got = mbar_wait(accum, 0);
-    if (!got) report_error(err, YL_DEVERR_TIMEOUT);
-    tc_fence_after();
-    const int oy = oy0 + warp, ox = ox0 + lane;
-    const bool mval = got && oy < p.oh && ox < p.ow;
-    const long long m = ((long long)img * p.oh + oy) * p.ow + ox;
-#pragma unroll 1
-    for (int c0 = 0; c0 < BN; c0 += 32) {
-      if (n0 + c0 >= e.n_total) break;
-      uint32_t r[32];
-      tmem_ld_32x32b_x32(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0, r);
-      tmem_ld_wait();
-      if (!mval) continue;
-      const int nb = n0 + c0;
-      float v[32];
-#pragma unroll
-      for (int q = 0; q < 32; ++q) v[q] = __uint_as_float(r[q]);
-      if (e.bias) {
-#pragma unroll
-        for (int q = 0; q < 32; ++q)
-          if (nb + q < e.n_total) v[q] += __ldg(e.bias + nb + q);
-      }
-      if (e.bias2d) {
-        const float* b2 = e.bias2d + (long long)img * e.n_total + nb;
-#pragma unroll
-        for (int q = 0; q < 32; ++q)
-          if (nb + q < e.n_total) v[q] += __ldg(b2 + q);
-      }
-      const bool full32 = (nb + 32 <= e.n_total);
-      if (e.residual) {
-        const float* rp = e.residual + m * e.ldr + nb;
-        if (full32 && (e.ldr & 3) == 0) {
-#pragma unroll
-          for (int q = 0; q < 32; q += 4) {
-            float4 rv = *reinterpret_cast<const float4*>(rp + q);
-            v[q] += rv.x; v[q + 1] += rv.y; v[q + 2] += rv.z; v[q + 3] += rv.w;
-          }
-        } else {
-#pragma unroll
-          for (int q = 0; q < 32; ++q)
-            if (nb + q < e.n_total) v[q] += rp[q];
-        }
-      }
-      if (e.round_tf32) {
-#pragma unroll
-        for (int q = 0; q < 32; ++q) v[q] = round_tf32(v[q]);
-      }
-      float* op = e.out + m * e.ldo + nb;
-      if (full32 && (e.ldo & 3) == 0) {
-#pragma unroll
-        for (int q = 0; q < 32; q += 4)
-          *reinterpret_cast<float4*>(op + q) = make_float4(v[q], v[q + 1], v[q + 2], v[q + 3]);
-      } else {
-#pragma unroll
-        for (int q = 0; q < 32; ++q)
-          if (nb + q < e.n_total) op[q] = v[q];
-      }
-    }
-  }
-
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 5) {
-    tc_fence_after();
-    tmem_dealloc(tmem, Cfg::kTmemCols);
-  }
-}
-
-// dW over row-aligned 32-pixel k-blocks: A = dy^T (4 atoms of 32 output
-// channels), B = the input shifted by this CTA's tap (BN/32 atoms of 32 input
-// channels); both MN-major, written by TMA in the SWIZZLE_128B_ATOM_32B
-// pattern that tcgen05 requires for MN-major tf32.
-struct TmaWgrad {
-  int ksize, pad, cin;
-  int oh, ow, n_img, xblocks;
-  long long blocks;       // n_img * oh * xblocks
-  long long per_split;    // k-blocks per split
-  int cout, n_total;
-  float* ws;
-  long long ws_split_stride;
-};
-
-template <int BN>
-__global__ void __launch_bounds__(kThreads, 1)
-    conv_wgrad_tma_kernel(const __grid_constant__ CUtensorMap tmap_dy,
-                          const __grid_constant__ CUtensorMap tmap_x, TmaWgrad w, int* err) {
-  using Cfg = TileCfg<BN>;
-  constexpr int S = Cfg::kStages;
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = align1024(smem_raw);
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * Cfg::kStageBytes);
-  uint64_t* empty = full + S;
-  uint64_t* accum = empty + S;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
-
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int m0 = blockIdx.x * kBM, n0 = blockIdx.y * BN;
-  const int tap = n0 / w.cin, ci0 = n0 - tap * w.cin;
-  const int ky = tap / w.ksize, kx = tap - (tap / w.ksize) * w.ksize;
-  const long long b_begin = blockIdx.z * w.per_split;
-  const long long b_end = min(w.blocks, b_begin + w.per_split);
-  const int nk = b_end > b_begin ? (int)(b_end - b_begin) : 0;
-
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < S; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1);
-    }
-    mbar_init(accum, 1);
-    fence_barrier_init();
-  }
-  if (warp == 5) {
-    tmem_alloc(tmem_slot, Cfg::kTmemCols);
-    tmem_relinquish();
-  }
-  if (warp == 4 && lane == 0) {
-    tma_prefetch_desc(&tmap_dy);
-    tma_prefetch_desc(&tmap_x);
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
-
-  if (warp == 4) {
-    if (lane == 0 && nk > 0) {
-      // decompose the first block once, then walk (x block, row, image) incrementally
-      long long b = b_begin;
-      int xb = (int)(b % w.xblocks);
-      long long r = b / w.xblocks;
-      int oy = (int)(r % w.oh);
-      int im = (int)(r / w.oh);
-      for (int kb = 0; kb < nk; ++kb) {
-        const int s = kb % S;
-        if (kb >= S && !mbar_wait(&empty[s], ((kb / S) - 1) & 1)) {
-          report_error(err, YL_DEVERR_TIMEOUT);
-          break;
-        }
-        const uint32_t a_dst = smem_u32(smem + s * Cfg::kStageBytes);
-        const uint32_t b_dst = a_dst + kATileBytes;
-        const int ox0 = xb * 32;
-        mbar_arrive_expect_tx(&full[s], kATileBytes + Cfg::kBTileBytes);
-#pragma unroll
-        for (int a = 0; a < 4; ++a)
-          tma_load_4d(a_dst + a * 4096, &tmap_dy, &full[s], m0 + 32 * a, ox0, oy, im);
-#pragma unroll
-        for (int a = 0; a < BN / 32; ++a)
-          tma_load_4d(b_dst + a * 4096, &tmap_x, &full[s], ci0 + 32 * a, ox0 + kx - w.pad,
-                      oy + ky - w.pad, im);
-        if (++xb == w.xblocks) {
-          xb = 0;
-          if (++oy == w.oh) {
-            oy = 0;
-            ++im;
-          }
-        }
-      }
-    }
-  } else if (warp == 5) {
-    if (lane == 0) {
-      constexpr uint32_t idesc = idesc_tf32(kBM, BN, 1, 1);
-      for (int kb = 0; kb < nk; ++kb) {
-        const int s = kb % S;
-        if (!mbar_wait(&full[s], (kb / S) & 1)) {
-          report_error(err, YL_DEVERR_TIMEOUT);
-          break;
-        }
-        tc_fence_after();
-        const uint32_t a_addr = smem_u32(smem + s * Cfg::kStageBytes);
-        const uint32_t b_addr = a_addr + kATileBytes;
-#pragma unroll
-        for (int kk = 0; kk < kBK / 8; ++kk)
-          umma_tf32(tmem, sw128b32_desc(a_addr + kk * 1024, 4096, 512),
-                    sw128b32_desc(b_addr + kk * 1024, 4096, 512), idesc, (kb | kk) != 0);
-        umma_commit(&empty[s]);
-      }
-      umma_commit(accum);
-    }
-  }
-
-  if (warp < 4) {
-    const bool got = mbar_wait(accum, 0);
-    if (!got) report_error(err, YL_DEVERR_TIMEOUT);
-    tc_fence_after();
-    const int co = m0 + warp * 32 + lane;
-    const bool rval = got && co < w.cout;
-    float* dst = w.ws + (long long)blockIdx.z * w.ws_split_stride + (long long)co * w.n_total;
-#pragma unroll 1
-    for (int c0 = 0; c0 < BN; c0 += 32) {
-      if (n0 + c0 >= w.n_total) break;
-      uint32_t r[32];
-      tmem_ld_32x32b_x32(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0, r);
-      tmem_ld_wait();
-      if (!rval) continue;
-      const int nb = n0 + c0;
-      if (nk == 0) {
-#pragma unroll
-        for (int q = 0; q < 32; ++q) r[q] = 0u;
-      }
-#pragma unroll
-      for (int q = 0; q < 32; q += 4)
-        *reinterpret_cast<float4*>(dst + nb + q) =
-            make_float4(__uint_as_float(r[q]), __uint_as_float(r[q + 1]),
-                        __uint_as_float(r[q + 2]), __uint_as_float(r[q + 3]));
-    }
-  }
-
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 5) {
-    tc_fence_after();
-    tmem_dealloc(tmem, Cfg::kTmemCols);
-  }
-}
-
-// Fixed-order sum of split-K partials: out[i] (+)= sum_s ws[s][i].
-__global__ void splitk_reduce_kernel(const float* __restrict__ ws, int splits, long long stride,
-                                     float* __restrict__ out, long long n, int accumulate) {
-  const long long n4 = n >> 2;
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n4;
-       i += (long long)gridDim.x * blockDim.x) {
-    float4 acc = reinterpret_cast<const float4*>(ws)[i];
-    for (int s = 1; s < splits; ++s) {
-      float4 v = reinterpret_cast<const float4*>(ws + s * stride)[i];
-      acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
-    }
-    if (accumulate) {
-      float4 o = reinterpret_cast<float4*>(out)[i];
-      acc.x += o.x; acc.y += o.y; acc.z += o.z; acc.w += o.w;
-    }
-    reinterpret_cast<float4*>(out)[i] = acc;
-  }
-  for (long long i = (n4 << 2) + blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
-       i += (long long)gridDim.x * blockDim.x) {
-    float acc = ws[i];
-    for (int s = 1; s < splits; ++s) acc += ws[s * stride + i];
-    out[i] = accumulate ? out[i] + acc : acc;
-  }
-}
-
 // ------------------------------------------------------------------ host side
-static PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    cudaDriverEntryPointQueryResult q;
-    void* p = nullptr;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
-            cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-  });
-  return fn;
-}
-
-// Tensor map over a row-major fp32 matrix [rows][cols]; box = {32, box_rows},
-// SWIZZLE_128B, out-of-range elements read as zero.
-static yl_status make_weight_tmap(CUtensorMap* tm, const float* w, int rows, int cols,
-                                  int box_rows) {
-  auto fn = get_encode_fn();
-  YL_CHECK(fn, YL_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
-  YL_CHECK((cols & 3) == 0, YL_ERR_SHAPE, "weight row length %d is not a multiple of 4", cols);
-  YL_CHECK(((uintptr_t)w & 15) == 0, YL_ERR_INVALID, "weight pointer not 16-byte aligned");
-  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
-  cuuint64_t strides[1] = {(cuuint64_t)cols * sizeof(float)};
-  cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)box_rows};
-  cuuint32_t estr[2] = {1, 1};
-  CUresult r = fn(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(w), dims, strides,
-                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  YL_CHECK(r == CUDA_SUCCESS, YL_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
-  return YL_OK;
-}
-
-// Tensor map over an NHWC activation {c, w, h, n} with pixel stride ps
-// (floats); box {32 channels, box_w, box_h, 1}; out-of-range reads are zero.
-static yl_status make_act_tmap(CUtensorMap* tm, const float* base, int c, int w, int h, int n,
-                               int ps, int box_w, int box_h, CUtensorMapSwizzle swz) {
-  auto fn = get_encode_fn();
-  YL_CHECK(fn, YL_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
-  YL_CHECK(((uintptr_t)base & 15) == 0 && ps % 4 == 0, YL_ERR_INVALID,
-           "activation tensor map: base/stride alignment");
-  cuuint64_t dims[4] = {(cuuint64_t)c, (cuuint64_t)w, (cuuint64_t)h, (cuuint64_t)n};
-  cuuint64_t strides[3] = {(cuuint64_t)ps * 4, (cuuint64_t)w * ps * 4,
-                           (cuuint64_t)h * w * ps * 4};
-  cuuint32_t box[4] = {32, (cuuint32_t)box_w, (cuuint32_t)box_h, 1};
-  cuuint32_t estr[4] = {1, 1, 1, 1};
-  CUresult r = fn(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, const_cast<float*>(base), dims, strides,
-                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
-                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  YL_CHECK(r == CUDA_SUCCESS, YL_ERR_CUDA, "cuTensorMapEncodeTiled (activation) failed (%d)",
-           (int)r);
-  return YL_OK;
-}
-
-// The source of `g` is a dense NHWC tensor of hv x wv pixels (what the TMA
-// paths need: rectangular boxes, no upsample, stride 1).
-static bool dense_source(const ConvGather& g) {
-  return g.stride == 1 && !g.up && g.row_stride == g.wv * g.ps &&
-         g.img_stride == (long long)g.hv * g.wv * g.ps && ((uintptr_t)g.src & 15) == 0;
-}
-
 static yl_status validate_gather(const ConvGather& g) {
   YL_CHECK(g.src != nullptr, YL_ERR_INVALID, "conv: source is NULL");
   YL_CHECK(g.ps % 4 == 0 && g.cin % 4 == 0 && g.cin <= g.ps, YL_ERR_SHAPE,
@@ -877,46 +449,12 @@ static yl_status launch_gemm(yl_ctx* ctx, const ConvGather& g, const float* w, i
   return check_launch("conv_gemm_kernel");
 }
 
-template <int BN>
-static yl_status launch_gemm_tma(yl_ctx* ctx, const ConvGather& g, const float* w, int n_rows,
-                                 const ConvEpilogue& e) {
-  using Cfg = TileCfg<BN>;
-  CUtensorMap ta, tw;
-  const int n_img = g.m_total / (g.oh * g.ow);
-  YL_TRY(make_act_tmap(&ta, g.src, g.cin, g.wv, g.hv, n_img, g.ps, 32, 4,
-                       CU_TENSOR_MAP_SWIZZLE_128B));
-  YL_TRY(make_weight_tmap(&tw, w, n_rows, g.k_total, BN));
-  TmaConv p;
-  p.mode = g.mode;
-  p.ksize = g.ksize;
-  p.pad = g.pad;
-  p.cpt = g.cin / 32;
-  p.nk = g.ksize * g.ksize * p.cpt;
-  p.oh = g.oh;
-  p.ow = g.ow;
-  p.n_img = n_img;
-  p.tiles_x = (g.ow + 31) / 32;
-  p.tiles_y = (g.oh + 3) / 4;
-  YL_CUDA(cudaFuncSetAttribute(conv_gemm_tma_kernel<BN>,
-                               cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes));
-  dim3 grid(p.tiles_x * p.tiles_y * n_img, (e.n_total + BN - 1) / BN);
-  conv_gemm_tma_kernel<BN><<<grid, kThreads, Cfg::kSmemBytes, ctx->stream>>>(ta, tw, p, e,
-                                                                            ctx->dev_err);
-  return check_launch("conv_gemm_tma_kernel");
-}
-
-yl_status conv_fprop(yl_ctx* ctx, const ConvGather& g, const float* w, int n_rows,
-                     const ConvEpilogue& e) {
+yl_status conv_fprop_gather(yl_ctx* ctx, const ConvGather& g, const float* w, int n_rows,
+                            const ConvEpilogue& e) {
   YL_TRY(validate_gather(g));
   YL_CHECK(e.out && e.n_total > 0 && e.ldo >= e.n_total, YL_ERR_SHAPE, "conv: bad output");
   YL_CHECK(n_rows >= 1, YL_ERR_SHAPE, "conv: no weight rows");
   if (g.m_total == 0) return YL_OK;
-  if (dense_source(g) && g.cin % 32 == 0 && g.m_total % (g.oh * g.ow) == 0) {
-    if (e.n_total <= 32) return launch_gemm_tma<32>(ctx, g, w, n_rows, e);
-    if (e.n_total <= 64) return launch_gemm_tma<64>(ctx, g, w, n_rows, e);
-    if (e.n_total <= 128 || e.n_total % 256 != 0) return launch_gemm_tma<128>(ctx, g, w, n_rows, e);
-    return launch_gemm_tma<256>(ctx, g, w, n_rows, e);
-  }
   if (e.n_total <= 32) return launch_gemm<32>(ctx, g, w, n_rows, e);
   if (e.n_total <= 64) return launch_gemm<64>(ctx, g, w, n_rows, e);
   if (e.n_total <= 128 || e.n_total % 256 != 0) return launch_gemm<128>(ctx, g, w, n_rows, e);
@@ -935,8 +473,9 @@ int conv_wgrad_pick_splits(yl_ctx* ctx, int cout, int k_total, int m_total) {
   return (int)splits;
 }
 
-yl_status conv_wgrad_ws(yl_ctx* ctx, const float* dy, int ldy, int cout, const ConvGather& g,
-                        float* dw, int accumulate, float* ws, int splits) {
+yl_status conv_wgrad_gather(yl_ctx* ctx, const float* dy, int ldy, int cout,
+                            const ConvGather& g, float* dw, int accumulate, float* ws,
+                            int splits) {
   YL_TRY(validate_gather(g));
   YL_CHECK(dy && dw && ws, YL_ERR_INVALID, "wgrad: NULL argument");
   YL_CHECK(ldy % 4 == 0 && cout % 4 == 0 && ldy >= cout, YL_ERR_SHAPE,
@@ -946,39 +485,6 @@ yl_status conv_wgrad_ws(yl_ctx* ctx, const float* dy, int ldy, int cout, const C
   constexpr int BN = 128;
   using Cfg = TileCfg<BN>;
   const int n_total = g.k_total;
-  if (dense_source(g) && g.cin % BN == 0 && g.m_total % (g.oh * g.ow) == 0) {
-    // TMA path: row-aligned 32-pixel k-blocks, one tap per CTA column
-    const int n_img = g.m_total / (g.oh * g.ow);
-    CUtensorMap tdy, tx;
-    YL_TRY(make_act_tmap(&tdy, dy, cout, g.ow, g.oh, n_img, ldy, 32, 1,
-                         CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B));
-    YL_TRY(make_act_tmap(&tx, g.src, g.cin, g.wv, g.hv, n_img, g.ps, 32, 1,
-                         CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B));
-    TmaWgrad t;
-    t.ksize = g.ksize;
-    t.pad = g.pad;
-    t.cin = g.cin;
-    t.oh = g.oh;
-    t.ow = g.ow;
-    t.n_img = n_img;
-    t.xblocks = (g.ow + 31) / 32;
-    t.blocks = (long long)n_img * g.oh * t.xblocks;
-    t.per_split = (t.blocks + splits - 1) / splits;
-    t.cout = cout;
-    t.n_total = n_total;
-    t.ws = ws;
-    t.ws_split_stride = (long long)cout * n_total;
-    YL_CUDA(cudaFuncSetAttribute(conv_wgrad_tma_kernel<BN>,
-                                 cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes));
-    dim3 grid((cout + kBM - 1) / kBM, n_total / BN, splits);
-    conv_wgrad_tma_kernel<BN><<<grid, kThreads, Cfg::kSmemBytes, ctx->stream>>>(tdy, tx, t,
-                                                                             ctx->dev_err);
-    YL_TRY(check_launch("conv_wgrad_tma_kernel"));
-    long long n = (long long)cout * n_total;
-    splitk_reduce_kernel<<<grid_1d(n / 4 + 1, 256), 256, 0, ctx->stream>>>(ws, splits, n, dw, n,
-                                                                           accumulate);
-    return check_launch("splitk_reduce_kernel");
-  }
   long long kblocks = (g.m_total + kBK - 1) / kBK;
   long long per = (kblocks + splits - 1) / splits;
   WgradArgs a;

@@ -1,0 +1,700 @@
+// yl_conv_tma.cu -- convolution through TMA boxes: every operand tile of the
+// implicit GEMM is a rectangular box of an NHWC tensor or of one of its 2x2
+// "phase views" (the sub-lattice of pixels (2i+a, 2j+b), itself a strided
+// 4-D tensor), loaded by one thread with out-of-range reads as zero (= the
+// convolution padding).  A small tap table says which view and which offset
+// each tap reads, so one kernel covers:
+//   * stride-1 conv forward and its dX (the flipped taps),
+//   * stride-2 conv forward (each tap reads one input phase view),
+//   * nearest-x2 upsample + 3x3 conv forward as four output phases, each a
+//     2x2 conv on the source with merged weights (16 MACs per output instead
+//     of 36, no upsampled tensor) -- the decoder's "up + conv",
+//   * stride-2 dX as four output phases with 1, 2, 2 and 4 taps,
+// and one wgrad kernel covers stride-1, stride-2 (input phase views) and
+// upsample-conv (output-gradient phase views) filter gradients.
+// Shapes the tap tables do not cover fall back to the cp.async gathers of
+// yl_conv.cu.
+#include "yl_conv_common.cuh"
+
+namespace yl {
+
+yl_status conv_fprop_gather(yl_ctx* ctx, const ConvGather& g, const float* w, int n_rows,
+                            const ConvEpilogue& e);
+yl_status conv_wgrad_gather(yl_ctx* ctx, const float* dy, int ldy, int cout,
+                            const ConvGather& g, float* dw, int accumulate, float* ws,
+                            int splits);
+
+constexpr int kMaxTaps = 9;
+
+struct TapPhase {
+  int ntaps, w_row0, ya, xa;
+  int8_t map[kMaxTaps], dy[kMaxTaps], dx[kMaxTaps];
+};
+
+struct ConvPlan {
+  int cpt;             // 32-channel chunks per tap
+  int gh, gw;          // tile grid extent (the output phase lattice)
+  int n_img, tiles_x, tiles_y;
+  int out_h, out_w;    // output tensor extent
+  int ys, xs;          // output pixel = (oy * ys + ya, ox * xs + xa)
+  TapPhase ph[4];      // indexed by blockIdx.z
+};
+
+// Output tile: 4 lattice rows x 32 lattice columns (128 GEMM rows).
+template <int BN>
+__global__ void __launch_bounds__(kThreads, 1)
+    conv_tma_fprop_kernel(const __grid_constant__ CUtensorMap ta0,
+                          const __grid_constant__ CUtensorMap ta1,
+                          const __grid_constant__ CUtensorMap ta2,
+                          const __grid_constant__ CUtensorMap ta3,
+                          const __grid_constant__ CUtensorMap tw, ConvPlan p, ConvEpilogue e,
+                          int* err) {
+  using Cfg = TileCfg<BN>;
+  constexpr int S = Cfg::kStages;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align1024(smem_raw);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * Cfg::kStageBytes);
+  uint64_t* empty = full + S;
+  uint64_t* accum = empty + S;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tx = blockIdx.x % p.tiles_x;
+  const int trest = blockIdx.x / p.tiles_x;
+  const int ty = trest % p.tiles_y;
+  const int img = trest / p.tiles_y;
+  const int ox0 = tx * 32, oy0 = ty * 4, n0 = blockIdx.y * BN;
+  const TapPhase& ph = p.ph[blockIdx.z];
+  const int nk = ph.ntaps * p.cpt;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(accum, 1);
+    fence_barrier_init();
+  }
+  if (warp == 5) {
+    tmem_alloc(tmem_slot, Cfg::kTmemCols);
+    tmem_relinquish();
+  }
+  if (warp == 4 && lane == 0) {
+    tma_prefetch_desc(&ta0);
+    tma_prefetch_desc(&tw);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 4) {
+    if (lane == 0) {
+      const CUtensorMap* maps[4] = {&ta0, &ta1, &ta2, &ta3};
+      int t = 0, chunk = 0;
+      for (int kb = 0; kb < nk; ++kb) {
+        const int s = kb % S;
+        if (kb >= S && !mbar_wait(&empty[s], ((kb / S) - 1) & 1)) {
+          report_error(err, YL_DEVERR_TIMEOUT);
+          break;
+        }
+        const uint32_t a_dst = smem_u32(smem + s * Cfg::kStageBytes);
+        mbar_arrive_expect_tx(&full[s], kATileBytes + Cfg::kBTileBytes);
+        tma_load_4d(a_dst, maps[ph.map[t]], &full[s], chunk * 32, ox0 + ph.dx[t], oy0 + ph.dy[t],
+                    img);
+        tma_load_2d(a_dst + kATileBytes, &tw, &full[s], kb * kBK, ph.w_row0 + n0);
+        if (++chunk == p.cpt) {
+          chunk = 0;
+          ++t;
+        }
+      }
+    }
+  } else if (warp == 5) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_tf32(kBM, BN, 0, 0);
+      for (int kb = 0; kb < nk; ++kb) {
+        const int s = kb % S;
+        if (!mbar_wait(&full[s], (kb / S) & 1)) {
+          report_error(err, YL_DEVERR_TIMEOUT);
+          break;
+        }
+        tc_fence_after();
+        const uint32_t a_addr = smem_u32(smem + s * Cfg::kStageBytes);
+        const uint32_t b_addr = a_addr + kATileBytes;
+#pragma unroll
+        for (int kk = 0; kk < kBK / 8; ++kk)
+          umma_tf32(tmem, sw128_desc(a_addr + kk * 32, 16, 1024),
+                    sw128_desc(b_addr + kk * 32, 16, 1024), idesc, (kb | kk) != 0);
+        umma_commit(&empty[s]);
+      }
+      umma_commit(accum);
+    }
+  }
+
+  if (warp < 4) {
+    const bool got = mbar_wait(accum, 0);
+    if (!got) report_error(err, YL_DEVERR_TIMEOUT);
+    tc_fence_after();
+    const int gy = oy0 + warp, gx = ox0 + lane;
+    const int Y = gy * p.ys + ph.ya, X = gx * p.xs + ph.xa;
+    const bool mval = got && gy < p.gh && gx < p.gw && Y < p.out_h && X < p.out_w;
+    const long long m = ((long long)img * p.out_h + Y) * p.out_w + X;
+#pragma unroll 1
+    for (int c0 = 0; c0 < BN; c0 += 32) {
+      if (n0 + c0 >= e.n_total) break;
+      uint32_t r[32];
+      tmem_ld_32x32b_x32(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0, r);
+      tmem_ld_wait();
+      if (!mval) continue;
+      const int nb = n0 + c0;
+      float v[32];
+#pragma unroll
+      for (int q = 0; q < 32; ++q) v[q] = __uint_as_float(r[q]);
+      if (e.bias) {
+#pragma unroll
+        for (int q = 0; q < 32; ++q)
+          if (nb + q < e.n_total) v[q] += __ldg(e.bias + nb + q);
+      }
+      if (e.bias2d) {
+        const float* b2 = e.bias2d + (long long)img * e.n_total + nb;
+#pragma unroll
+        for (int q = 0; q < 32; ++q)
+          if (nb + q < e.n_total) v[q] += __ldg(b2 + q);
+      }
+      const bool full32 = (nb + 32 <= e.n_total);
+      if (e.residual) {
+        const float* rp = e.residual + m * e.ldr + nb;
+        if (full32 && (e.ldr & 3) == 0) {
+#pragma unroll
+          for (int q = 0; q < 32; q += 4) {
+            float4 rv = *reinterpret_cast<const float4*>(rp + q);
+            v[q] += rv.x; v[q + 1] += rv.y; v[q + 2] += rv.z; v[q + 3] += rv.w;
+          }
+        } else {
+#pragma unroll
+          for (int q = 0; q < 32; ++q)
+            if (nb + q < e.n_total) v[q] += rp[q];
+        }
+      }
+      if (e.round_tf32) {
+#pragma unroll
+        for (int q = 0; q < 32; ++q) v[q] = round_tf32(v[q]);
+      }
+      float* op = e.out + m * e.ldo + nb;
+      if (full32 && (e.ldo & 3) == 0) {
+#pragma unroll
+        for (int q = 0; q < 32; q += 4)
+          *reinterpret_cast<float4*>(op + q) = make_float4(v[q], v[q + 1], v[q + 2], v[q + 3]);
+      } else {
+#pragma unroll
+        for (int q = 0; q < 32; ++q)
+          if (nb + q < e.n_total) op[q] = v[q];
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    tc_fence_after();
+    tmem_dealloc(tmem, Cfg::kTmemCols);
+  }
+}
+
+// ------------------------------------------------------------------ wgrad
+enum WgradMode : int { WG_PLAIN = 0, WG_STRIDE2 = 1, WG_UP = 2 };
+
+struct WgradPlan {
+  int mode, nkp;          // k-phases: 1, or 4 (the dy phase views of an upsample conv)
+  int gh, gw, xblocks;    // iteration lattice of one k-phase
+  int n_img;
+  long long blocks_per_kp, blocks, per_split;
+  int ksize, pad, cin, cout, n_total;
+  float* ws;
+  long long ws_split_stride;
+};
+
+// A = dy^T (4 atoms of 32 output channels), B = the input tile this CTA's tap
+// reads (BN/32 atoms of 32 input channels); k-blocks are 32 lattice columns of
+// one lattice row.  Both operands MN-major in SWIZZLE_128B_ATOM_32B.
+template <int BN>
+__global__ void __launch_bounds__(kThreads, 1)
+    conv_tma_wgrad_kernel(const __grid_constant__ CUtensorMap ta0,
+                          const __grid_constant__ CUtensorMap ta1,
+                          const __grid_constant__ CUtensorMap ta2,
+                          const __grid_constant__ CUtensorMap ta3,
+                          const __grid_constant__ CUtensorMap tb0,
+                          const __grid_constant__ CUtensorMap tb1,
+                          const __grid_constant__ CUtensorMap tb2,
+                          const __grid_constant__ CUtensorMap tb3, WgradPlan w, int* err) {
+  using Cfg = TileCfg<BN>;
+  constexpr int S = Cfg::kStages;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align1024(smem_raw);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * Cfg::kStageBytes);
+  uint64_t* empty = full + S;
+  uint64_t* accum = empty + S;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int m0 = blockIdx.x * kBM, n0 = blockIdx.y * BN;
+  const int tap = n0 / w.cin, ci0 = n0 - tap * w.cin;
+  const int ky = tap / w.ksize, kx = tap - (tap / w.ksize) * w.ksize;
+  const long long b_begin = blockIdx.z * w.per_split;
+  const long long b_end = min(w.blocks, b_begin + w.per_split);
+  const int nk = b_end > b_begin ? (int)(b_end - b_begin) : 0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(accum, 1);
+    fence_barrier_init();
+  }
+  if (warp == 5) {
+    tmem_alloc(tmem_slot, Cfg::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 4) {
+    if (lane == 0 && nk > 0) {
+      const CUtensorMap* amaps[4] = {&ta0, &ta1, &ta2, &ta3};
+      const CUtensorMap* bmaps[4] = {&tb0, &tb1, &tb2, &tb3};
+      long long b = b_begin;
+      int kp = (int)(b / w.blocks_per_kp);
+      long long r = b - (long long)kp * w.blocks_per_kp;
+      int xb = (int)(r % w.xblocks);
+      r /= w.xblocks;
+      int gy = (int)(r % w.gh);
+      int im = (int)(r / w.gh);
+      for (int kb = 0; kb < nk; ++kb) {
+        const int s = kb % S;
+        if (kb >= S && !mbar_wait(&empty[s], ((kb / S) - 1) & 1)) {
+          report_error(err, YL_DEVERR_TIMEOUT);
+          break;
+        }
+        // which views and offsets this k-block reads
+        int amap = 0, bmap = 0, by, bx;
+        if (w.mode == WG_PLAIN) {
+          by = ky - w.pad;
+          bx = kx - w.pad;
+        } else if (w.mode == WG_STRIDE2) {
+          const int ry = ky - w.pad, rx = kx - w.pad;
+          bmap = ((ry & 1) << 1) | (rx & 1);
+          by = ry >> 1;
+          bx = rx >> 1;
+        } else {  // WG_UP: k-phase kp = (a, b) of the output gradient
+          const int a = kp >> 1, bb = kp & 1;
+          amap = kp;
+          by = (a + ky - w.pad) >> 1;
+          bx = (bb + kx - w.pad) >> 1;
+        }
+        const uint32_t a_dst = smem_u32(smem + s * Cfg::kStageBytes);
+        const uint32_t b_dst = a_dst + kATileBytes;
+        const int gx0 = xb * 32;
+        mbar_arrive_expect_tx(&full[s], kATileBytes + Cfg::kBTileBytes);
+#pragma unroll
+        for (int a = 0; a < 4; ++a)
+          tma_load_4d(a_dst + a * 4096, amaps[amap], &full[s], m0 + 32 * a, gx0, gy, im);
+#pragma unroll
+        for (int a = 0; a < BN / 32; ++a)
+          tma_load_4d(b_dst + a * 4096, bmaps[bmap], &full[s], ci0 + 32 * a, gx0 + bx, gy + by,
+                      im);
+        if (++xb == w.xblocks) {
+          xb = 0;
+          if (++gy == w.gh) {
+            gy = 0;
+            if (++im == w.n_img) {
+              im = 0;
+              ++kp;
+            }
+          }
+        }
+      }
+    }
+  } else if (warp == 5) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_tf32(kBM, BN, 1, 1);
+      for (int kb = 0; kb < nk; ++kb) {
+        const int s = kb % S;
+        if (!mbar_wait(&full[s], (kb / S) & 1)) {
+          report_error(err, YL_DEVERR_TIMEOUT);
+          break;
+        }
+        tc_fence_after();
+        const uint32_t a_addr = smem_u32(smem + s * Cfg::kStageBytes);
+        const uint32_t b_addr = a_addr + kATileBytes;
+#pragma unroll
+        for (int kk = 0; kk < kBK / 8; ++kk)
+          umma_tf32(tmem, sw128b32_desc(a_addr + kk * 1024, 4096, 512),
+                    sw128b32_desc(b_addr + kk * 1024, 4096, 512), idesc, (kb | kk) != 0);
+        umma_commit(&empty[s]);
+      }
+      umma_commit(accum);
+    }
+  }
+
+  if (warp < 4) {
+    const bool got = mbar_wait(accum, 0);
+    if (!got) report_error(err, YL_DEVERR_TIMEOUT);
+    tc_fence_after();
+    const int co = m0 + warp * 32 + lane;
+    const bool rval = got && co < w.cout;
+    float* dst = w.ws + (long long)blockIdx.z * w.ws_split_stride + (long long)co * w.n_total;
+#pragma unroll 1
+    for (int c0 = 0; c0 < BN; c0 += 32) {
+      if (n0 + c0 >= w.n_total) break;
+      uint32_t r[32];
+      tmem_ld_32x32b_x32(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0, r);
+      tmem_ld_wait();
+      if (!rval) continue;
+      const int nb = n0 + c0;
+      if (nk == 0) {
+#pragma unroll
+        for (int q = 0; q < 32; ++q) r[q] = 0u;
+      }
+#pragma unroll
+      for (int q = 0; q < 32; q += 4)
+        *reinterpret_cast<float4*>(dst + nb + q) =
+            make_float4(__uint_as_float(r[q]), __uint_as_float(r[q + 1]),
+                        __uint_as_float(r[q + 2]), __uint_as_float(r[q + 3]));
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    tc_fence_after();
+    tmem_dealloc(tmem, Cfg::kTmemCols);
+  }
+}
+
+// ------------------------------------------------------------------ weight transforms
+// Row taps of output phase a for nearest-x2 upsample + 3x3 conv (pad 1):
+// phase a = 0 reads source rows i-1 (kernel row 0) and i (rows 1, 2);
+// phase a = 1 reads rows i (kernel rows 0, 1) and i+1 (row 2).
+__device__ __forceinline__ bool up_row_in(int a, int t, int k) {
+  return a == 0 ? (t == 0 ? k == 0 : k >= 1) : (t == 0 ? k <= 1 : k == 2);
+}
+// out[ph][co][t][ci] = sum of w[co][ky*3+kx][ci] over the kernel taps phase
+// ph = (a, b) merges into its tap t = (ty, tx); rounded to tf32.
+__global__ void up_merge_weights_kernel(const float* __restrict__ w, float* __restrict__ out,
+                                        int rows, int cin) {
+  const long long n = 4LL * rows * 4 * cin;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int ci = (int)(i % cin);
+    long long r = i / cin;
+    const int t = (int)(r % 4);
+    r /= 4;
+    const int co = (int)(r % rows);
+    const int ph = (int)(r / rows);
+    const int a = ph >> 1, b = ph & 1, ty = t >> 1, tx = t & 1;
+    float s = 0.f;
+    for (int ky = 0; ky < 3; ++ky) {
+      if (!up_row_in(a, ty, ky)) continue;
+      for (int kx = 0; kx < 3; ++kx)
+        if (up_row_in(b, tx, kx)) s += w[((long long)co * 9 + ky * 3 + kx) * cin + ci];
+    }
+    out[i] = round_tf32(s);
+  }
+}
+
+// Stride-2 (pad 1) dX, output phase a: kernel rows with (a + 1 - ky) even.
+// a = 0: {ky 1 (dy row offset 0)}; a = 1: {ky 0 (offset +1), ky 2 (offset 0)}.
+__device__ __forceinline__ int s2_rows(int a, int* ks, int* offs) {
+  if (a == 0) {
+    ks[0] = 1;
+    offs[0] = 0;
+    return 1;
+  }
+  ks[0] = 0;
+  offs[0] = 1;
+  ks[1] = 2;
+  offs[1] = 0;
+  return 2;
+}
+// out[ph][ci][t][co] = wd[ci][tap(ph, t)][co] (wd is the dgrad weight [ci][9][co]).
+__global__ void s2_phase_weights_kernel(const float* __restrict__ wd, float* __restrict__ out,
+                                        int rows, int cout) {
+  const long long n = 4LL * rows * 4 * cout;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int co = (int)(i % cout);
+    long long r = i / cout;
+    const int t = (int)(r % 4);
+    r /= 4;
+    const int ci = (int)(r % rows);
+    const int ph = (int)(r / rows);
+    int kr[2], orr[2], kc[2], oc[2];
+    const int nr = s2_rows(ph >> 1, kr, orr), nc = s2_rows(ph & 1, kc, oc);
+    float v = 0.f;
+    if (t < nr * nc) {
+      const int ky = kr[t / nc], kx = kc[t % nc];
+      v = wd[((long long)ci * 9 + ky * 3 + kx) * cout + co];
+    }
+    out[i] = v;
+  }
+}
+
+// ------------------------------------------------------------------ host side
+struct View {
+  const float* base;
+  int c, w, h, n;
+  long long sx, sy, sn;  // strides in floats
+};
+
+static View plain_view(const float* p, int c, int w, int h, int n, int ps) {
+  return View{p, c, w, h, n, ps, (long long)w * ps, (long long)h * w * ps};
+}
+// Pixels (2i + a, 2j + b) of a w x h NHWC tensor as their own tensor.
+static View phase_view(const float* p, int c, int w, int h, int n, int ps, int a, int b) {
+  return View{p + ((long long)a * w + b) * ps, c, (w - b + 1) / 2, (h - a + 1) / 2, n,
+              2LL * ps, 2LL * w * ps, (long long)h * w * ps};
+}
+
+static yl_status make_view_tmap(CUtensorMap* tm, const View& v, int box_w, int box_h,
+                                CUtensorMapSwizzle swz) {
+  auto fn = get_encode_fn();
+  YL_CHECK(fn, YL_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
+  YL_CHECK(((uintptr_t)v.base & 15) == 0 && v.sx % 4 == 0 && v.w >= 1 && v.h >= 1, YL_ERR_INVALID,
+           "view tensor map: alignment / extent");
+  cuuint64_t dims[4] = {(cuuint64_t)v.c, (cuuint64_t)v.w, (cuuint64_t)v.h, (cuuint64_t)v.n};
+  cuuint64_t strides[3] = {(cuuint64_t)v.sx * 4, (cuuint64_t)v.sy * 4, (cuuint64_t)v.sn * 4};
+  cuuint32_t box[4] = {32, (cuuint32_t)box_w, (cuuint32_t)box_h, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = fn(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, const_cast<float*>(v.base), dims,
+                  strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  YL_CHECK(r == CUDA_SUCCESS, YL_ERR_CUDA, "cuTensorMapEncodeTiled (view) failed (%d)", (int)r);
+  return YL_OK;
+}
+
+template <int BN>
+static yl_status launch_plan(yl_ctx* ctx, const View* views, int nviews, const float* w, int w_rows,
+                             int w_cols, ConvPlan& p, int nphase, const ConvEpilogue& e) {
+  using Cfg = TileCfg<BN>;
+  CUtensorMap ta[4], tw;
+  for (int i = 0; i < 4; ++i)
+    YL_TRY(make_view_tmap(&ta[i], views[i < nviews ? i : 0], 32, 4, CU_TENSOR_MAP_SWIZZLE_128B));
+  YL_TRY(make_weight_tmap(&tw, w, w_rows, w_cols, BN));
+  p.tiles_x = (p.gw + 31) / 32;
+  p.tiles_y = (p.gh + 3) / 4;
+  YL_CUDA(cudaFuncSetAttribute(conv_tma_fprop_kernel<BN>,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes));
+  dim3 grid(p.tiles_x * p.tiles_y * p.n_img, (e.n_total + BN - 1) / BN, nphase);
+  conv_tma_fprop_kernel<BN><<<grid, kThreads, Cfg::kSmemBytes, ctx->stream>>>(
+      ta[0], ta[1], ta[2], ta[3], tw, p, e, ctx->dev_err);
+  return check_launch("conv_tma_fprop_kernel");
+}
+
+static yl_status run_plan(yl_ctx* ctx, const View* views, int nviews, const float* w, int w_rows,
+                          int w_cols, ConvPlan& p, int nphase, const ConvEpilogue& e) {
+  if (e.n_total <= 32) return launch_plan<32>(ctx, views, nviews, w, w_rows, w_cols, p, nphase, e);
+  if (e.n_total <= 64) return launch_plan<64>(ctx, views, nviews, w, w_rows, w_cols, p, nphase, e);
+  if (e.n_total <= 128 || e.n_total % 256 != 0)
+    return launch_plan<128>(ctx, views, nviews, w, w_rows, w_cols, p, nphase, e);
+  return launch_plan<256>(ctx, views, nviews, w, w_rows, w_cols, p, nphase, e);
+}
+
+// Source extent of a gather (the physical tensor the gather reads).
+static bool source_dims(const ConvGather& g, int* sw, int* sh) {
+  if (g.ps <= 0 || g.row_stride % g.ps != 0 || g.row_stride == 0) return false;
+  *sw = g.row_stride / g.ps;
+  if (g.img_stride % g.row_stride != 0) return false;
+  *sh = (int)(g.img_stride / g.row_stride);
+  return true;
+}
+
+yl_status conv_fprop(yl_ctx* ctx, const ConvGather& g, const float* w, int n_rows,
+                     const ConvEpilogue& e) {
+  int sw = 0, sh = 0;
+  const bool tma_ok = g.cin % 32 == 0 && g.m_total > 0 && g.m_total % (g.oh * g.ow) == 0 &&
+                      ((uintptr_t)g.src & 15) == 0 && g.ps % 4 == 0 && source_dims(g, &sw, &sh) &&
+                      e.n_total > 0 && e.ldo >= e.n_total;
+  if (!tma_ok) return conv_fprop_gather(ctx, g, w, n_rows, e);
+  const int n_img = g.m_total / (g.oh * g.ow);
+  ConvPlan p{};
+  p.cpt = g.cin / 32;
+  p.n_img = n_img;
+  const bool k3p1 = g.ksize == 3 && g.pad == 1;
+  if (g.mode == MODE_FPROP && g.stride == 1 && !g.up && sw == g.wv && sh == g.hv) {
+    // plain stride-1 conv: tap (ky, kx) reads offset (ky - pad, kx - pad)
+    View v = plain_view(g.src, g.cin, sw, sh, n_img, g.ps);
+    p.gh = g.oh; p.gw = g.ow; p.out_h = g.oh; p.out_w = g.ow; p.ys = p.xs = 1;
+    TapPhase& ph = p.ph[0];
+    ph.ntaps = g.ksize * g.ksize;
+    for (int t = 0; t < ph.ntaps; ++t) {
+      ph.map[t] = 0;
+      ph.dy[t] = (int8_t)(t / g.ksize - g.pad);
+      ph.dx[t] = (int8_t)(t % g.ksize - g.pad);
+    }
+    return run_plan(ctx, &v, 1, w, n_rows, g.k_total, p, 1, e);
+  }
+  if (g.mode == MODE_DGRAD && g.stride == 1 && sw == g.wv && sh == g.hv) {
+    // stride-1 dX: the flipped taps over dy
+    View v = plain_view(g.src, g.cin, sw, sh, n_img, g.ps);
+    p.gh = g.oh; p.gw = g.ow; p.out_h = g.oh; p.out_w = g.ow; p.ys = p.xs = 1;
+    TapPhase& ph = p.ph[0];
+    ph.ntaps = g.ksize * g.ksize;
+    for (int t = 0; t < ph.ntaps; ++t) {
+      ph.map[t] = 0;
+      ph.dy[t] = (int8_t)(g.pad - t / g.ksize);
+      ph.dx[t] = (int8_t)(g.pad - t % g.ksize);
+    }
+    return run_plan(ctx, &v, 1, w, n_rows, g.k_total, p, 1, e);
+  }
+  if (g.mode == MODE_FPROP && g.stride == 2 && !g.up && k3p1 && sw == g.wv && sh == g.hv &&
+      sw >= 2 && sh >= 2) {
+    // stride-2 conv: tap offset r = k - pad lands in input phase (r & 1) at lattice offset r >> 1
+    View v[4];
+    for (int a = 0; a < 2; ++a)
+      for (int b = 0; b < 2; ++b) v[a * 2 + b] = phase_view(g.src, g.cin, sw, sh, n_img, g.ps, a, b);
+    p.gh = g.oh; p.gw = g.ow; p.out_h = g.oh; p.out_w = g.ow; p.ys = p.xs = 1;
+    TapPhase& ph = p.ph[0];
+    ph.ntaps = 9;
+    for (int t = 0; t < 9; ++t) {
+      const int ry = t / 3 - 1, rx = t % 3 - 1;
+      ph.map[t] = (int8_t)(((ry & 1) << 1) | (rx & 1));
+      ph.dy[t] = (int8_t)(ry >> 1);
+      ph.dx[t] = (int8_t)(rx >> 1);
+    }
+    return run_plan(ctx, v, 4, w, n_rows, g.k_total, p, 1, e);
+  }
+  if (g.mode == MODE_FPROP && g.up && g.stride == 1 && k3p1 && g.hv == 2 * sh && g.wv == 2 * sw) {
+    // nearest-x2 upsample + conv: four output phases, each a 2x2 conv on the source
+    void* wsb = nullptr;
+    YL_TRY(scratch_get(ctx, (size_t)4 * n_rows * 4 * g.cin * sizeof(float), &wsb));
+    float* wm = (float*)wsb;
+    up_merge_weights_kernel<<<grid_1d(16LL * n_rows * g.cin, 256), 256, 0, ctx->stream>>>(
+        w, wm, n_rows, g.cin);
+    YL_TRY(check_launch("up_merge_weights_kernel"));
+    View v = plain_view(g.src, g.cin, sw, sh, n_img, g.ps);
+    p.gh = sh; p.gw = sw; p.out_h = g.oh; p.out_w = g.ow; p.ys = p.xs = 2;
+    for (int ph = 0; ph < 4; ++ph) {
+      const int a = ph >> 1, b = ph & 1;
+      TapPhase& tp = p.ph[ph];
+      tp.ntaps = 4;
+      tp.w_row0 = ph * n_rows;
+      tp.ya = a;
+      tp.xa = b;
+      for (int t = 0; t < 4; ++t) {
+        tp.map[t] = 0;
+        tp.dy[t] = (int8_t)((t >> 1) + a - 1);
+        tp.dx[t] = (int8_t)((t & 1) + b - 1);
+      }
+    }
+    return run_plan(ctx, &v, 1, wm, 4 * n_rows, 4 * g.cin, p, 4, e);
+  }
+  if (g.mode == MODE_DGRAD && g.stride == 2 && k3p1 && sw == g.wv && sh == g.hv) {
+    // stride-2 dX: output phase (a, b) gathers the dy taps whose parity matches
+    void* wsb = nullptr;
+    YL_TRY(scratch_get(ctx, (size_t)4 * n_rows * 4 * g.cin * sizeof(float), &wsb));
+    float* wp = (float*)wsb;
+    s2_phase_weights_kernel<<<grid_1d(16LL * n_rows * g.cin, 256), 256, 0, ctx->stream>>>(
+        w, wp, n_rows, g.cin);
+    YL_TRY(check_launch("s2_phase_weights_kernel"));
+    View v = plain_view(g.src, g.cin, sw, sh, n_img, g.ps);
+    p.gh = (g.oh + 1) / 2; p.gw = (g.ow + 1) / 2; p.out_h = g.oh; p.out_w = g.ow;
+    p.ys = p.xs = 2;
+    for (int ph = 0; ph < 4; ++ph) {
+      const int a = ph >> 1, b = ph & 1;
+      const int nr = a == 0 ? 1 : 2, nc = b == 0 ? 1 : 2;
+      const int ro[2] = {a == 0 ? 0 : 1, 0}, co[2] = {b == 0 ? 0 : 1, 0};
+      TapPhase& tp = p.ph[ph];
+      tp.ntaps = nr * nc;
+      tp.w_row0 = ph * n_rows;
+      tp.ya = a;
+      tp.xa = b;
+      for (int t = 0; t < tp.ntaps; ++t) {
+        tp.map[t] = 0;
+        tp.dy[t] = (int8_t)ro[t / nc];
+        tp.dx[t] = (int8_t)co[t % nc];
+      }
+    }
+    return run_plan(ctx, &v, 1, wp, 4 * n_rows, 4 * g.cin, p, 4, e);
+  }
+  return conv_fprop_gather(ctx, g, w, n_rows, e);
+}
+
+yl_status conv_wgrad_ws(yl_ctx* ctx, const float* dy, int ldy, int cout, const ConvGather& g,
+                        float* dw, int accumulate, float* ws, int splits) {
+  constexpr int BN = 128;
+  using Cfg = TileCfg<BN>;
+  int sw = 0, sh = 0;
+  const bool k3p1 = g.ksize == 3 && g.pad == 1;
+  const bool base_ok = g.cin % BN == 0 && g.m_total > 0 && g.m_total % (g.oh * g.ow) == 0 &&
+                       ((uintptr_t)g.src & 15) == 0 && ((uintptr_t)dy & 15) == 0 &&
+                       g.ps % 4 == 0 && ldy % 4 == 0 && source_dims(g, &sw, &sh) && splits >= 1;
+  int mode = -1;
+  if (base_ok) {
+    if (g.stride == 1 && !g.up && sw == g.wv && sh == g.hv) mode = WG_PLAIN;
+    else if (g.stride == 2 && !g.up && k3p1 && sw == g.wv && sh == g.hv && sw >= 2 && sh >= 2)
+      mode = WG_STRIDE2;
+    else if (g.stride == 1 && g.up && k3p1 && g.hv == 2 * sh && g.wv == 2 * sw && g.oh % 2 == 0 &&
+             g.ow % 2 == 0)
+      mode = WG_UP;
+  }
+  if (mode < 0) return conv_wgrad_gather(ctx, dy, ldy, cout, g, dw, accumulate, ws, splits);
+  const int n_img = g.m_total / (g.oh * g.ow);
+  View av[4], bv[4];
+  int nav = 1, nbv = 1;
+  WgradPlan w{};
+  w.mode = mode;
+  w.ksize = g.ksize;
+  w.pad = g.pad;
+  w.cin = g.cin;
+  w.cout = cout;
+  w.n_total = g.k_total;
+  if (mode == WG_UP) {
+    for (int ph = 0; ph < 4; ++ph)
+      av[ph] = phase_view(dy, cout, g.ow, g.oh, n_img, ldy, ph >> 1, ph & 1);
+    nav = 4;
+    bv[0] = plain_view(g.src, g.cin, sw, sh, n_img, g.ps);
+    w.nkp = 4;
+    w.gh = g.oh / 2;
+    w.gw = g.ow / 2;
+  } else {
+    av[0] = plain_view(dy, cout, g.ow, g.oh, n_img, ldy);
+    if (mode == WG_STRIDE2) {
+      for (int a = 0; a < 2; ++a)
+        for (int b = 0; b < 2; ++b)
+          bv[a * 2 + b] = phase_view(g.src, g.cin, sw, sh, n_img, g.ps, a, b);
+      nbv = 4;
+    } else {
+      bv[0] = plain_view(g.src, g.cin, sw, sh, n_img, g.ps);
+    }
+    w.nkp = 1;
+    w.gh = g.oh;
+    w.gw = g.ow;
+  }
+  w.xblocks = (w.gw + 31) / 32;
+  w.n_img = n_img;
+  w.blocks_per_kp = (long long)n_img * w.gh * w.xblocks;
+  w.blocks = w.blocks_per_kp * w.nkp;
+  w.per_split = (w.blocks + splits - 1) / splits;
+  w.ws = ws;
+  w.ws_split_stride = (long long)cout * g.k_total;
+  CUtensorMap ta[4], tb[4];
+  for (int i = 0; i < 4; ++i) {
+    YL_TRY(make_view_tmap(&ta[i], av[i < nav ? i : 0], 32, 1, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B));
+    YL_TRY(make_view_tmap(&tb[i], bv[i < nbv ? i : 0], 32, 1, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B));
+  }
+  YL_CUDA(cudaFuncSetAttribute(conv_tma_wgrad_kernel<BN>,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes));
+  dim3 grid((cout + kBM - 1) / kBM, g.k_total / BN, splits);
+  conv_tma_wgrad_kernel<BN><<<grid, kThreads, Cfg::kSmemBytes, ctx->stream>>>(
+      ta[0], ta[1], ta[2], ta[3], tb[0], tb[1], tb[2], tb[3], w, ctx->dev_err);
+  YL_TRY(check_launch("conv_tma_wgrad_kernel"));
+  const long long n = (long long)cout * g.k_total;
+  splitk_reduce_kernel<<<grid_1d(n / 4 + 1, 256), 256, 0, ctx->stream>>>(ws, splits, n, dw, n,
+                                                                         accumulate);
+  return check_launch("splitk_reduce_kernel");
+}
+
+}  // namespace yl
