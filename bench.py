@@ -161,7 +161,7 @@ def run_reference(args):
             "n_gpus": args.gpus, "steps": steps, "warmup": warmup,
             "ms_per_step": 1000 * cb["seconds_per_sample_step"], "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": "joint VAE + motion-net train step (config 5), CPU oracle "
+            "config": {"workload": "joint VAE + motion-net train step at 854x480, CPU oracle "
                                    "sample", "parallelism": "host threads"},
             "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
             "e2e": {"value": cb["value"], "unit": "frame-pairs/s", "h2d_bytes_per_step": 0,
@@ -176,7 +176,8 @@ def run_native(args):
     from yumelayers_b200 import synth
     from yumelayers_b200._lib import lib
     from yumelayers_b200.session import Context
-    from yumelayers_b200.trainer import Comm, Trainer, default_config, share_unique_id
+    from yumelayers_b200.trainer import (Comm, Trainer, default_config, max_over_ranks,
+                                         share_unique_id)
 
     rank, world, local = dist_env()
     torch.cuda.set_device(local)
@@ -194,7 +195,7 @@ def run_native(args):
     B, H, W = args.batch, args.height, args.width
     tr = Trainer(default_config(batch=B, height=H, width=W, seed=0), ctx=ctx, comm=comm)
 
-    # synthetic clips, a few distinct step batches
+    # synthetic 17-frame clips, a few distinct step batches
     clips = [synth.make_clip(1000 * rank + c, h=H, w=854 if W == 856 else W, width_padded=W)
              for c in range(2)]
     nb = 3
@@ -215,13 +216,6 @@ def run_native(args):
             dist.barrier()
         torch.cuda.synchronize()
 
-    def max_over_ranks(x: float) -> float:
-        if world == 1:
-            return x
-        t = torch.tensor([x], dtype=torch.float64, device=f"cuda:{local}")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
-
     for i in range(args.warmup):
         tr.step_device(dev[i % nb].data_ptr(), tdev[i % nb].data_ptr(), losses_dev.data_ptr())
     barrier()
@@ -240,7 +234,7 @@ def run_native(args):
         ev1.synchronize()
     barrier()
     launches = lib().yl_kernel_launch_count() - launches0
-    ms = max_over_ranks(ev0.elapsed_time(ev1))
+    ms = max_over_ranks(ev0.elapsed_time(ev1), f"cuda:{local}")
     clocks = clk.summary()
     stats = tr.kernel_stats(reset=True)
     tr.set_config(profile=0)
@@ -258,15 +252,16 @@ def run_native(args):
     e1.synchronize()
     wall = time.perf_counter() - w0
     barrier()
-    e2e_ms = max_over_ranks(max(e0.elapsed_time(e1), 1000 * wall))
+    e2e_ms = max_over_ranks(max(e0.elapsed_time(e1), 1000 * wall), f"cuda:{local}")
 
     value = world * B * args.steps / (ms / 1000.0)
     e2e_value = world * B * args.steps / (e2e_ms / 1000.0)
     peaks = measured_peaks()
-    bf16 = peaks.get("bf16_tflops")
+    # the convs run inside a step of a few hundred ms: the sustained GEMM peak
+    bf16 = peaks.get("bf16_tflops_sustained")
     hbm = peaks.get("hbm_gbs")
-    peak_src = "measured" if bf16 else "fallback"
-    bf16 = bf16 or 1590.0
+    peak_src = "measured sustained" if bf16 else "fallback sustained"
+    bf16 = bf16 or 1400.0
     hbm = hbm or 6650.0
     tf32_peak = bf16 / 2.0
     kernels = {}
@@ -292,6 +287,7 @@ def run_native(args):
                               f"{bf16:.1f} TFLOP/s (no tf32 peak is measured)"),
                 "all_convs": {"achieved": conv_flops / (conv_ms * 1e-3) / 1e12,
                               "frac": conv_flops / (conv_ms * 1e-3) / 1e12 / tf32_peak}}
+    act_gb = tr.activation_bytes() / 1e9
     if rank == 0:
         cpu = None
         if world == 1 and not args.no_cpu_baseline:
@@ -306,12 +302,13 @@ def run_native(args):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "tf32",
             "data": "synthetic (seeded 17-frame clips: blobs + gratings + 4 moving sprites)",
-            "config": {"workload": "joint VAE + motion-net train step (config 5): VAE fwd+bwd "
+            "config": {"workload": "joint VAE + motion-net train step at 854x480: VAE fwd+bwd "
                                    "on frame k, encoder fwd on frames 0/16, U-Net fwd+bwd, "
                                    "all-reduce, Adam",
                        "frame": f"{H}x{W} (854 padded to 856)", "per_gpu_batch": B,
                        "global_batch": B * world, "parallelism": f"dp{world}",
-                       "l2": "working set ~60 GB per GPU >> 126 MB L2; no explicit flush",
+                       "l2": (f"working set {act_gb:.0f} GB per GPU >> 126 MB L2; "
+                              "no explicit flush"),
                        "conv_tflop_per_step": conv_flops / 1e12 / args.steps},
             "e2e": {"value": e2e_value, "unit": "frame-pairs/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": 8, "ms_per_step": e2e_ms / args.steps},

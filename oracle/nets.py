@@ -10,7 +10,7 @@ SiLU; LinearGPU (DenoiserMLP.swift:51-64); motionTimeEmbedding
 vae_grad_kernel MetalKernelSourcesB.swift:365-402) with trainingNoiseSeed
 (ConvVAEHelpers.swift:33-37); L1 (l1grad_kernel B:453-461) + beta * mean KL
 (ConvGPU.swift:435-438); Adam (MetalKernelSourcesA.swift:271-287).  The
-network tables are the same as the CUDA executor's (the BASELINE VAE and
+network tables are the same as the CUDA executor's (the 854x480 conv VAE and
 motion U-Net), read from the trainer's parameter table so the two start
 from identical weights.  Layout: NCHW numpy arrays.
 """
@@ -161,7 +161,7 @@ def noise_seed(L, step: int, img: int) -> int:
 
 
 class VAE:
-    """The BASELINE conv VAE (same layer table as the CUDA executor)."""
+    """The 854x480-frame conv VAE (same layer table as the CUDA executor)."""
     ENC = [("enc.rb1a", 128, 128), ("enc.rb1b", 128, 128), ("enc.down1", 128, 128),
            ("enc.rb2a", 128, 256), ("enc.rb2b", 256, 256), ("enc.down2", 256, 256),
            ("enc.rb3a", 256, 256), ("enc.rb3b", 256, 256), ("enc.down3", 256, 256)]
@@ -257,7 +257,7 @@ class VAE:
 
 
 class UNet:
-    """The BASELINE motion U-Net (same table as the CUDA executor)."""
+    """The latent-space motion U-Net (same table as the CUDA executor)."""
     BLOCKS = ["down1.rb_a", "down1.rb_b", "down2.rb_a", "down2.rb_b", "mid.rb_a", "mid.rb_b",
               "up1.rb_a", "up1.rb_b", "up2.rb_a", "up2.rb_b"]
     CH = {"down1.rb_a": (128, 128), "down1.rb_b": (128, 128), "down2.rb_a": (128, 256),

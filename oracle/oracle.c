@@ -638,7 +638,7 @@ ORC_API void orc_conv2d_bwd(const float* x, int N, int C, int H, int W,
 }
 
 /* GroupNorm with affine gamma/beta and eps (torch.nn.GroupNorm semantics, the
- * BASELINE op; affine-free clamp variant is orc_groupnorm_ref above), followed
+ * workload op; affine-free clamp variant is orc_groupnorm_ref above), followed
  * by SiLU when silu != 0.  Per image; double statistics like groupNormCPU
  * (LossFunctions.swift:97-126).  mean/rstd (N*G) are optional outputs. */
 ORC_API void orc_gn_silu_fwd(const float* x, int N, int C, int HW, int G, float eps,
@@ -768,7 +768,7 @@ ORC_API void orc_linear_bwd(const float* X, const float* Wt, const float* dY, fl
     }
 }
 
-/* VAE loss head (BASELINE: L1 reconstruction + beta * KL averaged per latent
+/* VAE loss head (L1 reconstruction + beta * KL averaged per latent
  * element, the KL scaling of ConvVAEGPU.backward, ConvGPU.swift:435-438):
  * returns loss; writes dRecon = sign(r - t)/n_r (l1grad_kernel, B:453-461). */
 ORC_API double orc_l1_kl_loss(const float* recon, const float* target, long nr,

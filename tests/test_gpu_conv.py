@@ -21,7 +21,7 @@ def kaiming_uniform(rng, oc, ic, k):
 
 CASES = [
     # (name, n, c, oc, h, w, k, stride, pad, up, up_hw)
-    ("config1", 2, 32, 32, 64, 64, 3, 1, 1, False, None),
+    ("n2_c32_64x64", 2, 32, 32, 64, 64, 3, 1, 1, False, None),
     ("ragged", 1, 12, 20, 9, 13, 3, 1, 1, False, None),
     ("stride2", 2, 16, 24, 15, 17, 3, 2, 1, False, None),
     ("up", 2, 8, 16, 5, 6, 3, 1, 1, True, None),

@@ -7,7 +7,7 @@
 // LinearGPU (DenoiserMLP.swift:20-71), ConvVAEGPU encode/decode/backward
 // (ConvGPU.swift:301-462), the motion net's lerp + residual prediction
 // (MotionMLP.swift:39-111) and TrainContext's step (TrainConvVAE.swift:
-// 327-362) -- re-expressed for the BASELINE architectures (GroupNorm32+SiLU
+// 327-362) -- re-expressed for the target architectures (GroupNorm32+SiLU
 // residual blocks, 128/256-channel VAE, 128/256/384-level U-Net).
 //
 // Per step nothing is allocated after the first step: activations are
@@ -327,7 +327,7 @@ yl_status GNL::bind(Net& net, int n) {
   return net.arena.alloc((size_t)n * G, &rstd);
 }
 yl_status GNL::init(yl_ctx* ctx, uint64_t seed) {
-  // BASELINE init: gamma = 1 + 0.02 N(0,1), beta = 0.02 N(0,1)
+  // workload init: gamma = 1 + 0.02 N(0,1), beta = 0.02 N(0,1)
   init_normal_kernel<<<grid_1d(c, 256), 256, 0, ctx->stream>>>(gamma, c, 1.f, 0.02f, seed);
   YL_TRY(check_launch("init_normal_kernel"));
   init_normal_kernel<<<grid_1d(c, 256), 256, 0, ctx->stream>>>(beta, c, 0.f, 0.02f, seed ^ 0x5bd1e995);

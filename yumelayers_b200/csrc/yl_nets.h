@@ -150,7 +150,7 @@ struct Net {
   yl_status prepare_weights();
 };
 
-// Conv VAE: 854x480 frames padded to 856, 32-channel
+// Conv VAE of the 854x480 frame workload: frames padded to 856, 32-channel
 // latent at 1/8 resolution.
 struct VAE : Net {
   static constexpr int kLatent = 32;
@@ -166,7 +166,7 @@ struct VAE : Net {
   yl_status backward(int64_t step, float beta);  // from drecon
 };
 
-// Motion U-Net in the 32-channel latent space.
+// Motion U-Net (levels 128/256/384) in the 32-channel latent space.
 struct UNet : Net {
   static constexpr int kLat = 32, kEmb = 128, kTime = 512, kBlocks = 10;
   int N = 0, H = 0, W = 0;

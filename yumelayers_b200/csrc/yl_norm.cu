@@ -4,7 +4,7 @@
 // Replaces groupNorm / encodeGroupNormGrad (GpuSessionOps.swift:121-131,
 // GpuSessionNormGrad.swift:10-24; kernels MetalKernelSourcesC.swift:10-101,
 // one thread per group with serial loops) plus the separate activation and
-// activation-gradient passes (relu/sigmoid kernels B:191-224).  The BASELINE
+// activation-gradient passes (relu/sigmoid kernels B:191-224).  The target
 // op is torch.nn.GroupNorm (affine, eps) followed by SiLU; `mode` 1 selects
 // the reference's own variance rule (var = max(E[x^2]-E[x]^2, 1e-5), no eps).
 //

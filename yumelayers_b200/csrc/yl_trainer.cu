@@ -1,7 +1,7 @@
 // yl_trainer.cu -- the joint VAE + motion-net training step behind the C ABI,
 // data-parallel over NCCL.
 //
-// One step on each rank, per BASELINE config 5 with per-rank batch B
+// One step on each rank of the joint frame-pair workload, per-rank batch B
 // (TrainContext.runStep, TrainConvVAE.swift:327-362, and the motion step,
 // MotionTrainer.swift:214-260 / 450-485, folded into one):
 //   1. encoder forward (no gradient) on frames 0 and 16 -> zA, zB (latent means)

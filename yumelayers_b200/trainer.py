@@ -81,6 +81,18 @@ def shard_batch(global_batch: int, world: int, rank: int) -> tuple[int, int]:
     return rank * per, (rank + 1) * per
 
 
+def max_over_ranks(x: float, device: str = "cpu") -> float:
+    """The maximum of a per-rank scalar (a timed duration) over the default
+    torch.distributed group; the scalar itself when there is no group."""
+    import torch
+    import torch.distributed as dist
+    if not dist.is_available() or not dist.is_initialized() or dist.get_world_size() == 1:
+        return x
+    t = torch.tensor([x], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
 class Trainer:
     """One rank's joint trainer (``yl_trainer``)."""
 
