@@ -265,13 +265,15 @@ yl_status yl_groupnorm_silu_fwd(yl_ctx* ctx, const float* x, int n, int c, int h
   YL_CHECK(ctx && x && y, YL_ERR_INVALID, "yl_groupnorm_silu_fwd: NULL argument");
   YL_CHECK(layout == YL_LAYOUT_NCHW || layout == YL_LAYOUT_NHWC, YL_ERR_INVALID, "bad layout");
   const long long hw = (long long)h * w;
-  Pieces pc;
-  size_t o_x = pc.add(n * hw * c), o_y = pc.add(n * hw * c), o_s = pc.add(2 * (size_t)n * groups);
+  const bool direct = layout == YL_LAYOUT_NHWC && c % 4 == 0;
+  Pieces pc;  // staging copies only when the caller's layout is not the internal one
+  size_t o_x = direct ? 0 : pc.add(n * hw * c), o_y = direct ? 0 : pc.add(n * hw * c);
+  size_t o_s = pc.add(2 * (size_t)n * groups);
   void* base = nullptr;
   YL_TRY(scratch_get(ctx, pc.carve.offset, &base, 1));
   char* sb = (char*)base;
-  float* xh = layout == YL_LAYOUT_NHWC && c % 4 == 0 ? (float*)x : (float*)(sb + o_x);
-  float* yh = layout == YL_LAYOUT_NHWC && c % 4 == 0 ? y : (float*)(sb + o_y);
+  float* xh = direct ? (float*)x : (float*)(sb + o_x);
+  float* yh = direct ? y : (float*)(sb + o_y);
   float* mean = mean_out ? mean_out : (float*)(sb + o_s);
   float* rstd = rstd_out ? rstd_out : (float*)(sb + o_s) + (size_t)n * groups;
   if (xh != x) YL_TRY(to_internal(ctx, x, layout, n, c, hw, c, 0, xh));
@@ -290,9 +292,10 @@ yl_status yl_groupnorm_silu_bwd(yl_ctx* ctx, const float* x, const float* dy, in
   YL_CHECK(layout == YL_LAYOUT_NCHW || layout == YL_LAYOUT_NHWC, YL_ERR_INVALID, "bad layout");
   const long long hw = (long long)h * w;
   const bool direct = layout == YL_LAYOUT_NHWC && c % 4 == 0;
-  Pieces pc;
-  size_t o_x = pc.add(n * hw * c), o_dy = pc.add(n * hw * c), o_a = pc.add(n * hw * c),
-         o_dx = pc.add(n * hw * c), o_s = pc.add(2 * (size_t)n * groups);
+  Pieces pc;  // staging copies only when the caller's layout is not the internal one
+  const size_t e = direct ? 0 : (size_t)(n * hw * c);
+  size_t o_x = pc.add(e), o_dy = pc.add(e), o_a = pc.add(addend ? e : 0), o_dx = pc.add(e),
+         o_s = pc.add(2 * (size_t)n * groups);
   void* base = nullptr;
   YL_TRY(scratch_get(ctx, pc.carve.offset, &base, 1));
   char* sb = (char*)base;
