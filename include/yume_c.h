@@ -229,6 +229,21 @@ yl_status yl_groupnorm_silu_fwd(yl_ctx* ctx, const float* x, int n, int c, int h
                                 int layout, int groups, float eps, int mode, const float* gamma,
                                 const float* beta, int apply_silu, float* y, float* mean_out,
                                 float* rstd_out);
+/* yl_groupnorm_silu_fwd for callers that may not allocate device memory
+ * during the call (a host whose allocator refuses growth after start-up, or
+ * code that must not add allocations to work it is recording).  It has no
+ * counterpart in the reference, whose every op allocates its output.
+ * The statistics partials live in a fixed 1 MiB array inside the library
+ * (n * chunks * 2 * groups doubles, chunks <= 592/n + 1); larger requests
+ * return YL_ERR_SHAPE without launching.  NHWC layout only; mean_out and
+ * rstd_out (n*groups) are required.  The first call on each device looks the
+ * array up (cudaGetSymbolAddress) and must come before any stream capture.
+ * Nothing needs to start at zero.  Calls that overlap on one device share
+ * the array and race: serialise them. */
+yl_status yl_groupnorm_silu_fwd_noalloc(yl_ctx* ctx, const float* x, int n, int c, int h, int w,
+                                        int groups, float eps, int mode, const float* gamma,
+                                        const float* beta, int apply_silu, float* y,
+                                        float* mean_out, float* rstd_out);
 /* encodeGroupNormGrad (GpuSessionNormGrad.swift:10-24) with the affine and
  * SiLU terms: dx (+= addend when not NULL), dgamma/dbeta summed over (n, h, w).
  * mean/rstd may be NULL (recomputed). */

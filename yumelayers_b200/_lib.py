@@ -122,6 +122,7 @@ SIGNATURES: dict[str, list] = {
     "yl_conv_transpose2d_bwd_filter": [P, C.POINTER(ConvDesc), P, P, P, P],
     "yl_groupnorm_silu_fwd": [P, P, I, I, I, I, I, I, F, I, P, P, I, P, P, P],
     "yl_groupnorm_silu_bwd": [P, P, P, I, I, I, I, I, I, F, I, P, P, I, P, P, P, P, P, P],
+    "yl_groupnorm_silu_fwd_noalloc": [P, P, I, I, I, I, I, F, I, P, P, I, P, P, P],
     "yl_linear_fwd": [P, P, P, P, P, I, I, I],
     "yl_linear_bwd": [P, P, P, P, P, P, P, I, I, I],
     "yl_timestep_embedding": [P, P, I, I, I, P],

@@ -19,6 +19,8 @@
 //           (2) dx = rstd*(dxh - mean(dxh) - xh*mean(dxh*xh)) (+ addend).
 // Memory traffic per element: forward 2 reads + 1 write, backward 4 reads +
 // 1 write (+1 read for the addend).
+#include <mutex>
+
 #include "yl_kernels.h"
 #include "yl_norm.h"
 #include "yl_ptx.cuh"
@@ -337,4 +339,89 @@ yl_status gn_silu_backward(yl_ctx* ctx, const float* x, const float* dy, int ldd
   return check_launch("gn_bwd_apply_kernel");
 }
 
+// ---------------------------------------------------------------------------
+// GroupNorm(+affine)+SiLU forward that allocates no device memory.
+//
+// yl_groupnorm_silu_fwd takes its per-(image, chunk, group) statistics
+// partials from the context's stream-ordered scratch, which grows with
+// cudaMallocAsync whenever a call needs more than it holds.  Some callers may
+// not allocate inside the call: a host that fixes the process's device
+// footprint at start-up (its pool or allocator refuses later growth), or code
+// that must not add allocation nodes or synchronisation to the work it is
+// recording.  This variant keeps the partials in a fixed array compiled into
+// the library instead.
+//
+// Limits and rules:
+//  * the partials need n * chunks * 2 * groups doubles, chunks being the
+//    pixel split of gn_geom (at most 592 / n + 1); calls that need more than
+//    kGnNoAllocDoubles (131072 doubles = 1 MiB) are rejected with
+//    YL_ERR_SHAPE before anything is launched;
+//  * NHWC layout only, channels and channels per group multiples of 4, and
+//    the caller provides mean_out / rstd_out (no other temporaries exist);
+//  * the first call on each device looks the array up with
+//    cudaGetSymbolAddress (which may load the library's device code), so make
+//    one call on every device before recording the calls into a graph;
+//  * nothing has to start at zero: each call overwrites every partial it
+//    reads;
+//  * one array per device: calls that overlap on the same device (two
+//    streams, two threads, two contexts) race on it.  Serialise them.
+constexpr size_t kGnNoAllocDoubles = 131072;
+static __device__ __align__(256) double g_gn_noalloc_partials[kGnNoAllocDoubles];
+
+namespace {
+constexpr int kMaxNoAllocDevices = 64;
+std::mutex g_noalloc_mu;
+double* g_noalloc_ptr[kMaxNoAllocDevices] = {};
+}  // namespace
+
+static yl_status gn_noalloc_scratch(int device, double** out) {
+  YL_CHECK(device >= 0 && device < kMaxNoAllocDevices, YL_ERR_INVALID,
+           "no-alloc groupnorm: device %d out of range", device);
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_ptr[device]) {
+    int cur = -1;
+    YL_CUDA(cudaGetDevice(&cur));
+    YL_CHECK(cur == device, YL_ERR_INVALID,
+             "no-alloc groupnorm: the context's device %d must be current (current is %d)",
+             device, cur);
+    void* p = nullptr;
+    YL_CUDA(cudaGetSymbolAddress(&p, g_gn_noalloc_partials));
+    g_noalloc_ptr[device] = static_cast<double*>(p);
+  }
+  *out = g_noalloc_ptr[device];
+  return YL_OK;
+}
+
 }  // namespace yl
+
+extern "C" yl_status yl_groupnorm_silu_fwd_noalloc(yl_ctx* ctx, const float* x, int n, int c,
+                                                   int h, int w, int groups, float eps, int mode,
+                                                   const float* gamma, const float* beta,
+                                                   int apply_silu, float* y, float* mean_out,
+                                                   float* rstd_out) {
+  using namespace yl;
+  YL_CHECK(ctx && x && y && mean_out && rstd_out, YL_ERR_INVALID,
+           "yl_groupnorm_silu_fwd_noalloc: NULL argument (mean_out and rstd_out are required)");
+  const long long hw = (long long)h * w;
+  YL_CHECK(h > 0 && w > 0, YL_ERR_SHAPE, "yl_groupnorm_silu_fwd_noalloc: empty image");
+  YL_TRY(gn_check(n, c, groups, hw, c));
+  GnGeom q = gn_geom(n, c, groups, hw, c);
+  const size_t need = (size_t)n * q.chunks * 2 * groups;
+  YL_CHECK(need <= kGnNoAllocDoubles, YL_ERR_SHAPE,
+           "yl_groupnorm_silu_fwd_noalloc: n=%d groups=%d needs %zu statistics doubles, above "
+           "the fixed %zu; use yl_groupnorm_silu_fwd",
+           n, groups, need, kGnNoAllocDoubles);
+  double* part = nullptr;
+  YL_TRY(gn_noalloc_scratch(ctx->device, &part));
+  dim3 grid(q.chunks, n);
+  gn_stats_partial_kernel<<<grid, q.quads * q.rows, 2 * groups * sizeof(double), ctx->stream>>>(
+      x, q, part);
+  YL_TRY(check_launch("gn_stats_partial_kernel"));
+  gn_stats_final_kernel<<<(n * groups + 127) / 128, 128, 0, ctx->stream>>>(part, q, eps, mode,
+                                                                          mean_out, rstd_out);
+  YL_TRY(check_launch("gn_stats_final_kernel"));
+  const long long total = (long long)n * hw * q.quads;
+  gn_apply_kernel<<<grid_1d(total, 256, ctx->num_sms * 16), 256, 0, ctx->stream>>>(
+      x, q, mean_out, rstd_out, gamma, beta, apply_silu, 0, y, c);
+  return check_launch("gn_apply_kernel");
+}
