@@ -37,11 +37,49 @@ struct ConvPlan {
   int n_img, tiles_x, tiles_y;
   int out_h, out_w;    // output tensor extent
   int ys, xs;          // output pixel = (oy * ys + ya, ox * xs + xa)
-  TapPhase ph[4];      // indexed by blockIdx.z
+  int n_nblk;          // BN-wide blocks of output channels
+  int pix_tiles;       // tiles_x * tiles_y * n_img
+  int n_tiles;         // pix_tiles * n_nblk * phases
+  TapPhase ph[4];      // indexed by the tile's phase
 };
 
-// Output tile: 4 lattice rows x 32 lattice columns (128 GEMM rows).
-template <int BN>
+// A tile is MT x 128 GEMM rows (MT*4 lattice rows x 32 lattice columns) by BN
+// output channels.  MT = 2 gives two M=128 accumulators that share every B
+// (weight) tile, which halves the weight bytes per MMA for cout <= 128.
+template <int BN, int MT>
+struct FpropCfg {
+  static constexpr int kATile = MT * kATileBytes;
+  static constexpr int kBTile = BN * 128;
+  static constexpr int kStage = kATile + kBTile;
+  static constexpr int kStages = (200 * 1024) / kStage > 8 ? 8 : (200 * 1024) / kStage;
+  static constexpr int kAccCols = MT * BN < 32 ? 32 : MT * BN;
+  static constexpr int kTmemCols = 2 * kAccCols;  // two accumulator buffers
+  static constexpr int kSmemBytes = kStages * kStage + (2 * kStages + 4) * 8 + 16 + 1024;
+  static_assert(kTmemCols <= 512, "accumulators exceed TMEM");
+};
+
+struct FpropTile {
+  int nb, z, img, ty, tx;
+};
+
+__device__ __forceinline__ FpropTile fprop_tile(const ConvPlan& p, int t) {
+  FpropTile c;
+  c.nb = t % p.n_nblk;
+  t /= p.n_nblk;
+  const int pix = t % p.pix_tiles;
+  c.z = t / p.pix_tiles;
+  c.tx = pix % p.tiles_x;
+  const int r = pix / p.tiles_x;
+  c.ty = r % p.tiles_y;
+  c.img = r / p.tiles_y;
+  return c;
+}
+
+// Persistent: each CTA walks tiles blockIdx.x, blockIdx.x + gridDim.x, ...
+// Warp 4 streams A/B k-blocks through the shared-memory ring across tile
+// boundaries, warp 5 issues the MMAs into one of two TMEM accumulator
+// buffers, warps 0-3 drain the other buffer (epilogue) meanwhile.
+template <int BN, int MT>
 __global__ void __launch_bounds__(kThreads, 1)
     conv_tma_fprop_kernel(const __grid_constant__ CUtensorMap ta0,
                           const __grid_constant__ CUtensorMap ta1,
@@ -49,30 +87,28 @@ __global__ void __launch_bounds__(kThreads, 1)
                           const __grid_constant__ CUtensorMap ta3,
                           const __grid_constant__ CUtensorMap tw, ConvPlan p, ConvEpilogue e,
                           int* err) {
-  using Cfg = TileCfg<BN>;
+  using Cfg = FpropCfg<BN, MT>;
   constexpr int S = Cfg::kStages;
+  constexpr int kRows = 4 * MT;  // lattice rows per tile
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * Cfg::kStageBytes);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * Cfg::kStage);
   uint64_t* empty = full + S;
-  uint64_t* accum = empty + S;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
+  uint64_t* acc_full = empty + S;      // [2]: MMA -> epilogue
+  uint64_t* acc_empty = acc_full + 2;  // [2]: epilogue (128 threads) -> MMA
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int tx = blockIdx.x % p.tiles_x;
-  const int trest = blockIdx.x / p.tiles_x;
-  const int ty = trest % p.tiles_y;
-  const int img = trest / p.tiles_y;
-  const int ox0 = tx * 32, oy0 = ty * 4, n0 = blockIdx.y * BN;
-  const TapPhase& ph = p.ph[blockIdx.z];
-  const int nk = ph.ntaps * p.cpt;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    mbar_init(accum, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 128);
+    }
     fence_barrier_init();
   }
   if (warp == 5) {
@@ -91,105 +127,149 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 4) {
     if (lane == 0) {
       const CUtensorMap* maps[4] = {&ta0, &ta1, &ta2, &ta3};
-      int t = 0, chunk = 0;
-      for (int kb = 0; kb < nk; ++kb) {
-        const int s = kb % S;
-        if (kb >= S && !mbar_wait(&empty[s], ((kb / S) - 1) & 1)) {
-          report_error(err, YL_DEVERR_TIMEOUT);
-          break;
-        }
-        const uint32_t a_dst = smem_u32(smem + s * Cfg::kStageBytes);
-        mbar_arrive_expect_tx(&full[s], kATileBytes + Cfg::kBTileBytes);
-        tma_load_4d(a_dst, maps[ph.map[t]], &full[s], chunk * 32, ox0 + ph.dx[t], oy0 + ph.dy[t],
-                    img);
-        tma_load_2d(a_dst + kATileBytes, &tw, &full[s], kb * kBK, ph.w_row0 + n0);
-        if (++chunk == p.cpt) {
-          chunk = 0;
-          ++t;
+      uint32_t it = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < p.n_tiles; tile += gridDim.x) {
+        const FpropTile c = fprop_tile(p, tile);
+        const TapPhase& ph = p.ph[c.z];
+        const int nk = ph.ntaps * p.cpt;
+        const int ox0 = c.tx * 32, oy0 = c.ty * kRows, n0 = c.nb * BN;
+        int t = 0, chunk = 0;
+        for (int kb = 0; kb < nk; ++kb, ++it) {
+          const int s = it % S;
+          if (it >= S && !mbar_wait(&empty[s], ((it / S) - 1) & 1)) {
+            report_error(err, YL_DEVERR_TIMEOUT);
+            ok = false;
+            break;
+          }
+          const uint32_t a_dst = smem_u32(smem + s * Cfg::kStage);
+          mbar_arrive_expect_tx(&full[s], Cfg::kStage);
+          tma_load_4d(a_dst, maps[ph.map[t]], &full[s], chunk * 32, ox0 + ph.dx[t],
+                      oy0 + ph.dy[t], c.img);
+          tma_load_2d(a_dst + Cfg::kATile, &tw, &full[s], kb * kBK, ph.w_row0 + n0);
+          if (++chunk == p.cpt) {
+            chunk = 0;
+            ++t;
+          }
         }
       }
     }
   } else if (warp == 5) {
     if (lane == 0) {
       constexpr uint32_t idesc = idesc_tf32(kBM, BN, 0, 0);
-      for (int kb = 0; kb < nk; ++kb) {
-        const int s = kb % S;
-        if (!mbar_wait(&full[s], (kb / S) & 1)) {
+      uint32_t it = 0;
+      int tc = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < p.n_tiles; tile += gridDim.x, ++tc) {
+        const int buf = tc & 1, use = tc >> 1;
+        if (tc >= 2 && !mbar_wait(&acc_empty[buf], (use - 1) & 1)) {
           report_error(err, YL_DEVERR_TIMEOUT);
           break;
         }
         tc_fence_after();
-        const uint32_t a_addr = smem_u32(smem + s * Cfg::kStageBytes);
-        const uint32_t b_addr = a_addr + kATileBytes;
-#pragma unroll
-        for (int kk = 0; kk < kBK / 8; ++kk)
-          umma_tf32(tmem, sw128_desc(a_addr + kk * 32, 16, 1024),
-                    sw128_desc(b_addr + kk * 32, 16, 1024), idesc, (kb | kk) != 0);
-        umma_commit(&empty[s]);
-      }
-      umma_commit(accum);
-    }
-  }
-
-  if (warp < 4) {
-    const bool got = mbar_wait(accum, 0);
-    if (!got) report_error(err, YL_DEVERR_TIMEOUT);
-    tc_fence_after();
-    const int gy = oy0 + warp, gx = ox0 + lane;
-    const int Y = gy * p.ys + ph.ya, X = gx * p.xs + ph.xa;
-    const bool mval = got && gy < p.gh && gx < p.gw && Y < p.out_h && X < p.out_w;
-    const long long m = ((long long)img * p.out_h + Y) * p.out_w + X;
-#pragma unroll 1
-    for (int c0 = 0; c0 < BN; c0 += 32) {
-      if (n0 + c0 >= e.n_total) break;
-      uint32_t r[32];
-      tmem_ld_32x32b_x32(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0, r);
-      tmem_ld_wait();
-      if (!mval) continue;
-      const int nb = n0 + c0;
-      float v[32];
-#pragma unroll
-      for (int q = 0; q < 32; ++q) v[q] = __uint_as_float(r[q]);
-      if (e.bias) {
-#pragma unroll
-        for (int q = 0; q < 32; ++q)
-          if (nb + q < e.n_total) v[q] += __ldg(e.bias + nb + q);
-      }
-      if (e.bias2d) {
-        const float* b2 = e.bias2d + (long long)img * e.n_total + nb;
-#pragma unroll
-        for (int q = 0; q < 32; ++q)
-          if (nb + q < e.n_total) v[q] += __ldg(b2 + q);
-      }
-      const bool full32 = (nb + 32 <= e.n_total);
-      if (e.residual) {
-        const float* rp = e.residual + m * e.ldr + nb;
-        if (full32 && (e.ldr & 3) == 0) {
-#pragma unroll
-          for (int q = 0; q < 32; q += 4) {
-            float4 rv = *reinterpret_cast<const float4*>(rp + q);
-            v[q] += rv.x; v[q + 1] += rv.y; v[q + 2] += rv.z; v[q + 3] += rv.w;
+        const FpropTile c = fprop_tile(p, tile);
+        const int nk = p.ph[c.z].ntaps * p.cpt;
+        const uint32_t dacc = tmem + (uint32_t)(buf * Cfg::kAccCols);
+        for (int kb = 0; kb < nk; ++kb, ++it) {
+          const int s = it % S;
+          if (!mbar_wait(&full[s], (it / S) & 1)) {
+            report_error(err, YL_DEVERR_TIMEOUT);
+            ok = false;
+            break;
           }
-        } else {
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(smem + s * Cfg::kStage);
+          const uint32_t b_addr = a_addr + Cfg::kATile;
 #pragma unroll
-          for (int q = 0; q < 32; ++q)
-            if (nb + q < e.n_total) v[q] += rp[q];
+          for (int kk = 0; kk < kBK / 8; ++kk) {
+            const uint64_t bdesc = sw128_desc(b_addr + kk * 32, 16, 1024);
+#pragma unroll
+            for (int m = 0; m < MT; ++m)
+              umma_tf32(dacc + (uint32_t)(m * BN),
+                        sw128_desc(a_addr + m * kATileBytes + kk * 32, 16, 1024), bdesc, idesc,
+                        (kb | kk) != 0);
+          }
+          umma_commit(&empty[s]);
+        }
+        if (ok) umma_commit(&acc_full[buf]);
+      }
+    }
+  } else {
+    // epilogue: warp w owns TMEM lanes 32w..32w+31 = lattice row 4m + w of subtile m
+    int tc = 0;
+    for (int tile = blockIdx.x; tile < p.n_tiles; tile += gridDim.x, ++tc) {
+      const int buf = tc & 1, use = tc >> 1;
+      if (!mbar_wait(&acc_full[buf], use & 1)) {
+        report_error(err, YL_DEVERR_TIMEOUT);
+        break;
+      }
+      tc_fence_after();
+      const FpropTile c = fprop_tile(p, tile);
+      const TapPhase& ph = p.ph[c.z];
+      const int n0 = c.nb * BN;
+#pragma unroll 1
+      for (int m = 0; m < MT; ++m) {
+        const int gy = c.ty * kRows + m * 4 + warp, gx = c.tx * 32 + lane;
+        const int Y = gy * p.ys + ph.ya, X = gx * p.xs + ph.xa;
+        const bool mval = gy < p.gh && gx < p.gw && Y < p.out_h && X < p.out_w;
+        const long long mrow = ((long long)c.img * p.out_h + Y) * p.out_w + X;
+        const uint32_t tbase = tmem + ((uint32_t)(warp * 32) << 16) +
+                               (uint32_t)(buf * Cfg::kAccCols + m * BN);
+#pragma unroll 1
+        for (int c0 = 0; c0 < BN; c0 += 32) {
+          if (n0 + c0 >= e.n_total) break;
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(tbase + (uint32_t)c0, r);
+          tmem_ld_wait();
+          if (!mval) continue;
+          const int nb = n0 + c0;
+          float v[32];
+#pragma unroll
+          for (int q = 0; q < 32; ++q) v[q] = __uint_as_float(r[q]);
+          if (e.bias) {
+#pragma unroll
+            for (int q = 0; q < 32; ++q)
+              if (nb + q < e.n_total) v[q] += __ldg(e.bias + nb + q);
+          }
+          if (e.bias2d) {
+            const float* b2 = e.bias2d + (long long)c.img * e.n_total + nb;
+#pragma unroll
+            for (int q = 0; q < 32; ++q)
+              if (nb + q < e.n_total) v[q] += __ldg(b2 + q);
+          }
+          const bool full32 = (nb + 32 <= e.n_total);
+          if (e.residual) {
+            const float* rp = e.residual + mrow * e.ldr + nb;
+            if (full32 && (e.ldr & 3) == 0) {
+#pragma unroll
+              for (int q = 0; q < 32; q += 4) {
+                float4 rv = *reinterpret_cast<const float4*>(rp + q);
+                v[q] += rv.x; v[q + 1] += rv.y; v[q + 2] += rv.z; v[q + 3] += rv.w;
+              }
+            } else {
+#pragma unroll
+              for (int q = 0; q < 32; ++q)
+                if (nb + q < e.n_total) v[q] += rp[q];
+            }
+          }
+          if (e.round_tf32) {
+#pragma unroll
+            for (int q = 0; q < 32; ++q) v[q] = round_tf32(v[q]);
+          }
+          float* op = e.out + mrow * e.ldo + nb;
+          if (full32 && (e.ldo & 3) == 0) {
+#pragma unroll
+            for (int q = 0; q < 32; q += 4)
+              *reinterpret_cast<float4*>(op + q) = make_float4(v[q], v[q + 1], v[q + 2], v[q + 3]);
+          } else {
+#pragma unroll
+            for (int q = 0; q < 32; ++q)
+              if (nb + q < e.n_total) op[q] = v[q];
+          }
         }
       }
-      if (e.round_tf32) {
-#pragma unroll
-        for (int q = 0; q < 32; ++q) v[q] = round_tf32(v[q]);
-      }
-      float* op = e.out + m * e.ldo + nb;
-      if (full32 && (e.ldo & 3) == 0) {
-#pragma unroll
-        for (int q = 0; q < 32; q += 4)
-          *reinterpret_cast<float4*>(op + q) = make_float4(v[q], v[q + 1], v[q + 2], v[q + 3]);
-      } else {
-#pragma unroll
-        for (int q = 0; q < 32; ++q)
-          if (nb + q < e.n_total) op[q] = v[q];
-      }
+      tc_fence_before();
+      mbar_arrive(&acc_empty[buf]);
     }
   }
 
@@ -475,31 +555,46 @@ static yl_status make_view_tmap(CUtensorMap* tm, const View& v, int box_w, int b
   return YL_OK;
 }
 
-template <int BN>
+template <int BN, int MT>
 static yl_status launch_plan(yl_ctx* ctx, const View* views, int nviews, const float* w, int w_rows,
                              int w_cols, ConvPlan& p, int nphase, const ConvEpilogue& e) {
-  using Cfg = TileCfg<BN>;
+  using Cfg = FpropCfg<BN, MT>;
   CUtensorMap ta[4], tw;
   for (int i = 0; i < 4; ++i)
-    YL_TRY(make_view_tmap(&ta[i], views[i < nviews ? i : 0], 32, 4, CU_TENSOR_MAP_SWIZZLE_128B));
+    YL_TRY(make_view_tmap(&ta[i], views[i < nviews ? i : 0], 32, 4 * MT,
+                          CU_TENSOR_MAP_SWIZZLE_128B));
   YL_TRY(make_weight_tmap(&tw, w, w_rows, w_cols, BN));
   p.tiles_x = (p.gw + 31) / 32;
-  p.tiles_y = (p.gh + 3) / 4;
-  YL_CUDA(cudaFuncSetAttribute(conv_tma_fprop_kernel<BN>,
+  p.tiles_y = (p.gh + 4 * MT - 1) / (4 * MT);
+  p.n_nblk = (e.n_total + BN - 1) / BN;
+  p.pix_tiles = p.tiles_x * p.tiles_y * p.n_img;
+  const long long tiles = (long long)p.pix_tiles * p.n_nblk * nphase;
+  YL_CHECK(tiles > 0 && tiles < (1LL << 31), YL_ERR_SHAPE, "conv: %lld tiles", tiles);
+  p.n_tiles = (int)tiles;
+  YL_CUDA(cudaFuncSetAttribute(conv_tma_fprop_kernel<BN, MT>,
                                cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes));
-  dim3 grid(p.tiles_x * p.tiles_y * p.n_img, (e.n_total + BN - 1) / BN, nphase);
-  conv_tma_fprop_kernel<BN><<<grid, kThreads, Cfg::kSmemBytes, ctx->stream>>>(
+  const int grid = p.n_tiles < ctx->num_sms ? p.n_tiles : ctx->num_sms;
+  conv_tma_fprop_kernel<BN, MT><<<grid, kThreads, Cfg::kSmemBytes, ctx->stream>>>(
       ta[0], ta[1], ta[2], ta[3], tw, p, e, ctx->dev_err);
   return check_launch("conv_tma_fprop_kernel");
 }
 
+// Tile choice: BN covers the output channels in as few blocks as possible;
+// two M subtiles when BN <= 128 and the lattice is tall enough that 8-row
+// tiles waste little of the last tile row.
 static yl_status run_plan(yl_ctx* ctx, const View* views, int nviews, const float* w, int w_rows,
                           int w_cols, ConvPlan& p, int nphase, const ConvEpilogue& e) {
-  if (e.n_total <= 32) return launch_plan<32>(ctx, views, nviews, w, w_rows, w_cols, p, nphase, e);
-  if (e.n_total <= 64) return launch_plan<64>(ctx, views, nviews, w, w_rows, w_cols, p, nphase, e);
-  if (e.n_total <= 128 || e.n_total % 256 != 0)
-    return launch_plan<128>(ctx, views, nviews, w, w_rows, w_cols, p, nphase, e);
-  return launch_plan<256>(ctx, views, nviews, w, w_rows, w_cols, p, nphase, e);
+  const bool tall = p.gh % 8 == 0 || p.gh >= 64;
+  if (e.n_total <= 32) return launch_plan<32, 1>(ctx, views, nviews, w, w_rows, w_cols, p, nphase, e);
+  if (e.n_total <= 64) {
+    if (tall) return launch_plan<64, 2>(ctx, views, nviews, w, w_rows, w_cols, p, nphase, e);
+    return launch_plan<64, 1>(ctx, views, nviews, w, w_rows, w_cols, p, nphase, e);
+  }
+  if (e.n_total <= 128 || e.n_total % 256 != 0) {
+    if (tall) return launch_plan<128, 2>(ctx, views, nviews, w, w_rows, w_cols, p, nphase, e);
+    return launch_plan<128, 1>(ctx, views, nviews, w, w_rows, w_cols, p, nphase, e);
+  }
+  return launch_plan<256, 1>(ctx, views, nviews, w, w_rows, w_cols, p, nphase, e);
 }
 
 // Source extent of a gather (the physical tensor the gather reads).
