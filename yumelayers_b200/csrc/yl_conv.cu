@@ -461,18 +461,6 @@ yl_status conv_fprop_gather(yl_ctx* ctx, const ConvGather& g, const float* w, in
   return launch_gemm<256>(ctx, g, w, n_rows, e);
 }
 
-int conv_wgrad_pick_splits(yl_ctx* ctx, int cout, int k_total, int m_total) {
-  const int BN = 128;
-  long long tiles = (long long)((cout + kBM - 1) / kBM) * ((k_total + BN - 1) / BN);
-  long long target = 2LL * ctx->num_sms;
-  long long kblocks = (m_total + kBK - 1) / kBK;
-  long long splits = (target + tiles - 1) / tiles;
-  // keep at least 8 k-blocks of work per split
-  splits = std::min(splits, std::max(1LL, kblocks / 8));
-  splits = std::max(1LL, std::min(splits, 512LL));
-  return (int)splits;
-}
-
 yl_status conv_wgrad_gather(yl_ctx* ctx, const float* dy, int ldy, int cout,
                             const ConvGather& g, float* dw, int accumulate, float* ws,
                             int splits) {

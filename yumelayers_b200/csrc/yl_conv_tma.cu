@@ -294,10 +294,62 @@ struct WgradPlan {
   long long ws_split_stride;
 };
 
-// A = dy^T (4 atoms of 32 output channels), B = the input tile this CTA's tap
-// reads (BN/32 atoms of 32 input channels); k-blocks are 32 lattice columns of
-// one lattice row.  Both operands MN-major in SWIZZLE_128B_ATOM_32B.
-template <int BN>
+// dW tile: MT x 128 output channels (rows) by NSUB x NW columns of
+// [tap][cin]; k-blocks are BKP lattice columns of one lattice row.  A = dy
+// (MT*4 atoms of 32 output channels), B = the input pixels each column's tap
+// reads (NSUB*NW/32 atoms of 32 input channels, a tile may span several
+// taps); both MN-major in SWIZZLE_128B_ATOM_32B.  MT = 2 shares every B atom
+// between two M=128 accumulators, NSUB = 2 shares every A atom between two
+// MMAs: both raise the MMA work per byte brought in from L2.
+template <int MT, int NSUB, int NW, int BKP>
+struct WgradCfg {
+  static constexpr int kAtomBytes = BKP * 128;
+  static constexpr int kBN = NSUB * NW;
+  static constexpr int kAAtoms = MT * 4;
+  static constexpr int kBAtoms = kBN / 32;
+  static constexpr int kATile = kAAtoms * kAtomBytes;
+  static constexpr int kStage = kATile + kBAtoms * kAtomBytes;
+  static constexpr int kStages = (200 * 1024) / kStage > 8 ? 8 : (200 * 1024) / kStage;
+  static constexpr int kCols = MT * kBN;
+  static constexpr int kTmemCols =
+      kCols <= 32 ? 32 : kCols <= 64 ? 64 : kCols <= 128 ? 128 : kCols <= 256 ? 256 : 512;
+  static constexpr int kSmemBytes = kStages * kStage + (2 * kStages + 2) * 8 + 16 + 1024;
+  static_assert(NW % 32 == 0 && NW >= 32 && NW <= 256, "MMA N");
+  static_assert(kCols <= 512, "accumulators exceed TMEM");
+  static_assert(BKP % 8 == 0, "k-block is whole K=8 MMA steps");
+};
+
+// Where B atom j of a tile reads: which input view and the lattice offset of
+// its tap (for an upsample conv the offset also depends on the dy phase kp).
+struct WgAtom {
+  int8_t map, by, bx;
+  int ci;
+};
+
+__device__ __forceinline__ WgAtom wgrad_atom(const WgradPlan& w, int n, int kp) {
+  WgAtom a;
+  const int tap = n / w.cin;
+  a.ci = n - tap * w.cin;
+  const int ky = tap / w.ksize, kx = tap - (tap / w.ksize) * w.ksize;
+  if (w.mode == WG_PLAIN) {
+    a.map = 0;
+    a.by = (int8_t)(ky - w.pad);
+    a.bx = (int8_t)(kx - w.pad);
+  } else if (w.mode == WG_STRIDE2) {
+    const int ry = ky - w.pad, rx = kx - w.pad;
+    a.map = (int8_t)(((ry & 1) << 1) | (rx & 1));
+    a.by = (int8_t)(ry >> 1);
+    a.bx = (int8_t)(rx >> 1);
+  } else {  // WG_UP: dy phase kp = (pa, pb) reads source rows (pa + ky - pad) >> 1
+    const int pa = kp >> 1, pb = kp & 1;
+    a.map = 0;
+    a.by = (int8_t)((pa + ky - w.pad) >> 1);
+    a.bx = (int8_t)((pb + kx - w.pad) >> 1);
+  }
+  return a;
+}
+
+template <int MT, int NSUB, int NW, int BKP>
 __global__ void __launch_bounds__(kThreads, 1)
     conv_tma_wgrad_kernel(const __grid_constant__ CUtensorMap ta0,
                           const __grid_constant__ CUtensorMap ta1,
@@ -307,19 +359,17 @@ __global__ void __launch_bounds__(kThreads, 1)
                           const __grid_constant__ CUtensorMap tb1,
                           const __grid_constant__ CUtensorMap tb2,
                           const __grid_constant__ CUtensorMap tb3, WgradPlan w, int* err) {
-  using Cfg = TileCfg<BN>;
+  using Cfg = WgradCfg<MT, NSUB, NW, BKP>;
   constexpr int S = Cfg::kStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * Cfg::kStageBytes);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * Cfg::kStage);
   uint64_t* empty = full + S;
   uint64_t* accum = empty + S;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int m0 = blockIdx.x * kBM, n0 = blockIdx.y * BN;
-  const int tap = n0 / w.cin, ci0 = n0 - tap * w.cin;
-  const int ky = tap / w.ksize, kx = tap - (tap / w.ksize) * w.ksize;
+  const int m0 = blockIdx.x * (MT * kBM), n0 = blockIdx.y * Cfg::kBN;
   const long long b_begin = blockIdx.z * w.per_split;
   const long long b_end = min(w.blocks, b_begin + w.per_split);
   const int nk = b_end > b_begin ? (int)(b_end - b_begin) : 0;
@@ -352,39 +402,27 @@ __global__ void __launch_bounds__(kThreads, 1)
       r /= w.xblocks;
       int gy = (int)(r % w.gh);
       int im = (int)(r / w.gh);
+      WgAtom at[Cfg::kBAtoms];
+#pragma unroll
+      for (int j = 0; j < Cfg::kBAtoms; ++j) at[j] = wgrad_atom(w, n0 + 32 * j, kp);
       for (int kb = 0; kb < nk; ++kb) {
         const int s = kb % S;
         if (kb >= S && !mbar_wait(&empty[s], ((kb / S) - 1) & 1)) {
           report_error(err, YL_DEVERR_TIMEOUT);
           break;
         }
-        // which views and offsets this k-block reads
-        int amap = 0, bmap = 0, by, bx;
-        if (w.mode == WG_PLAIN) {
-          by = ky - w.pad;
-          bx = kx - w.pad;
-        } else if (w.mode == WG_STRIDE2) {
-          const int ry = ky - w.pad, rx = kx - w.pad;
-          bmap = ((ry & 1) << 1) | (rx & 1);
-          by = ry >> 1;
-          bx = rx >> 1;
-        } else {  // WG_UP: k-phase kp = (a, b) of the output gradient
-          const int a = kp >> 1, bb = kp & 1;
-          amap = kp;
-          by = (a + ky - w.pad) >> 1;
-          bx = (bb + kx - w.pad) >> 1;
-        }
-        const uint32_t a_dst = smem_u32(smem + s * Cfg::kStageBytes);
-        const uint32_t b_dst = a_dst + kATileBytes;
-        const int gx0 = xb * 32;
-        mbar_arrive_expect_tx(&full[s], kATileBytes + Cfg::kBTileBytes);
+        const uint32_t a_dst = smem_u32(smem + s * Cfg::kStage);
+        const uint32_t b_dst = a_dst + Cfg::kATile;
+        const int gx0 = xb * BKP;
+        const CUtensorMap* amap = amaps[w.mode == WG_UP ? kp : 0];
+        mbar_arrive_expect_tx(&full[s], Cfg::kStage);
 #pragma unroll
-        for (int a = 0; a < 4; ++a)
-          tma_load_4d(a_dst + a * 4096, amaps[amap], &full[s], m0 + 32 * a, gx0, gy, im);
+        for (int a = 0; a < Cfg::kAAtoms; ++a)
+          tma_load_4d(a_dst + a * Cfg::kAtomBytes, amap, &full[s], m0 + 32 * a, gx0, gy, im);
 #pragma unroll
-        for (int a = 0; a < BN / 32; ++a)
-          tma_load_4d(b_dst + a * 4096, bmaps[bmap], &full[s], ci0 + 32 * a, gx0 + bx, gy + by,
-                      im);
+        for (int j = 0; j < Cfg::kBAtoms; ++j)
+          tma_load_4d(b_dst + j * Cfg::kAtomBytes, bmaps[at[j].map], &full[s], at[j].ci,
+                      gx0 + at[j].bx, gy + at[j].by, im);
         if (++xb == w.xblocks) {
           xb = 0;
           if (++gy == w.gh) {
@@ -392,6 +430,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (++im == w.n_img) {
               im = 0;
               ++kp;
+              if (w.mode == WG_UP && kp < w.nkp) {
+#pragma unroll
+                for (int j = 0; j < Cfg::kBAtoms; ++j) at[j] = wgrad_atom(w, n0 + 32 * j, kp);
+              }
             }
           }
         }
@@ -399,7 +441,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 5) {
     if (lane == 0) {
-      constexpr uint32_t idesc = idesc_tf32(kBM, BN, 1, 1);
+      constexpr uint32_t idesc = idesc_tf32(kBM, NW, 1, 1);
       for (int kb = 0; kb < nk; ++kb) {
         const int s = kb % S;
         if (!mbar_wait(&full[s], (kb / S) & 1)) {
@@ -407,12 +449,22 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         tc_fence_after();
-        const uint32_t a_addr = smem_u32(smem + s * Cfg::kStageBytes);
-        const uint32_t b_addr = a_addr + kATileBytes;
+        const uint32_t a_addr = smem_u32(smem + s * Cfg::kStage);
+        const uint32_t b_addr = a_addr + Cfg::kATile;
 #pragma unroll
-        for (int kk = 0; kk < kBK / 8; ++kk)
-          umma_tf32(tmem, sw128b32_desc(a_addr + kk * 1024, 4096, 512),
-                    sw128b32_desc(b_addr + kk * 1024, 4096, 512), idesc, (kb | kk) != 0);
+        for (int kk = 0; kk < BKP / 8; ++kk) {
+#pragma unroll
+          for (int m = 0; m < MT; ++m) {
+            const uint64_t adesc =
+                sw128b32_desc(a_addr + m * 4 * Cfg::kAtomBytes + kk * 1024, Cfg::kAtomBytes, 512);
+#pragma unroll
+            for (int j = 0; j < NSUB; ++j)
+              umma_tf32(tmem + (uint32_t)(m * Cfg::kBN + j * NW), adesc,
+                        sw128b32_desc(b_addr + j * (NW / 32) * Cfg::kAtomBytes + kk * 1024,
+                                      Cfg::kAtomBytes, 512),
+                        idesc, (kb | kk) != 0);
+          }
+        }
         umma_commit(&empty[s]);
       }
       umma_commit(accum);
@@ -423,26 +475,29 @@ __global__ void __launch_bounds__(kThreads, 1)
     const bool got = mbar_wait(accum, 0);
     if (!got) report_error(err, YL_DEVERR_TIMEOUT);
     tc_fence_after();
-    const int co = m0 + warp * 32 + lane;
-    const bool rval = got && co < w.cout;
-    float* dst = w.ws + (long long)blockIdx.z * w.ws_split_stride + (long long)co * w.n_total;
 #pragma unroll 1
-    for (int c0 = 0; c0 < BN; c0 += 32) {
-      if (n0 + c0 >= w.n_total) break;
-      uint32_t r[32];
-      tmem_ld_32x32b_x32(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0, r);
-      tmem_ld_wait();
-      if (!rval) continue;
-      const int nb = n0 + c0;
-      if (nk == 0) {
+    for (int m = 0; m < MT; ++m) {
+      const int co = m0 + m * kBM + warp * 32 + lane;
+      const bool rval = got && co < w.cout;
+      float* dst = w.ws + (long long)blockIdx.z * w.ws_split_stride + (long long)co * w.n_total;
+#pragma unroll 1
+      for (int c0 = 0; c0 < Cfg::kBN; c0 += 32) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)(m * Cfg::kBN + c0),
+                           r);
+        tmem_ld_wait();
+        if (!rval) continue;
+        if (nk == 0) {
 #pragma unroll
-        for (int q = 0; q < 32; ++q) r[q] = 0u;
+          for (int q = 0; q < 32; ++q) r[q] = 0u;
+        }
+        const int nb = n0 + c0;
+#pragma unroll
+        for (int q = 0; q < 32; q += 4)
+          *reinterpret_cast<float4*>(dst + nb + q) =
+              make_float4(__uint_as_float(r[q]), __uint_as_float(r[q + 1]),
+                          __uint_as_float(r[q + 2]), __uint_as_float(r[q + 3]));
       }
-#pragma unroll
-      for (int q = 0; q < 32; q += 4)
-        *reinterpret_cast<float4*>(dst + nb + q) =
-            make_float4(__uint_as_float(r[q]), __uint_as_float(r[q + 1]),
-                        __uint_as_float(r[q + 2]), __uint_as_float(r[q + 3]));
     }
   }
 
@@ -538,15 +593,15 @@ static View phase_view(const float* p, int c, int w, int h, int n, int ps, int a
               2LL * ps, 2LL * w * ps, (long long)h * w * ps};
 }
 
-static yl_status make_view_tmap(CUtensorMap* tm, const View& v, int box_w, int box_h,
-                                CUtensorMapSwizzle swz) {
+static yl_status make_view_tmap(CUtensorMap* tm, const View& v, int box_c, int box_h,
+                                CUtensorMapSwizzle swz, int box_w = 32) {
   auto fn = get_encode_fn();
   YL_CHECK(fn, YL_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
   YL_CHECK(((uintptr_t)v.base & 15) == 0 && v.sx % 4 == 0 && v.w >= 1 && v.h >= 1, YL_ERR_INVALID,
            "view tensor map: alignment / extent");
   cuuint64_t dims[4] = {(cuuint64_t)v.c, (cuuint64_t)v.w, (cuuint64_t)v.h, (cuuint64_t)v.n};
   cuuint64_t strides[3] = {(cuuint64_t)v.sx * 4, (cuuint64_t)v.sy * 4, (cuuint64_t)v.sn * 4};
-  cuuint32_t box[4] = {32, (cuuint32_t)box_w, (cuuint32_t)box_h, 1};
+  cuuint32_t box[4] = {(cuuint32_t)box_c, (cuuint32_t)box_w, (cuuint32_t)box_h, 1};
   cuuint32_t estr[4] = {1, 1, 1, 1};
   CUresult r = fn(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, const_cast<float*>(v.base), dims,
                   strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
@@ -717,15 +772,66 @@ yl_status conv_fprop(yl_ctx* ctx, const ConvGather& g, const float* w, int n_row
   return conv_fprop_gather(ctx, g, w, n_rows, e);
 }
 
+// Tile shape of the TMA wgrad for a cout x n_total filter gradient
+// (n_total = taps * cin); mt = 0 means no TMA tile divides n_total.
+struct WgTile {
+  int mt, nsub, nw, bkp;
+  int bn() const { return nsub * nw; }
+};
+
+static WgTile wgrad_tile(int cout, int n_total) {
+  if (cout % 256 == 0 && n_total % 256 == 0) return {2, 1, 256, 16};
+  if (n_total % 384 == 0) return {1, 2, 192, 16};
+  if (n_total % 256 == 0) return {1, 1, 256, 16};
+  if (n_total % 128 == 0) return {1, 1, 128, 32};
+  return {0, 0, 0, 0};
+}
+
+// Split-K factor: one wave of CTAs (tiles * splits <= SM count), at least
+// four k-blocks per split.
+int conv_wgrad_pick_splits(yl_ctx* ctx, int cout, int k_total, int m_total) {
+  WgTile t = wgrad_tile(cout, k_total);
+  if (!t.mt) t = {1, 1, 128, 32};
+  const long long tiles =
+      (long long)((cout + t.mt * kBM - 1) / (t.mt * kBM)) * ((k_total + t.bn() - 1) / t.bn());
+  const long long kblocks = ((long long)m_total + t.bkp - 1) / t.bkp;
+  long long splits = std::max(1LL, ctx->num_sms / tiles);
+  splits = std::min(splits, std::max(1LL, kblocks / 4));
+  return (int)std::min(splits, 512LL);
+}
+
+template <int MT, int NSUB, int NW, int BKP>
+static yl_status launch_wgrad(yl_ctx* ctx, const View* av, int nav, const View* bv, int nbv,
+                              WgradPlan& w, int splits) {
+  using Cfg = WgradCfg<MT, NSUB, NW, BKP>;
+  CUtensorMap ta[4], tb[4];
+  for (int i = 0; i < 4; ++i) {
+    YL_TRY(make_view_tmap(&ta[i], av[i < nav ? i : 0], 32, 1,
+                          CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B, BKP));
+    YL_TRY(make_view_tmap(&tb[i], bv[i < nbv ? i : 0], 32, 1,
+                          CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B, BKP));
+  }
+  w.xblocks = (w.gw + BKP - 1) / BKP;
+  w.blocks_per_kp = (long long)w.n_img * w.gh * w.xblocks;
+  w.blocks = w.blocks_per_kp * w.nkp;
+  w.per_split = (w.blocks + splits - 1) / splits;
+  YL_CUDA(cudaFuncSetAttribute(conv_tma_wgrad_kernel<MT, NSUB, NW, BKP>,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes));
+  dim3 grid((w.cout + MT * kBM - 1) / (MT * kBM), w.n_total / Cfg::kBN, splits);
+  conv_tma_wgrad_kernel<MT, NSUB, NW, BKP><<<grid, kThreads, Cfg::kSmemBytes, ctx->stream>>>(
+      ta[0], ta[1], ta[2], ta[3], tb[0], tb[1], tb[2], tb[3], w, ctx->dev_err);
+  return check_launch("conv_tma_wgrad_kernel");
+}
+
 yl_status conv_wgrad_ws(yl_ctx* ctx, const float* dy, int ldy, int cout, const ConvGather& g,
                         float* dw, int accumulate, float* ws, int splits) {
-  constexpr int BN = 128;
-  using Cfg = TileCfg<BN>;
   int sw = 0, sh = 0;
   const bool k3p1 = g.ksize == 3 && g.pad == 1;
-  const bool base_ok = g.cin % BN == 0 && g.m_total > 0 && g.m_total % (g.oh * g.ow) == 0 &&
-                       ((uintptr_t)g.src & 15) == 0 && ((uintptr_t)dy & 15) == 0 &&
-                       g.ps % 4 == 0 && ldy % 4 == 0 && source_dims(g, &sw, &sh) && splits >= 1;
+  const WgTile tile = wgrad_tile(cout, g.k_total);
+  const bool base_ok = tile.mt > 0 && g.cin % 32 == 0 && g.m_total > 0 &&
+                       g.m_total % (g.oh * g.ow) == 0 && ((uintptr_t)g.src & 15) == 0 &&
+                       ((uintptr_t)dy & 15) == 0 && g.ps % 4 == 0 && ldy % 4 == 0 &&
+                       source_dims(g, &sw, &sh) && splits >= 1;
   int mode = -1;
   if (base_ok) {
     if (g.stride == 1 && !g.up && sw == g.wv && sh == g.hv) mode = WG_PLAIN;
@@ -746,6 +852,7 @@ yl_status conv_wgrad_ws(yl_ctx* ctx, const float* dy, int ldy, int cout, const C
   w.cin = g.cin;
   w.cout = cout;
   w.n_total = g.k_total;
+  w.n_img = n_img;
   if (mode == WG_UP) {
     for (int ph = 0; ph < 4; ++ph)
       av[ph] = phase_view(dy, cout, g.ow, g.oh, n_img, ldy, ph >> 1, ph & 1);
@@ -768,24 +875,12 @@ yl_status conv_wgrad_ws(yl_ctx* ctx, const float* dy, int ldy, int cout, const C
     w.gh = g.oh;
     w.gw = g.ow;
   }
-  w.xblocks = (w.gw + 31) / 32;
-  w.n_img = n_img;
-  w.blocks_per_kp = (long long)n_img * w.gh * w.xblocks;
-  w.blocks = w.blocks_per_kp * w.nkp;
-  w.per_split = (w.blocks + splits - 1) / splits;
   w.ws = ws;
   w.ws_split_stride = (long long)cout * g.k_total;
-  CUtensorMap ta[4], tb[4];
-  for (int i = 0; i < 4; ++i) {
-    YL_TRY(make_view_tmap(&ta[i], av[i < nav ? i : 0], 32, 1, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B));
-    YL_TRY(make_view_tmap(&tb[i], bv[i < nbv ? i : 0], 32, 1, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B));
-  }
-  YL_CUDA(cudaFuncSetAttribute(conv_tma_wgrad_kernel<BN>,
-                               cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes));
-  dim3 grid((cout + kBM - 1) / kBM, g.k_total / BN, splits);
-  conv_tma_wgrad_kernel<BN><<<grid, kThreads, Cfg::kSmemBytes, ctx->stream>>>(
-      ta[0], ta[1], ta[2], ta[3], tb[0], tb[1], tb[2], tb[3], w, ctx->dev_err);
-  YL_TRY(check_launch("conv_tma_wgrad_kernel"));
+  if (tile.mt == 2) YL_TRY((launch_wgrad<2, 1, 256, 16>(ctx, av, nav, bv, nbv, w, splits)));
+  else if (tile.nsub == 2) YL_TRY((launch_wgrad<1, 2, 192, 16>(ctx, av, nav, bv, nbv, w, splits)));
+  else if (tile.nw == 256) YL_TRY((launch_wgrad<1, 1, 256, 16>(ctx, av, nav, bv, nbv, w, splits)));
+  else YL_TRY((launch_wgrad<1, 1, 128, 32>(ctx, av, nav, bv, nbv, w, splits)));
   const long long n = (long long)cout * g.k_total;
   splitk_reduce_kernel<<<grid_1d(n / 4 + 1, 256), 256, 0, ctx->stream>>>(ws, splits, n, dw, n,
                                                                          accumulate);
