@@ -290,6 +290,7 @@ struct WgradPlan {
   int n_img;
   long long blocks_per_kp, blocks, per_split;
   int ksize, pad, cin, cout, n_total;
+  int ga, gb;             // 32-channel atoms per A (dy) / B (input) TMA box
   float* ws;
   long long ws_split_stride;
 };
@@ -416,13 +417,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int gx0 = xb * BKP;
         const CUtensorMap* amap = amaps[w.mode == WG_UP ? kp : 0];
         mbar_arrive_expect_tx(&full[s], Cfg::kStage);
-#pragma unroll
-        for (int a = 0; a < Cfg::kAAtoms; ++a)
-          tma_load_4d(a_dst + a * Cfg::kAtomBytes, amap, &full[s], m0 + 32 * a, gx0, gy, im);
-#pragma unroll
-        for (int j = 0; j < Cfg::kBAtoms; ++j)
-          tma_load_4d(b_dst + j * Cfg::kAtomBytes, bmaps[at[j].map], &full[s], at[j].ci,
-                      gx0 + at[j].bx, gy + at[j].by, im);
+        for (int a = 0; a < Cfg::kAAtoms; a += w.ga)
+          tma_load_5d(a_dst + a * Cfg::kAtomBytes, amap, &full[s], 0, gx0, gy, m0 / 32 + a, im);
+        for (int j = 0; j < Cfg::kBAtoms; j += w.gb)
+          tma_load_5d(b_dst + j * Cfg::kAtomBytes, bmaps[at[j].map], &full[s], 0,
+                      gx0 + at[j].bx, gy + at[j].by, at[j].ci / 32, im);
         if (++xb == w.xblocks) {
           xb = 0;
           if (++gy == w.gh) {
@@ -607,6 +606,32 @@ static yl_status make_view_tmap(CUtensorMap* tm, const View& v, int box_c, int b
                   strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   YL_CHECK(r == CUDA_SUCCESS, YL_ERR_CUDA, "cuTensorMapEncodeTiled (view) failed (%d)", (int)r);
+  return YL_OK;
+}
+
+// 5-D map of a view split into 32-channel atoms {32, w, h, atoms, n}; a box
+// is `atoms` whole atoms of box_w pixels of one row, stored atom after atom
+// (the MN-major operand layout).  A view with fewer than 32 channels is one
+// partial atom (the rest of the box reads as zero); otherwise the channel
+// count must be a multiple of 32.
+static yl_status make_atom_tmap(CUtensorMap* tm, const View& v, int box_w, int atoms,
+                                CUtensorMapSwizzle swz) {
+  auto fn = get_encode_fn();
+  YL_CHECK(fn, YL_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
+  YL_CHECK(((uintptr_t)v.base & 15) == 0 && v.sx % 4 == 0 && v.w >= 1 && v.h >= 1 &&
+               (v.c <= 32 || v.c % 32 == 0) && v.c % 4 == 0,
+           YL_ERR_INVALID, "atom tensor map: alignment / extent");
+  const int c0 = v.c < 32 ? v.c : 32;
+  cuuint64_t dims[5] = {(cuuint64_t)c0, (cuuint64_t)v.w, (cuuint64_t)v.h,
+                        (cuuint64_t)((v.c + 31) / 32), (cuuint64_t)v.n};
+  cuuint64_t strides[4] = {(cuuint64_t)v.sx * 4, (cuuint64_t)v.sy * 4, 128,
+                           (cuuint64_t)v.sn * 4};
+  cuuint32_t box[5] = {32, (cuuint32_t)box_w, 1, (cuuint32_t)atoms, 1};
+  cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+  CUresult r = fn(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 5, const_cast<float*>(v.base), dims,
+                  strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  YL_CHECK(r == CUDA_SUCCESS, YL_ERR_CUDA, "cuTensorMapEncodeTiled (atoms) failed (%d)", (int)r);
   return YL_OK;
 }
 
@@ -804,12 +829,16 @@ template <int MT, int NSUB, int NW, int BKP>
 static yl_status launch_wgrad(yl_ctx* ctx, const View* av, int nav, const View* bv, int nbv,
                               WgradPlan& w, int splits) {
   using Cfg = WgradCfg<MT, NSUB, NW, BKP>;
+  // A box: all of the tile's dy atoms at once when cout is whole atoms; B box:
+  // four atoms (128 input channels of one tap) when the taps allow it
+  w.ga = w.cout % 32 == 0 ? Cfg::kAAtoms : 1;
+  w.gb = (w.cin / 32) % 4 == 0 && Cfg::kBAtoms % 4 == 0 ? 4 : 1;
   CUtensorMap ta[4], tb[4];
   for (int i = 0; i < 4; ++i) {
-    YL_TRY(make_view_tmap(&ta[i], av[i < nav ? i : 0], 32, 1,
-                          CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B, BKP));
-    YL_TRY(make_view_tmap(&tb[i], bv[i < nbv ? i : 0], 32, 1,
-                          CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B, BKP));
+    YL_TRY(make_atom_tmap(&ta[i], av[i < nav ? i : 0], BKP, w.ga,
+                          CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B));
+    YL_TRY(make_atom_tmap(&tb[i], bv[i < nbv ? i : 0], BKP, w.gb,
+                          CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B));
   }
   w.xblocks = (w.gw + BKP - 1) / BKP;
   w.blocks_per_kp = (long long)w.n_img * w.gh * w.xblocks;
@@ -828,7 +857,8 @@ yl_status conv_wgrad_ws(yl_ctx* ctx, const float* dy, int ldy, int cout, const C
   int sw = 0, sh = 0;
   const bool k3p1 = g.ksize == 3 && g.pad == 1;
   const WgTile tile = wgrad_tile(cout, g.k_total);
-  const bool base_ok = tile.mt > 0 && g.cin % 32 == 0 && g.m_total > 0 &&
+  const bool base_ok = tile.mt > 0 && g.cin % 32 == 0 && (cout <= 32 || cout % 32 == 0) &&
+                       cout % 4 == 0 && g.m_total > 0 &&
                        g.m_total % (g.oh * g.ow) == 0 && ((uintptr_t)g.src & 15) == 0 &&
                        ((uintptr_t)dy & 15) == 0 && g.ps % 4 == 0 && ldy % 4 == 0 &&
                        source_dims(g, &sw, &sh) && splits >= 1;
