@@ -49,7 +49,7 @@ def test_noalloc_matches_allocating_entry_point_twice(ctx, n, c, h, w, g):
 
 
 def test_noalloc_rejects_requests_above_its_fixed_scratch(ctx):
-    # 1024 groups on two images need 2 * 297 * 2 * 1024 doubles > 131072
+    # 1024 groups on two 64x64 images need 2 * 256 * 2 * 1024 doubles > 131072
     n, c, h, w, g = 2, 4096, 64, 64, 1024
     x = GPUTensor(ctx, 1, n * h * w * c)
     y = GPUTensor(ctx, 1, n * h * w * c)

@@ -19,6 +19,7 @@
 //           (2) dx = rstd*(dxh - mean(dxh) - xh*mean(dxh*xh)) (+ addend).
 // Memory traffic per element: forward 2 reads + 1 write, backward 4 reads +
 // 1 write (+1 read for the addend).
+#include <algorithm>
 #include <mutex>
 
 #include "yl_kernels.h"
@@ -29,12 +30,21 @@ namespace yl {
 
 __device__ __forceinline__ float silu_f(float a) { return a / (1.f + __expf(-a)); }
 
+// Launch geometry shared by all GroupNorm kernels.  A block is quads x rows
+// threads; thread (quad, row) owns channels [4*quad, 4*quad+4) and walks the
+// pixels p0 + row, p0 + row + rows, ... of its block's chunk, so every
+// per-channel constant (group statistics, gamma, beta) is loop-invariant and
+// no index needs a division.  Reductions use `chunks` pixel chunks per image
+// (one wave of 4 blocks per SM over all images, at least 16 pixels per
+// thread); the elementwise passes use `achunks`.
 struct GnGeom {
   int n, c, g, ps;
   long long hw;
-  int chunks;
-  int quads, rows;  // block = quads * rows threads
+  int chunks, achunks;
+  int quads, rows;
 };
+
+constexpr int kGnBlocksPerWave = 148 * 4;
 
 static GnGeom gn_geom(int n, int c, int g, long long hw, int ps) {
   GnGeom q;
@@ -45,15 +55,23 @@ static GnGeom gn_geom(int n, int c, int g, long long hw, int ps) {
   q.hw = hw;
   q.quads = c / 4;
   q.rows = q.quads >= 256 ? 1 : 256 / q.quads;
-  long long per_img_threads = (long long)q.rows;
-  long long chunks = (hw + 4 * per_img_threads - 1) / (4 * per_img_threads);  // >= 4 px per thread
-  if (chunks > 148 * 4 / (n > 0 ? n : 1) + 1) chunks = 148 * 4 / (n > 0 ? n : 1) + 1;
-  if (chunks < 1) chunks = 1;
-  q.chunks = (int)chunks;
+  const long long per_img = n > 0 ? n : 1;
+  long long cap = hw / (16LL * q.rows);
+  if (cap < 1) cap = 1;
+  q.chunks = (int)std::max(1LL, std::min((long long)kGnBlocksPerWave / per_img, cap));
+  q.achunks = (int)std::max(1LL, std::min(2LL * kGnBlocksPerWave / per_img, cap));
   return q;
 }
 
-// partial[img][chunk][g] = (sum, sumsq)
+__device__ __forceinline__ void chunk_range(const GnGeom& q, int chunk, int nchunks, long long* p0,
+                                            long long* p1) {
+  const long long per = (q.hw + nchunks - 1) / nchunks;
+  *p0 = chunk * per;
+  *p1 = min(q.hw, *p0 + per);
+}
+
+// partial[img][chunk][g] = (sum, sumsq).  Four pixels per iteration are summed
+// in float, then added to the thread's double accumulators.
 __global__ void gn_stats_partial_kernel(const float* __restrict__ x, GnGeom q,
                                         double* __restrict__ part) {
   extern __shared__ double sh[];  // [g][2]
@@ -62,36 +80,63 @@ __global__ void gn_stats_partial_kernel(const float* __restrict__ x, GnGeom q,
   for (int i = t; i < 2 * q.g; i += blockDim.x) sh[i] = 0.0;
   __syncthreads();
   const int quad = t % q.quads, row = t / q.quads;
-  const int cg = q.c / q.g;
-  const int grp = (quad * 4) / cg;
-  const long long per = (q.hw + q.chunks - 1) / q.chunks;
-  const long long p0 = chunk * per, p1 = min(q.hw, p0 + per);
+  const int grp = (quad * 4) / (q.c / q.g);
+  long long p0, p1;
+  chunk_range(q, chunk, q.chunks, &p0, &p1);
   const float* base = x + (long long)img * q.hw * q.ps + quad * 4;
+  const long long step = (long long)q.rows * q.ps;
   double s = 0.0, ss = 0.0;
-  for (long long p = p0 + row; p < p1; p += q.rows) {
-    const float4 v = *reinterpret_cast<const float4*>(base + p * q.ps);
-    s += (double)v.x + (double)v.y + (double)v.z + (double)v.w;
-    ss += (double)v.x * v.x + (double)v.y * v.y + (double)v.z * v.z + (double)v.w * v.w;
+  long long p = p0 + row;
+  const float* xp = base + p * q.ps;
+  for (; p + 3LL * q.rows < p1; p += 4LL * q.rows, xp += 4 * step) {
+    const float4 a = __ldg(reinterpret_cast<const float4*>(xp));
+    const float4 b = __ldg(reinterpret_cast<const float4*>(xp + step));
+    const float4 c = __ldg(reinterpret_cast<const float4*>(xp + 2 * step));
+    const float4 d = __ldg(reinterpret_cast<const float4*>(xp + 3 * step));
+    const float fs = ((a.x + a.y) + (a.z + a.w)) + ((b.x + b.y) + (b.z + b.w)) +
+                     ((c.x + c.y) + (c.z + c.w)) + ((d.x + d.y) + (d.z + d.w));
+    const float fq = ((a.x * a.x + a.y * a.y) + (a.z * a.z + a.w * a.w)) +
+                     ((b.x * b.x + b.y * b.y) + (b.z * b.z + b.w * b.w)) +
+                     ((c.x * c.x + c.y * c.y) + (c.z * c.z + c.w * c.w)) +
+                     ((d.x * d.x + d.y * d.y) + (d.z * d.z + d.w * d.w));
+    s += fs;
+    ss += fq;
   }
-  atomicAdd(&sh[2 * grp], s);
-  atomicAdd(&sh[2 * grp + 1], ss);
+  for (; p < p1; p += q.rows, xp += step) {
+    const float4 a = __ldg(reinterpret_cast<const float4*>(xp));
+    s += (double)((a.x + a.y) + (a.z + a.w));
+    ss += (double)((a.x * a.x + a.y * a.y) + (a.z * a.z + a.w * a.w));
+  }
+  if (p0 + row < p1) {
+    atomicAdd(&sh[2 * grp], s);
+    atomicAdd(&sh[2 * grp + 1], ss);
+  }
   __syncthreads();
   double* out = part + ((long long)img * q.chunks + chunk) * 2 * q.g;
   for (int i = t; i < 2 * q.g; i += blockDim.x) out[i] = sh[i];
 }
 
+// One warp per (image, group): lanes sum the chunk partials in a fixed
+// strided order, then a fixed shuffle tree (deterministic).
 __global__ void gn_stats_final_kernel(const double* __restrict__ part, GnGeom q, float eps,
                                       int mode, float* __restrict__ mean,
                                       float* __restrict__ rstd) {
-  const int idx = blockIdx.x * blockDim.x + threadIdx.x;  // img * g + grp
+  const int idx = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;  // img * g + grp
+  const int lane = threadIdx.x & 31;
   if (idx >= q.n * q.g) return;
   const int img = idx / q.g, grp = idx % q.g;
   double s = 0.0, ss = 0.0;
-  for (int k = 0; k < q.chunks; ++k) {
+  for (int k = lane; k < q.chunks; k += 32) {
     const double* pp = part + ((long long)img * q.chunks + k) * 2 * q.g;
     s += pp[2 * grp];
     ss += pp[2 * grp + 1];
   }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    s += __shfl_xor_sync(0xffffffffu, s, o);
+    ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  }
+  if (lane) return;
   const double cnt = (double)q.hw * (q.c / q.g);
   const double m = s / cnt;
   double var = ss / cnt - m * m;
@@ -107,35 +152,75 @@ __global__ void gn_stats_final_kernel(const double* __restrict__ part, GnGeom q,
   rstd[idx] = (float)r;
 }
 
+__device__ __forceinline__ float4 gn_act4(float4 v, const float (&sc)[4], const float (&sh)[4],
+                                          int silu, int round) {
+  float o[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    float a = fmaf(o[k], sc[k], sh[k]);
+    if (silu) a = silu_f(a);
+    o[k] = round ? round_tf32(a) : a;
+  }
+  return make_float4(o[0], o[1], o[2], o[3]);
+}
+
+// y = [silu]((x - mean) * rstd * gamma + beta) = [silu](x * scale + shift).
 __global__ void gn_apply_kernel(const float* __restrict__ x, GnGeom q,
                                 const float* __restrict__ mean, const float* __restrict__ rstd,
                                 const float* __restrict__ gamma, const float* __restrict__ beta,
                                 int silu, int round, float* __restrict__ y, int ldy) {
-  const long long total = (long long)q.n * q.hw * q.quads;
-  const int cg = q.c / q.g;
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
-       i += (long long)gridDim.x * blockDim.x) {
-    const int quad = (int)(i % q.quads);
-    const long long pix = i / q.quads;  // img * hw + p
-    const int img = (int)(pix / q.hw);
-    const int c = quad * 4;
-    const int grp = c / cg;
-    const float m = mean[img * q.g + grp], r = rstd[img * q.g + grp];
-    const float4 v = *reinterpret_cast<const float4*>(x + pix * q.ps + c);
-    float o[4] = {v.x, v.y, v.z, v.w};
+  const int img = blockIdx.y;
+  const int quad = threadIdx.x % q.quads, row = threadIdx.x / q.quads;
+  const int c = quad * 4;
+  const int gi = img * q.g + c / (q.c / q.g);
+  const float m = mean[gi], r = rstd[gi];
+  float sc[4], sf[4];
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      float a = (o[k] - m) * r;
-      if (gamma) a = a * __ldg(gamma + c + k);
-      if (beta) a = a + __ldg(beta + c + k);
-      if (silu) a = silu_f(a);
-      o[k] = round ? round_tf32(a) : a;
-    }
-    *reinterpret_cast<float4*>(y + pix * ldy + c) = make_float4(o[0], o[1], o[2], o[3]);
+  for (int k = 0; k < 4; ++k) {
+    const float ga = gamma ? __ldg(gamma + c + k) : 1.f;
+    const float be = beta ? __ldg(beta + c + k) : 0.f;
+    sc[k] = r * ga;
+    sf[k] = be - m * r * ga;
+  }
+  long long p0, p1;
+  chunk_range(q, blockIdx.x, q.achunks, &p0, &p1);
+  const float* xb = x + (long long)img * q.hw * q.ps + c;
+  float* yb = y + (long long)img * q.hw * ldy + c;
+  long long p = p0 + row;
+  const long long R = q.rows;
+  for (; p + R < p1; p += 2 * R) {
+    const float4 a = __ldg(reinterpret_cast<const float4*>(xb + p * q.ps));
+    const float4 b = __ldg(reinterpret_cast<const float4*>(xb + (p + R) * q.ps));
+    *reinterpret_cast<float4*>(yb + p * ldy) = gn_act4(a, sc, sf, silu, round);
+    *reinterpret_cast<float4*>(yb + (p + R) * ldy) = gn_act4(b, sc, sf, silu, round);
+  }
+  if (p < p1) {
+    const float4 a = __ldg(reinterpret_cast<const float4*>(xb + p * q.ps));
+    *reinterpret_cast<float4*>(yb + p * ldy) = gn_act4(a, sc, sf, silu, round);
   }
 }
 
-// Backward partials: per (img, chunk): group sums [g][2] then channel sums [c][2].
+// Per element of the backward: xh = (x - mean) * rstd, a = xh * gamma + beta,
+// da = dy * silu'(a) (or dy), dxh = da * gamma.
+struct GnBwdConst {
+  float m, r, ga[4], be[4];
+};
+
+__device__ __forceinline__ void gn_bwd_elem(float x, float dy, float ga, float be, float m, float r,
+                                            int silu, float* xh, float* da) {
+  *xh = (x - m) * r;
+  float d = dy;
+  if (silu) {
+    const float a = fmaf(*xh, ga, be);
+    const float sg = 1.f / (1.f + __expf(-a));
+    d *= sg * (1.f + a * (1.f - sg));
+  }
+  *da = d;
+}
+
+// Backward partials per (img, chunk): group sums [g][2] of (dxh, dxh*xh), then
+// channel sums [c][2] of (da*xh, da) for dgamma, dbeta.  Two pixels per
+// iteration are combined in float before the double accumulators.
 __global__ void gn_bwd_partial_kernel(const float* __restrict__ x, const float* __restrict__ dy,
                                       int lddy, GnGeom q, const float* __restrict__ mean,
                                       const float* __restrict__ rstd,
@@ -149,86 +234,106 @@ __global__ void gn_bwd_partial_kernel(const float* __restrict__ x, const float* 
   for (int i = t; i < nsh; i += blockDim.x) sh[i] = 0.0;
   __syncthreads();
   const int quad = t % q.quads, row = t / q.quads;
-  const int cg = q.c / q.g;
   const int c = quad * 4;
-  const int grp = c / cg;
+  const int grp = c / (q.c / q.g);
   const float m = mean[img * q.g + grp], r = rstd[img * q.g + grp];
   float ga[4], be[4];
 #pragma unroll
   for (int k = 0; k < 4; ++k) {
-    ga[k] = gamma ? gamma[c + k] : 1.f;
-    be[k] = beta ? beta[c + k] : 0.f;
+    ga[k] = gamma ? __ldg(gamma + c + k) : 1.f;
+    be[k] = beta ? __ldg(beta + c + k) : 0.f;
   }
-  const long long per = (q.hw + q.chunks - 1) / q.chunks;
-  const long long p0 = chunk * per, p1 = min(q.hw, p0 + per);
+  long long p0, p1;
+  chunk_range(q, chunk, q.chunks, &p0, &p1);
   const float* xb = x + (long long)img * q.hw * q.ps + c;
   const float* db = dy + (long long)img * q.hw * lddy + c;
   double sd = 0, sdx = 0, dg[4] = {0, 0, 0, 0}, dbt[4] = {0, 0, 0, 0};
-  for (long long p = p0 + row; p < p1; p += q.rows) {
-    const float4 xv = *reinterpret_cast<const float4*>(xb + p * q.ps);
-    const float4 dv = *reinterpret_cast<const float4*>(db + p * lddy);
-    const float xs[4] = {xv.x, xv.y, xv.z, xv.w};
-    const float ds[4] = {dv.x, dv.y, dv.z, dv.w};
+  const long long R = q.rows;
+  long long p = p0 + row;
+  for (; p < p1; p += 2 * R) {
+    const bool two = p + R < p1;
+    const float4 xa = __ldg(reinterpret_cast<const float4*>(xb + p * q.ps));
+    const float4 da4 = __ldg(reinterpret_cast<const float4*>(db + p * lddy));
+    float4 xb4 = make_float4(0.f, 0.f, 0.f, 0.f), db4 = xb4;
+    if (two) {
+      xb4 = __ldg(reinterpret_cast<const float4*>(xb + (p + R) * q.ps));
+      db4 = __ldg(reinterpret_cast<const float4*>(db + (p + R) * lddy));
+    }
+    const float x0[4] = {xa.x, xa.y, xa.z, xa.w}, d0[4] = {da4.x, da4.y, da4.z, da4.w};
+    const float x1[4] = {xb4.x, xb4.y, xb4.z, xb4.w}, d1[4] = {db4.x, db4.y, db4.z, db4.w};
+    float fsd = 0.f, fsdx = 0.f;
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
-      const float xh = (xs[k] - m) * r;
-      float da = ds[k];
-      if (silu) {
-        const float a = xh * ga[k] + be[k];
-        const float sg = 1.f / (1.f + __expf(-a));
-        da *= sg * (1.f + a * (1.f - sg));
-      }
-      dg[k] += (double)da * xh;
-      dbt[k] += da;
-      const float dxh = da * ga[k];
-      sd += dxh;
-      sdx += (double)dxh * xh;
+      float xh0, dd0, xh1 = 0.f, dd1 = 0.f;
+      gn_bwd_elem(x0[k], d0[k], ga[k], be[k], m, r, silu, &xh0, &dd0);
+      if (two) gn_bwd_elem(x1[k], d1[k], ga[k], be[k], m, r, silu, &xh1, &dd1);
+      const float gx = dd0 * xh0 + dd1 * xh1, gs = dd0 + dd1;
+      dg[k] += gx;
+      dbt[k] += gs;
+      fsd += gs * ga[k];
+      fsdx += gx * ga[k];
     }
+    sd += fsd;
+    sdx += fsdx;
   }
-  atomicAdd(&sh[2 * grp], sd);
-  atomicAdd(&sh[2 * grp + 1], sdx);
+  if (p0 + row < p1) {
+    atomicAdd(&sh[2 * grp], sd);
+    atomicAdd(&sh[2 * grp + 1], sdx);
 #pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    atomicAdd(&sh[2 * q.g + 2 * (c + k)], dg[k]);
-    atomicAdd(&sh[2 * q.g + 2 * (c + k) + 1], dbt[k]);
+    for (int k = 0; k < 4; ++k) {
+      atomicAdd(&sh[2 * q.g + 2 * (c + k)], dg[k]);
+      atomicAdd(&sh[2 * q.g + 2 * (c + k) + 1], dbt[k]);
+    }
   }
   __syncthreads();
   double* out = part + ((long long)img * q.chunks + chunk) * nsh;
   for (int i = t; i < nsh; i += blockDim.x) out[i] = sh[i];
 }
 
-// Reduces the partials: per (img, grp) -> coef[img][grp][2] = (mean(dxh), mean(dxh*xh));
-// per channel -> dgamma, dbeta (fixed order over images and chunks).
+// One warp per (img, grp) -> coef[img][grp][2] = (mean(dxh), mean(dxh*xh)),
+// then one warp per channel -> dgamma, dbeta; fixed-order sums.
 __global__ void gn_bwd_final_kernel(const double* __restrict__ part, GnGeom q,
                                     float* __restrict__ coef, float* dgamma, float* dbeta,
                                     int accumulate) {
   const int nsh = 2 * q.g + 2 * q.c;
-  const int idx = blockIdx.x * blockDim.x + threadIdx.x;
+  const int wid = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  const int lane = threadIdx.x & 31;
   const double cnt = (double)q.hw * (q.c / q.g);
-  if (idx < q.n * q.g) {
-    const int img = idx / q.g, grp = idx % q.g;
-    double a = 0, b = 0;
-    for (int k = 0; k < q.chunks; ++k) {
+  double a = 0, b = 0;
+  if (wid < q.n * q.g) {
+    const int img = wid / q.g, grp = wid % q.g;
+    for (int k = lane; k < q.chunks; k += 32) {
       const double* pp = part + ((long long)img * q.chunks + k) * nsh;
       a += pp[2 * grp];
       b += pp[2 * grp + 1];
     }
-    coef[2 * idx] = (float)(a / cnt);
-    coef[2 * idx + 1] = (float)(b / cnt);
+  } else if (wid < q.n * q.g + q.c) {
+    const int ch = wid - q.n * q.g;
+    for (int k = lane; k < q.n * q.chunks; k += 32) {
+      const double* pp = part + (long long)k * nsh + 2 * q.g;
+      a += pp[2 * ch];
+      b += pp[2 * ch + 1];
+    }
+  } else {
+    return;
   }
-  if (idx < q.c) {
-    double a = 0, b = 0;
-    for (int img = 0; img < q.n; ++img)
-      for (int k = 0; k < q.chunks; ++k) {
-        const double* pp = part + ((long long)img * q.chunks + k) * nsh + 2 * q.g;
-        a += pp[2 * idx];
-        b += pp[2 * idx + 1];
-      }
-    if (dgamma) dgamma[idx] = accumulate ? dgamma[idx] + (float)a : (float)a;
-    if (dbeta) dbeta[idx] = accumulate ? dbeta[idx] + (float)b : (float)b;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    a += __shfl_xor_sync(0xffffffffu, a, o);
+    b += __shfl_xor_sync(0xffffffffu, b, o);
+  }
+  if (lane) return;
+  if (wid < q.n * q.g) {
+    coef[2 * wid] = (float)(a / cnt);
+    coef[2 * wid + 1] = (float)(b / cnt);
+  } else {
+    const int ch = wid - q.n * q.g;
+    if (dgamma) dgamma[ch] = accumulate ? dgamma[ch] + (float)a : (float)a;
+    if (dbeta) dbeta[ch] = accumulate ? dbeta[ch] + (float)b : (float)b;
   }
 }
 
+// dx = rstd * (dxh - mean(dxh) - xh * mean(dxh*xh)) (+ addend).
 __global__ void gn_bwd_apply_kernel(const float* __restrict__ x, const float* __restrict__ dy,
                                     int lddy, GnGeom q, const float* __restrict__ mean,
                                     const float* __restrict__ rstd,
@@ -237,39 +342,40 @@ __global__ void gn_bwd_apply_kernel(const float* __restrict__ x, const float* __
                                     const float* __restrict__ coef,
                                     const float* __restrict__ addend, int ldadd,
                                     float* __restrict__ dx, int lddx, int round) {
-  const long long total = (long long)q.n * q.hw * q.quads;
-  const int cg = q.c / q.g;
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
-       i += (long long)gridDim.x * blockDim.x) {
-    const int quad = (int)(i % q.quads);
-    const long long pix = i / q.quads;
-    const int img = (int)(pix / q.hw);
-    const int c = quad * 4;
-    const int gi = img * q.g + c / cg;
-    const float m = mean[gi], r = rstd[gi];
-    const float md = coef[2 * gi], mdx = coef[2 * gi + 1];
-    const float4 xv = *reinterpret_cast<const float4*>(x + pix * q.ps + c);
-    const float4 dv = *reinterpret_cast<const float4*>(dy + pix * lddy + c);
-    const float xs[4] = {xv.x, xv.y, xv.z, xv.w};
-    const float ds[4] = {dv.x, dv.y, dv.z, dv.w};
+  const int img = blockIdx.y;
+  const int quad = threadIdx.x % q.quads, row = threadIdx.x / q.quads;
+  const int c = quad * 4;
+  const int gi = img * q.g + c / (q.c / q.g);
+  const float m = mean[gi], r = rstd[gi];
+  const float md = coef[2 * gi], mdx = coef[2 * gi + 1];
+  float ga[4], be[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    ga[k] = gamma ? __ldg(gamma + c + k) : 1.f;
+    be[k] = beta ? __ldg(beta + c + k) : 0.f;
+  }
+  long long p0, p1;
+  chunk_range(q, blockIdx.x, q.achunks, &p0, &p1);
+  const float* xb = x + (long long)img * q.hw * q.ps + c;
+  const float* dyb = dy + (long long)img * q.hw * lddy + c;
+  const float* ab = addend ? addend + (long long)img * q.hw * ldadd + c : nullptr;
+  float* dxb = dx + (long long)img * q.hw * lddx + c;
+  for (long long p = p0 + row; p < p1; p += q.rows) {
+    const float4 xv = __ldg(reinterpret_cast<const float4*>(xb + p * q.ps));
+    const float4 dv = __ldg(reinterpret_cast<const float4*>(dyb + p * lddy));
     float4 av = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (addend) av = *reinterpret_cast<const float4*>(addend + pix * ldadd + c);
+    if (ab) av = __ldg(reinterpret_cast<const float4*>(ab + p * ldadd));
+    const float xs[4] = {xv.x, xv.y, xv.z, xv.w}, ds[4] = {dv.x, dv.y, dv.z, dv.w};
     const float adds[4] = {av.x, av.y, av.z, av.w};
     float o[4];
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
-      const float ga = gamma ? __ldg(gamma + c + k) : 1.f;
-      const float xh = (xs[k] - m) * r;
-      float da = ds[k];
-      if (silu) {
-        const float a = xh * ga + (beta ? __ldg(beta + c + k) : 0.f);
-        const float sg = 1.f / (1.f + __expf(-a));
-        da *= sg * (1.f + a * (1.f - sg));
-      }
-      const float v = r * (da * ga - md - xh * mdx) + adds[k];
+      float xh, da;
+      gn_bwd_elem(xs[k], ds[k], ga[k], be[k], m, r, silu, &xh, &da);
+      const float v = r * (da * ga[k] - md - xh * mdx) + adds[k];
       o[k] = round ? round_tf32(v) : v;
     }
-    *reinterpret_cast<float4*>(dx + pix * lddx + c) = make_float4(o[0], o[1], o[2], o[3]);
+    *reinterpret_cast<float4*>(dxb + p * lddx) = make_float4(o[0], o[1], o[2], o[3]);
   }
 }
 
@@ -283,30 +389,44 @@ static yl_status gn_check(int n, int c, int g, long long hw, int ps) {
   return YL_OK;
 }
 
+// The two launches of the statistics pass, with the partials in `part`
+// (n * chunks * 2 * g doubles).
+static yl_status gn_stats_launch(yl_ctx* ctx, const float* x, const GnGeom& q, float eps, int mode,
+                                 double* part, float* mean, float* rstd) {
+  dim3 grid(q.chunks, q.n);
+  gn_stats_partial_kernel<<<grid, q.quads * q.rows, 2 * q.g * sizeof(double), ctx->stream>>>(
+      x, q, part);
+  YL_TRY(check_launch("gn_stats_partial_kernel"));
+  const int warps = q.n * q.g;
+  gn_stats_final_kernel<<<(warps + 7) / 8, 256, 0, ctx->stream>>>(part, q, eps, mode, mean, rstd);
+  return check_launch("gn_stats_final_kernel");
+}
+
+static yl_status gn_apply_launch(yl_ctx* ctx, const float* x, const GnGeom& q, const float* mean,
+                                 const float* rstd, const float* gamma, const float* beta,
+                                 int silu, int round, float* y, int ldy) {
+  dim3 grid(q.achunks, q.n);
+  gn_apply_kernel<<<grid, q.quads * q.rows, 0, ctx->stream>>>(x, q, mean, rstd, gamma, beta, silu,
+                                                             round, y, ldy);
+  return check_launch("gn_apply_kernel");
+}
+
 yl_status gn_stats(yl_ctx* ctx, const float* x, int n, int c, int g, long long hw, int ps,
                    float eps, int mode, float* mean, float* rstd) {
   YL_TRY(gn_check(n, c, g, hw, ps));
   GnGeom q = gn_geom(n, c, g, hw, ps);
   void* ws = nullptr;
   YL_TRY(scratch_get(ctx, (size_t)n * q.chunks * 2 * g * sizeof(double), &ws));
-  dim3 grid(q.chunks, n);
-  gn_stats_partial_kernel<<<grid, q.quads * q.rows, 2 * g * sizeof(double), ctx->stream>>>(
-      x, q, (double*)ws);
-  YL_TRY(check_launch("gn_stats_partial_kernel"));
-  gn_stats_final_kernel<<<(n * g + 127) / 128, 128, 0, ctx->stream>>>((double*)ws, q, eps, mode,
-                                                                     mean, rstd);
-  return check_launch("gn_stats_final_kernel");
+  return gn_stats_launch(ctx, x, q, eps, mode, (double*)ws, mean, rstd);
 }
 
 yl_status gn_silu_forward(yl_ctx* ctx, const float* x, int n, int c, int g, long long hw, int ps,
                           float eps, int mode, const float* gamma, const float* beta, int silu,
                           float* y, int ldy, int round, float* mean, float* rstd) {
   YL_TRY(gn_stats(ctx, x, n, c, g, hw, ps, eps, mode, mean, rstd));
-  GnGeom q = gn_geom(n, c, g, hw, ps);
-  long long total = (long long)n * hw * q.quads;
-  gn_apply_kernel<<<grid_1d(total, 256, ctx->num_sms * 16), 256, 0, ctx->stream>>>(
-      x, q, mean, rstd, gamma, beta, silu, round, y, ldy);
-  return check_launch("gn_apply_kernel");
+  YL_CHECK(ldy % 4 == 0, YL_ERR_SHAPE, "groupnorm: output stride must be a multiple of 4");
+  return gn_apply_launch(ctx, x, gn_geom(n, c, g, hw, ps), mean, rstd, gamma, beta, silu, round,
+                         y, ldy);
 }
 
 yl_status gn_silu_backward(yl_ctx* ctx, const float* x, const float* dy, int lddy, int n, int c,
@@ -329,12 +449,12 @@ yl_status gn_silu_backward(yl_ctx* ctx, const float* x, const float* dy, int ldd
   gn_bwd_partial_kernel<<<grid, q.quads * q.rows, nsh * sizeof(double), ctx->stream>>>(
       x, dy, lddy, q, mean, rstd, gamma, beta, silu, part);
   YL_TRY(check_launch("gn_bwd_partial_kernel"));
-  int m = n * g > c ? n * g : c;
-  gn_bwd_final_kernel<<<(m + 127) / 128, 128, 0, ctx->stream>>>(part, q, coef, dgamma, dbeta,
-                                                               accumulate_params);
+  const int warps = n * g + c;
+  gn_bwd_final_kernel<<<(warps + 7) / 8, 256, 0, ctx->stream>>>(part, q, coef, dgamma, dbeta,
+                                                              accumulate_params);
   YL_TRY(check_launch("gn_bwd_final_kernel"));
-  long long total = (long long)n * hw * q.quads;
-  gn_bwd_apply_kernel<<<grid_1d(total, 256, ctx->num_sms * 16), 256, 0, ctx->stream>>>(
+  dim3 agrid(q.achunks, n);
+  gn_bwd_apply_kernel<<<agrid, q.quads * q.rows, 0, ctx->stream>>>(
       x, dy, lddy, q, mean, rstd, gamma, beta, silu, coef, addend, ldadd, dx, lddx, round);
   return check_launch("gn_bwd_apply_kernel");
 }
@@ -413,15 +533,6 @@ extern "C" yl_status yl_groupnorm_silu_fwd_noalloc(yl_ctx* ctx, const float* x, 
            n, groups, need, kGnNoAllocDoubles);
   double* part = nullptr;
   YL_TRY(gn_noalloc_scratch(ctx->device, &part));
-  dim3 grid(q.chunks, n);
-  gn_stats_partial_kernel<<<grid, q.quads * q.rows, 2 * groups * sizeof(double), ctx->stream>>>(
-      x, q, part);
-  YL_TRY(check_launch("gn_stats_partial_kernel"));
-  gn_stats_final_kernel<<<(n * groups + 127) / 128, 128, 0, ctx->stream>>>(part, q, eps, mode,
-                                                                          mean_out, rstd_out);
-  YL_TRY(check_launch("gn_stats_final_kernel"));
-  const long long total = (long long)n * hw * q.quads;
-  gn_apply_kernel<<<grid_1d(total, 256, ctx->num_sms * 16), 256, 0, ctx->stream>>>(
-      x, q, mean_out, rstd_out, gamma, beta, apply_silu, 0, y, c);
-  return check_launch("gn_apply_kernel");
+  YL_TRY(gn_stats_launch(ctx, x, q, eps, mode, part, mean_out, rstd_out));
+  return gn_apply_launch(ctx, x, q, mean_out, rstd_out, gamma, beta, apply_silu, 0, y, c);
 }

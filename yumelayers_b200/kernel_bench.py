@@ -55,7 +55,9 @@ def main(argv=None):
             row[m + "_tflops"] = round(p.flops / (ms * 1e-3) / 1e12, 1)
         print(json.dumps(row), flush=True)
     if a.groupnorm:
-        for (n, c, h, w) in [(8, 128, 480, 856), (8, 256, 240, 428)]:
+        gn_shapes = ([(8, 128, 480, 856), (8, 256, 240, 428)] if a.shapes == "vae"
+                     else [(8, 128, 192, 192)])
+        for (n, c, h, w) in gn_shapes:
             f, b = C.c_double(), C.c_double()
             call("yl_profile_groupnorm", ctx.handle, n, c, h, w, a.reps, C.byref(f), C.byref(b))
             e = n * c * h * w * 4
