@@ -79,7 +79,14 @@ __device__ __forceinline__ FpropTile fprop_tile(const ConvPlan& p, int t) {
 // Warp 4 streams A/B k-blocks through the shared-memory ring across tile
 // boundaries, warp 5 issues the MMAs into one of two TMEM accumulator
 // buffers, warps 0-3 drain the other buffer (epilogue) meanwhile.
-template <int BN, int MT>
+//
+// TR (transposed accumulator, BN = 128, MT = 2): the weight tile is the MMA's
+// A operand (M = 128 output channels) and the 256-pixel tile its B operand
+// (N = 256), one M=128 x N=256 MMA per K step instead of two 128 x 128 ones.
+// TMEM then holds [channel][pixel]: epilogue thread = one output channel,
+// and each store instruction of a warp writes 32 consecutive channels of one
+// pixel.
+template <int BN, int MT, bool TR = false>
 __global__ void __launch_bounds__(kThreads, 1)
     conv_tma_fprop_kernel(const __grid_constant__ CUtensorMap ta0,
                           const __grid_constant__ CUtensorMap ta1,
@@ -156,7 +163,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 5) {
     if (lane == 0) {
-      constexpr uint32_t idesc = idesc_tf32(kBM, BN, 0, 0);
+      constexpr uint32_t idesc = TR ? idesc_tf32(BN, MT * kBM, 0, 0) : idesc_tf32(kBM, BN, 0, 0);
       uint32_t it = 0;
       int tc = 0;
       bool ok = true;
@@ -183,11 +190,16 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int kk = 0; kk < kBK / 8; ++kk) {
             const uint64_t bdesc = sw128_desc(b_addr + kk * 32, 16, 1024);
-#pragma unroll
-            for (int m = 0; m < MT; ++m)
-              umma_tf32(dacc + (uint32_t)(m * BN),
-                        sw128_desc(a_addr + m * kATileBytes + kk * 32, 16, 1024), bdesc, idesc,
+            if constexpr (TR) {
+              umma_tf32(dacc, bdesc, sw128_desc(a_addr + kk * 32, 16, 1024), idesc,
                         (kb | kk) != 0);
+            } else {
+#pragma unroll
+              for (int m = 0; m < MT; ++m)
+                umma_tf32(dacc + (uint32_t)(m * BN),
+                          sw128_desc(a_addr + m * kATileBytes + kk * 32, 16, 1024), bdesc, idesc,
+                          (kb | kk) != 0);
+            }
           }
           umma_commit(&empty[s]);
         }
@@ -207,6 +219,52 @@ __global__ void __launch_bounds__(kThreads, 1)
       const FpropTile c = fprop_tile(p, tile);
       const TapPhase& ph = p.ph[c.z];
       const int n0 = c.nb * BN;
+      if constexpr (TR) {
+        // lane row = output channel, column = pixel (lattice row j of the tile, column q)
+        const int co = n0 + warp * 32 + lane;
+        const bool cval = co < e.n_total;
+        float badd = 0.f;
+        if (cval && e.bias) badd += __ldg(e.bias + co);
+        if (cval && e.bias2d) badd += __ldg(e.bias2d + (long long)c.img * e.n_total + co);
+        const uint32_t tbase =
+            tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)(buf * Cfg::kAccCols);
+#pragma unroll 1
+        for (int j = 0; j < kRows; ++j) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(tbase + (uint32_t)(j * 32), r);
+          tmem_ld_wait();
+          const int gy = c.ty * kRows + j;
+          const int Y = gy * p.ys + ph.ya;
+          if (!cval || gy >= p.gh || Y >= p.out_h) continue;
+          const long long rowp = ((long long)c.img * p.out_h + Y) * p.out_w;
+          // all residual loads first: out may alias nothing, but the compiler
+          // cannot know that and would otherwise wait on each load in turn
+          float v[32];
+#pragma unroll
+          for (int q = 0; q < 32; ++q) v[q] = __uint_as_float(r[q]) + badd;
+          if (e.residual) {
+            float rv[32];
+#pragma unroll
+            for (int q = 0; q < 32; ++q) {
+              const int gx = c.tx * 32 + q;
+              const int X = gx * p.xs + ph.xa;
+              rv[q] = gx < p.gw && X < p.out_w ? e.residual[(rowp + X) * e.ldr + co] : 0.f;
+            }
+#pragma unroll
+            for (int q = 0; q < 32; ++q) v[q] += rv[q];
+          }
+#pragma unroll
+          for (int q = 0; q < 32; ++q) {
+            const int gx = c.tx * 32 + q;
+            const int X = gx * p.xs + ph.xa;
+            if (gx < p.gw && X < p.out_w)
+              e.out[(rowp + X) * e.ldo + co] = e.round_tf32 ? round_tf32(v[q]) : v[q];
+          }
+        }
+        tc_fence_before();
+        mbar_arrive(&acc_empty[buf]);
+        continue;
+      }
 #pragma unroll 1
       for (int m = 0; m < MT; ++m) {
         const int gy = c.ty * kRows + m * 4 + warp, gx = c.tx * 32 + lane;
@@ -635,7 +693,7 @@ static yl_status make_atom_tmap(CUtensorMap* tm, const View& v, int box_w, int a
   return YL_OK;
 }
 
-template <int BN, int MT>
+template <int BN, int MT, bool TR = false>
 static yl_status launch_plan(yl_ctx* ctx, const View* views, int nviews, const float* w, int w_rows,
                              int w_cols, ConvPlan& p, int nphase, const ConvEpilogue& e) {
   using Cfg = FpropCfg<BN, MT>;
@@ -651,26 +709,33 @@ static yl_status launch_plan(yl_ctx* ctx, const View* views, int nviews, const f
   const long long tiles = (long long)p.pix_tiles * p.n_nblk * nphase;
   YL_CHECK(tiles > 0 && tiles < (1LL << 31), YL_ERR_SHAPE, "conv: %lld tiles", tiles);
   p.n_tiles = (int)tiles;
-  YL_CUDA(cudaFuncSetAttribute(conv_tma_fprop_kernel<BN, MT>,
+  YL_CUDA(cudaFuncSetAttribute(conv_tma_fprop_kernel<BN, MT, TR>,
                                cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes));
   const int grid = p.n_tiles < ctx->num_sms ? p.n_tiles : ctx->num_sms;
-  conv_tma_fprop_kernel<BN, MT><<<grid, kThreads, Cfg::kSmemBytes, ctx->stream>>>(
+  conv_tma_fprop_kernel<BN, MT, TR><<<grid, kThreads, Cfg::kSmemBytes, ctx->stream>>>(
       ta[0], ta[1], ta[2], ta[3], tw, p, e, ctx->dev_err);
   return check_launch("conv_tma_fprop_kernel");
 }
 
 // Tile choice: BN covers the output channels in as few blocks as possible;
-// two M subtiles when BN <= 128 and the lattice is tall enough that 8-row
-// tiles waste little of the last tile row.
+// two M subtiles (or, for cout <= 128 and long k loops, the transposed
+// 128 x 256 accumulator) when the lattice is tall enough that 8-row tiles
+// waste little of the last tile row.
 static yl_status run_plan(yl_ctx* ctx, const View* views, int nviews, const float* w, int w_rows,
                           int w_cols, ConvPlan& p, int nphase, const ConvEpilogue& e) {
   const bool tall = p.gh % 8 == 0 || p.gh >= 64;
+  // the transposed epilogue costs more instructions per tile: only worth it
+  // when every tile has a long k loop
+  int min_nk = 1 << 30;
+  for (int z = 0; z < nphase; ++z) min_nk = std::min(min_nk, p.ph[z].ntaps * p.cpt);
   if (e.n_total <= 32) return launch_plan<32, 1>(ctx, views, nviews, w, w_rows, w_cols, p, nphase, e);
   if (e.n_total <= 64) {
     if (tall) return launch_plan<64, 2>(ctx, views, nviews, w, w_rows, w_cols, p, nphase, e);
     return launch_plan<64, 1>(ctx, views, nviews, w, w_rows, w_cols, p, nphase, e);
   }
   if (e.n_total <= 128 || e.n_total % 256 != 0) {
+    if (tall && e.n_total <= 128 && min_nk >= 16)
+      return launch_plan<128, 2, true>(ctx, views, nviews, w, w_rows, w_cols, p, nphase, e);
     if (tall) return launch_plan<128, 2>(ctx, views, nviews, w, w_rows, w_cols, p, nphase, e);
     return launch_plan<128, 1>(ctx, views, nviews, w, w_rows, w_cols, p, nphase, e);
   }

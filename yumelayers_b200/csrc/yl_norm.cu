@@ -36,7 +36,8 @@ __device__ __forceinline__ float silu_f(float a) { return a / (1.f + __expf(-a))
 // per-channel constant (group statistics, gamma, beta) is loop-invariant and
 // no index needs a division.  Reductions use `chunks` pixel chunks per image
 // (one wave of 4 blocks per SM over all images, at least 16 pixels per
-// thread); the elementwise passes use `achunks`.
+// thread); the elementwise passes split each image into `achunks` work items
+// that a grid of resident blocks walks (no partial last wave).
 struct GnGeom {
   int n, c, g, ps;
   long long hw;
@@ -59,7 +60,7 @@ static GnGeom gn_geom(int n, int c, int g, long long hw, int ps) {
   long long cap = hw / (16LL * q.rows);
   if (cap < 1) cap = 1;
   q.chunks = (int)std::max(1LL, std::min((long long)kGnBlocksPerWave / per_img, cap));
-  q.achunks = (int)std::max(1LL, std::min(2LL * kGnBlocksPerWave / per_img, cap));
+  q.achunks = (int)std::max(1LL, std::min(4096LL / per_img, cap));
   return q;
 }
 
@@ -165,38 +166,45 @@ __device__ __forceinline__ float4 gn_act4(float4 v, const float (&sc)[4], const 
 }
 
 // y = [silu]((x - mean) * rstd * gamma + beta) = [silu](x * scale + shift).
-__global__ void gn_apply_kernel(const float* __restrict__ x, GnGeom q,
-                                const float* __restrict__ mean, const float* __restrict__ rstd,
-                                const float* __restrict__ gamma, const float* __restrict__ beta,
-                                int silu, int round, float* __restrict__ y, int ldy) {
-  const int img = blockIdx.y;
+__global__ void __launch_bounds__(256, 4)
+    gn_apply_kernel(const float* __restrict__ x, GnGeom q, const float* __restrict__ mean,
+                    const float* __restrict__ rstd, const float* __restrict__ gamma,
+                    const float* __restrict__ beta, int silu, int round, float* __restrict__ y,
+                    int ldy) {
   const int quad = threadIdx.x % q.quads, row = threadIdx.x / q.quads;
   const int c = quad * 4;
-  const int gi = img * q.g + c / (q.c / q.g);
-  const float m = mean[gi], r = rstd[gi];
-  float sc[4], sf[4];
+  const int grp = c / (q.c / q.g);
+  float ga[4], be[4];
 #pragma unroll
   for (int k = 0; k < 4; ++k) {
-    const float ga = gamma ? __ldg(gamma + c + k) : 1.f;
-    const float be = beta ? __ldg(beta + c + k) : 0.f;
-    sc[k] = r * ga;
-    sf[k] = be - m * r * ga;
+    ga[k] = gamma ? __ldg(gamma + c + k) : 1.f;
+    be[k] = beta ? __ldg(beta + c + k) : 0.f;
   }
-  long long p0, p1;
-  chunk_range(q, blockIdx.x, q.achunks, &p0, &p1);
-  const float* xb = x + (long long)img * q.hw * q.ps + c;
-  float* yb = y + (long long)img * q.hw * ldy + c;
-  long long p = p0 + row;
   const long long R = q.rows;
-  for (; p + R < p1; p += 2 * R) {
-    const float4 a = __ldg(reinterpret_cast<const float4*>(xb + p * q.ps));
-    const float4 b = __ldg(reinterpret_cast<const float4*>(xb + (p + R) * q.ps));
-    *reinterpret_cast<float4*>(yb + p * ldy) = gn_act4(a, sc, sf, silu, round);
-    *reinterpret_cast<float4*>(yb + (p + R) * ldy) = gn_act4(b, sc, sf, silu, round);
-  }
-  if (p < p1) {
-    const float4 a = __ldg(reinterpret_cast<const float4*>(xb + p * q.ps));
-    *reinterpret_cast<float4*>(yb + p * ldy) = gn_act4(a, sc, sf, silu, round);
+  for (int item = blockIdx.x; item < q.n * q.achunks; item += gridDim.x) {
+    const int img = item / q.achunks;
+    const float m = mean[img * q.g + grp], r = rstd[img * q.g + grp];
+    float sc[4], sf[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      sc[k] = r * ga[k];
+      sf[k] = be[k] - m * r * ga[k];
+    }
+    long long p0, p1;
+    chunk_range(q, item - img * q.achunks, q.achunks, &p0, &p1);
+    const float* xb = x + (long long)img * q.hw * q.ps + c;
+    float* yb = y + (long long)img * q.hw * ldy + c;
+    long long p = p0 + row;
+    for (; p + R < p1; p += 2 * R) {
+      const float4 a = __ldg(reinterpret_cast<const float4*>(xb + p * q.ps));
+      const float4 b = __ldg(reinterpret_cast<const float4*>(xb + (p + R) * q.ps));
+      *reinterpret_cast<float4*>(yb + p * ldy) = gn_act4(a, sc, sf, silu, round);
+      *reinterpret_cast<float4*>(yb + (p + R) * ldy) = gn_act4(b, sc, sf, silu, round);
+    }
+    if (p < p1) {
+      const float4 a = __ldg(reinterpret_cast<const float4*>(xb + p * q.ps));
+      *reinterpret_cast<float4*>(yb + p * ldy) = gn_act4(a, sc, sf, silu, round);
+    }
   }
 }
 
@@ -219,14 +227,15 @@ __device__ __forceinline__ void gn_bwd_elem(float x, float dy, float ga, float b
 }
 
 // Backward partials per (img, chunk): group sums [g][2] of (dxh, dxh*xh), then
-// channel sums [c][2] of (da*xh, da) for dgamma, dbeta.  Two pixels per
-// iteration are combined in float before the double accumulators.
-__global__ void gn_bwd_partial_kernel(const float* __restrict__ x, const float* __restrict__ dy,
-                                      int lddy, GnGeom q, const float* __restrict__ mean,
-                                      const float* __restrict__ rstd,
-                                      const float* __restrict__ gamma,
-                                      const float* __restrict__ beta, int silu,
-                                      double* __restrict__ part) {
+// channel sums [c][2] of (da*xh, da) for dgamma, dbeta.  Each thread sums its
+// pixels in float (a few hundred per chunk at most); the block and chunk
+// reductions are in double.  At most 64 registers, so four blocks fit per SM
+// and the reduction grid is exactly one wave.
+__global__ void __launch_bounds__(256, 4)
+    gn_bwd_partial_kernel(const float* __restrict__ x, const float* __restrict__ dy, int lddy,
+                          GnGeom q, const float* __restrict__ mean, const float* __restrict__ rstd,
+                          const float* __restrict__ gamma, const float* __restrict__ beta,
+                          int silu, double* __restrict__ part) {
   extern __shared__ double sh[];  // [g][2] + [c][2]
   const int img = blockIdx.y, chunk = blockIdx.x;
   const int t = threadIdx.x;
@@ -247,7 +256,7 @@ __global__ void gn_bwd_partial_kernel(const float* __restrict__ x, const float* 
   chunk_range(q, chunk, q.chunks, &p0, &p1);
   const float* xb = x + (long long)img * q.hw * q.ps + c;
   const float* db = dy + (long long)img * q.hw * lddy + c;
-  double sd = 0, sdx = 0, dg[4] = {0, 0, 0, 0}, dbt[4] = {0, 0, 0, 0};
+  float sd = 0.f, sdx = 0.f, dg[4] = {0.f, 0.f, 0.f, 0.f}, dbt[4] = {0.f, 0.f, 0.f, 0.f};
   const long long R = q.rows;
   long long p = p0 + row;
   for (; p < p1; p += 2 * R) {
@@ -277,12 +286,12 @@ __global__ void gn_bwd_partial_kernel(const float* __restrict__ x, const float* 
     sdx += fsdx;
   }
   if (p0 + row < p1) {
-    atomicAdd(&sh[2 * grp], sd);
-    atomicAdd(&sh[2 * grp + 1], sdx);
+    atomicAdd(&sh[2 * grp], (double)sd);
+    atomicAdd(&sh[2 * grp + 1], (double)sdx);
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
-      atomicAdd(&sh[2 * q.g + 2 * (c + k)], dg[k]);
-      atomicAdd(&sh[2 * q.g + 2 * (c + k) + 1], dbt[k]);
+      atomicAdd(&sh[2 * q.g + 2 * (c + k)], (double)dg[k]);
+      atomicAdd(&sh[2 * q.g + 2 * (c + k) + 1], (double)dbt[k]);
     }
   }
   __syncthreads();
@@ -334,48 +343,63 @@ __global__ void gn_bwd_final_kernel(const double* __restrict__ part, GnGeom q,
 }
 
 // dx = rstd * (dxh - mean(dxh) - xh * mean(dxh*xh)) (+ addend).
-__global__ void gn_bwd_apply_kernel(const float* __restrict__ x, const float* __restrict__ dy,
-                                    int lddy, GnGeom q, const float* __restrict__ mean,
-                                    const float* __restrict__ rstd,
-                                    const float* __restrict__ gamma,
-                                    const float* __restrict__ beta, int silu,
-                                    const float* __restrict__ coef,
-                                    const float* __restrict__ addend, int ldadd,
-                                    float* __restrict__ dx, int lddx, int round) {
-  const int img = blockIdx.y;
+__global__ void __launch_bounds__(256, 4)
+    gn_bwd_apply_kernel(const float* __restrict__ x, const float* __restrict__ dy, int lddy,
+                        GnGeom q, const float* __restrict__ mean, const float* __restrict__ rstd,
+                        const float* __restrict__ gamma, const float* __restrict__ beta, int silu,
+                        const float* __restrict__ coef, const float* __restrict__ addend,
+                        int ldadd, float* __restrict__ dx, int lddx, int round) {
   const int quad = threadIdx.x % q.quads, row = threadIdx.x / q.quads;
   const int c = quad * 4;
-  const int gi = img * q.g + c / (q.c / q.g);
-  const float m = mean[gi], r = rstd[gi];
-  const float md = coef[2 * gi], mdx = coef[2 * gi + 1];
+  const int grp = c / (q.c / q.g);
   float ga[4], be[4];
 #pragma unroll
   for (int k = 0; k < 4; ++k) {
     ga[k] = gamma ? __ldg(gamma + c + k) : 1.f;
     be[k] = beta ? __ldg(beta + c + k) : 0.f;
   }
-  long long p0, p1;
-  chunk_range(q, blockIdx.x, q.achunks, &p0, &p1);
-  const float* xb = x + (long long)img * q.hw * q.ps + c;
-  const float* dyb = dy + (long long)img * q.hw * lddy + c;
-  const float* ab = addend ? addend + (long long)img * q.hw * ldadd + c : nullptr;
-  float* dxb = dx + (long long)img * q.hw * lddx + c;
-  for (long long p = p0 + row; p < p1; p += q.rows) {
-    const float4 xv = __ldg(reinterpret_cast<const float4*>(xb + p * q.ps));
-    const float4 dv = __ldg(reinterpret_cast<const float4*>(dyb + p * lddy));
-    float4 av = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (ab) av = __ldg(reinterpret_cast<const float4*>(ab + p * ldadd));
-    const float xs[4] = {xv.x, xv.y, xv.z, xv.w}, ds[4] = {dv.x, dv.y, dv.z, dv.w};
-    const float adds[4] = {av.x, av.y, av.z, av.w};
-    float o[4];
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      float xh, da;
-      gn_bwd_elem(xs[k], ds[k], ga[k], be[k], m, r, silu, &xh, &da);
-      const float v = r * (da * ga[k] - md - xh * mdx) + adds[k];
-      o[k] = round ? round_tf32(v) : v;
+  const long long R = q.rows;
+  for (int item = blockIdx.x; item < q.n * q.achunks; item += gridDim.x) {
+    const int img = item / q.achunks;
+    const int gi = img * q.g + grp;
+    const float m = mean[gi], r = rstd[gi];
+    const float md = coef[2 * gi], mdx = coef[2 * gi + 1];
+    long long p0, p1;
+    chunk_range(q, item - img * q.achunks, q.achunks, &p0, &p1);
+    const float* xb = x + (long long)img * q.hw * q.ps + c;
+    const float* dyb = dy + (long long)img * q.hw * lddy + c;
+    const float* ab = addend ? addend + (long long)img * q.hw * ldadd + c : nullptr;
+    float* dxb = dx + (long long)img * q.hw * lddx + c;
+    for (long long p = p0 + row; p < p1; p += 2 * R) {
+      const bool two = p + R < p1;
+      float4 xv[2], dv[2], av[2];
+  #pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        xv[u] = dv[u] = av[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (u == 0 || two) {
+          const long long pp = p + u * R;
+          xv[u] = __ldg(reinterpret_cast<const float4*>(xb + pp * q.ps));
+          dv[u] = __ldg(reinterpret_cast<const float4*>(dyb + pp * lddy));
+          if (ab) av[u] = __ldg(reinterpret_cast<const float4*>(ab + pp * ldadd));
+        }
+      }
+  #pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        if (u == 1 && !two) break;
+        const float xs[4] = {xv[u].x, xv[u].y, xv[u].z, xv[u].w};
+        const float ds[4] = {dv[u].x, dv[u].y, dv[u].z, dv[u].w};
+        const float adds[4] = {av[u].x, av[u].y, av[u].z, av[u].w};
+        float o[4];
+  #pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          float xh, da;
+          gn_bwd_elem(xs[k], ds[k], ga[k], be[k], m, r, silu, &xh, &da);
+          const float v = r * (da * ga[k] - md - xh * mdx) + adds[k];
+          o[k] = round ? round_tf32(v) : v;
+        }
+        *reinterpret_cast<float4*>(dxb + (p + u * R) * lddx) = make_float4(o[0], o[1], o[2], o[3]);
+      }
     }
-    *reinterpret_cast<float4*>(dxb + p * lddx) = make_float4(o[0], o[1], o[2], o[3]);
   }
 }
 
@@ -402,12 +426,24 @@ static yl_status gn_stats_launch(yl_ctx* ctx, const float* x, const GnGeom& q, f
   return check_launch("gn_stats_final_kernel");
 }
 
+// Blocks of `kernel` that stay resident on the device at once (at least one).
+template <typename K>
+static int resident_grid(yl_ctx* ctx, K kernel, int threads, long long items) {
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, 0) != cudaSuccess ||
+      per_sm < 1)
+    per_sm = 1;
+  const long long g = (long long)per_sm * ctx->num_sms;
+  return (int)std::max(1LL, std::min(g, items));
+}
+
 static yl_status gn_apply_launch(yl_ctx* ctx, const float* x, const GnGeom& q, const float* mean,
                                  const float* rstd, const float* gamma, const float* beta,
                                  int silu, int round, float* y, int ldy) {
-  dim3 grid(q.achunks, q.n);
-  gn_apply_kernel<<<grid, q.quads * q.rows, 0, ctx->stream>>>(x, q, mean, rstd, gamma, beta, silu,
-                                                             round, y, ldy);
+  const int threads = q.quads * q.rows;
+  const int grid = resident_grid(ctx, gn_apply_kernel, threads, (long long)q.n * q.achunks);
+  gn_apply_kernel<<<grid, threads, 0, ctx->stream>>>(x, q, mean, rstd, gamma, beta, silu, round, y,
+                                                    ldy);
   return check_launch("gn_apply_kernel");
 }
 
@@ -453,7 +489,8 @@ yl_status gn_silu_backward(yl_ctx* ctx, const float* x, const float* dy, int ldd
   gn_bwd_final_kernel<<<(warps + 7) / 8, 256, 0, ctx->stream>>>(part, q, coef, dgamma, dbeta,
                                                               accumulate_params);
   YL_TRY(check_launch("gn_bwd_final_kernel"));
-  dim3 agrid(q.achunks, n);
+  const int agrid =
+      resident_grid(ctx, gn_bwd_apply_kernel, q.quads * q.rows, (long long)n * q.achunks);
   gn_bwd_apply_kernel<<<agrid, q.quads * q.rows, 0, ctx->stream>>>(
       x, dy, lddy, q, mean, rstd, gamma, beta, silu, coef, addend, ldadd, dx, lddx, round);
   return check_launch("gn_bwd_apply_kernel");

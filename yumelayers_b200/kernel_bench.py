@@ -30,6 +30,8 @@ VAE_SHAPES = [
 ]
 SMALL_SHAPES = [
     ("small_128_128", 8, 128, 192, 192, 128, 3, 1, 0),
+    ("small_256_256", 8, 256, 96, 192, 256, 3, 1, 0),
+    ("mid_128_128", 2, 128, 480, 856, 128, 3, 1, 0),
 ]
 
 
