@@ -38,6 +38,7 @@ CASES = [
     ("up_c128", 2, 128, 128, 10, 12, 3, 1, 1, True, None),
     ("up_c256_128", 1, 256, 128, 8, 14, 3, 1, 1, True, None),
     ("up_crop_c128", 1, 128, 128, 8, 9, 3, 1, 1, True, (15, 17)),
+    ("up_c256_256", 2, 256, 256, 6, 10, 3, 1, 1, True, None),
     ("s2_odd_c128_256", 1, 128, 256, 15, 17, 3, 2, 1, False, None),
     ("c256_to_128", 1, 256, 128, 30, 54, 3, 1, 1, False, None),
 ]

@@ -24,7 +24,7 @@ yl_status conv_wgrad_gather(yl_ctx* ctx, const float* dy, int ldy, int cout,
                             const ConvGather& g, float* dw, int accumulate, float* ws,
                             int splits);
 
-constexpr int kMaxTaps = 9;
+constexpr int kMaxTaps = 16;
 
 struct TapPhase {
   int ntaps, w_row0, ya, xa;
@@ -340,13 +340,19 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ------------------------------------------------------------------ wgrad
+// WG_UP: the filter gradient of a nearest-x2 upsample + 3x3 conv as four
+// independent GEMMs, one per output phase (a, b): the merged 2x2 taps of that
+// phase against the phase view of dy, at the source resolution (16 merged
+// taps instead of 9 taps at the output resolution); a final pass sums the
+// merged gradients back onto the 9 kernel taps.
 enum WgradMode : int { WG_PLAIN = 0, WG_STRIDE2 = 1, WG_UP = 2 };
 
 struct WgradPlan {
-  int mode, nkp;          // k-phases: 1, or 4 (the dy phase views of an upsample conv)
-  int gh, gw, xblocks;    // iteration lattice of one k-phase
+  int mode;
+  int nblk_ph;            // WG_UP: column blocks per output phase
+  int gh, gw, xblocks;    // k-block lattice (WG_UP: the source resolution)
   int n_img;
-  long long blocks_per_kp, blocks, per_split;
+  long long blocks, per_split;
   int ksize, pad, cin, cout, n_total;
   int ga, gb;             // 32-channel atoms per A (dy) / B (input) TMA box
   float* ws;
@@ -389,7 +395,8 @@ __device__ __forceinline__ WgAtom wgrad_atom(const WgradPlan& w, int n, int kp) 
   WgAtom a;
   const int tap = n / w.cin;
   a.ci = n - tap * w.cin;
-  const int ky = tap / w.ksize, kx = tap - (tap / w.ksize) * w.ksize;
+  const int kw = w.mode == WG_UP ? 2 : w.ksize;  // merged taps form a 2x2 grid
+  const int ky = tap / kw, kx = tap - (tap / kw) * kw;
   if (w.mode == WG_PLAIN) {
     a.map = 0;
     a.by = (int8_t)(ky - w.pad);
@@ -399,11 +406,11 @@ __device__ __forceinline__ WgAtom wgrad_atom(const WgradPlan& w, int n, int kp) 
     a.map = (int8_t)(((ry & 1) << 1) | (rx & 1));
     a.by = (int8_t)(ry >> 1);
     a.bx = (int8_t)(rx >> 1);
-  } else {  // WG_UP: dy phase kp = (pa, pb) reads source rows (pa + ky - pad) >> 1
+  } else {  // WG_UP: column n of phase kp = (pa, pb) is merged tap (ty, tx) = (ky, kx) < 2
     const int pa = kp >> 1, pb = kp & 1;
     a.map = 0;
-    a.by = (int8_t)((pa + ky - w.pad) >> 1);
-    a.bx = (int8_t)((pb + kx - w.pad) >> 1);
+    a.by = (int8_t)(ky + pa - 1);
+    a.bx = (int8_t)(kx + pb - 1);
   }
   return a;
 }
@@ -428,7 +435,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int m0 = blockIdx.x * (MT * kBM), n0 = blockIdx.y * Cfg::kBN;
+  const int m0 = blockIdx.x * (MT * kBM);
+  // WG_UP: blockIdx.y = (output phase, column block within the phase)
+  const int phase = w.mode == WG_UP ? (int)blockIdx.y / w.nblk_ph : 0;
+  const int n0 = (w.mode == WG_UP ? (int)blockIdx.y % w.nblk_ph : (int)blockIdx.y) * Cfg::kBN;
+  const int col0 = w.mode == WG_UP ? phase * 4 * w.cin + n0 : n0;
   const long long b_begin = blockIdx.z * w.per_split;
   const long long b_end = min(w.blocks, b_begin + w.per_split);
   const int nk = b_end > b_begin ? (int)(b_end - b_begin) : 0;
@@ -454,16 +465,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0 && nk > 0) {
       const CUtensorMap* amaps[4] = {&ta0, &ta1, &ta2, &ta3};
       const CUtensorMap* bmaps[4] = {&tb0, &tb1, &tb2, &tb3};
-      long long b = b_begin;
-      int kp = (int)(b / w.blocks_per_kp);
-      long long r = b - (long long)kp * w.blocks_per_kp;
+      long long r = b_begin;
       int xb = (int)(r % w.xblocks);
       r /= w.xblocks;
       int gy = (int)(r % w.gh);
       int im = (int)(r / w.gh);
+      const CUtensorMap* amap = amaps[phase];
       WgAtom at[Cfg::kBAtoms];
 #pragma unroll
-      for (int j = 0; j < Cfg::kBAtoms; ++j) at[j] = wgrad_atom(w, n0 + 32 * j, kp);
+      for (int j = 0; j < Cfg::kBAtoms; ++j) at[j] = wgrad_atom(w, n0 + 32 * j, phase);
       for (int kb = 0; kb < nk; ++kb) {
         const int s = kb % S;
         if (kb >= S && !mbar_wait(&empty[s], ((kb / S) - 1) & 1)) {
@@ -473,7 +483,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t a_dst = smem_u32(smem + s * Cfg::kStage);
         const uint32_t b_dst = a_dst + Cfg::kATile;
         const int gx0 = xb * BKP;
-        const CUtensorMap* amap = amaps[w.mode == WG_UP ? kp : 0];
         mbar_arrive_expect_tx(&full[s], Cfg::kStage);
         for (int a = 0; a < Cfg::kAAtoms; a += w.ga)
           tma_load_5d(a_dst + a * Cfg::kAtomBytes, amap, &full[s], 0, gx0, gy, m0 / 32 + a, im);
@@ -484,14 +493,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           xb = 0;
           if (++gy == w.gh) {
             gy = 0;
-            if (++im == w.n_img) {
-              im = 0;
-              ++kp;
-              if (w.mode == WG_UP && kp < w.nkp) {
-#pragma unroll
-                for (int j = 0; j < Cfg::kBAtoms; ++j) at[j] = wgrad_atom(w, n0 + 32 * j, kp);
-              }
-            }
+            if (++im == w.n_img) im = 0;
           }
         }
       }
@@ -536,7 +538,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int m = 0; m < MT; ++m) {
       const int co = m0 + m * kBM + warp * 32 + lane;
       const bool rval = got && co < w.cout;
-      float* dst = w.ws + (long long)blockIdx.z * w.ws_split_stride + (long long)co * w.n_total;
+      float* dst =
+          w.ws + (long long)blockIdx.z * w.ws_split_stride + (long long)co * w.n_total + col0 - n0;
 #pragma unroll 1
       for (int c0 = 0; c0 < Cfg::kBN; c0 += 32) {
         uint32_t r[32];
@@ -611,6 +614,31 @@ __device__ __forceinline__ int s2_rows(int a, int* ks, int* offs) {
   offs[1] = 0;
   return 2;
 }
+// out[ci][ph * 4 + t][co] = sum of wd[ci][ky*3+kx][co] over the kernel taps
+// that output phase ph = (a, b) merges into its source tap t = (ty, tx) (wd
+// is the dgrad weight [ci][9][co]); rounded to tf32.  The dX of an upsample
+// conv reads the four phase views of dy through these 16 merged taps.
+__global__ void up_merge_dgrad_weights_kernel(const float* __restrict__ wd,
+                                              float* __restrict__ out, int rows, int cout) {
+  const long long n = 16LL * rows * cout;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int co = (int)(i % cout);
+    long long r = i / cout;
+    const int pt = (int)(r % 16);
+    const int ci = (int)(r / 16);
+    const int ph = pt >> 2, t = pt & 3;
+    const int a = ph >> 1, b = ph & 1, ty = t >> 1, tx = t & 1;
+    float s = 0.f;
+    for (int ky = 0; ky < 3; ++ky) {
+      if (!up_row_in(a, ty, ky)) continue;
+      for (int kx = 0; kx < 3; ++kx)
+        if (up_row_in(b, tx, kx)) s += wd[((long long)ci * 9 + ky * 3 + kx) * cout + co];
+    }
+    out[i] = round_tf32(s);
+  }
+}
+
 // out[ph][ci][t][co] = wd[ci][tap(ph, t)][co] (wd is the dgrad weight [ci][9][co]).
 __global__ void s2_phase_weights_kernel(const float* __restrict__ wd, float* __restrict__ out,
                                         int rows, int cout) {
@@ -862,6 +890,40 @@ yl_status conv_fprop(yl_ctx* ctx, const ConvGather& g, const float* w, int n_row
   return conv_fprop_gather(ctx, g, w, n_rows, e);
 }
 
+// dX of a nearest-x2 upsample + 3x3 conv (pad 1) at the source resolution
+// sh x sw: dX[u][v] = sum over the four output phases (a, b) and their 2x2
+// merged taps of Wm[ph][t]^T dy_ph[u + 1 - a - ty][v + 1 - b - tx], with
+// dy_ph the phase views of dy (2sh x 2sw).  16 taps at the source
+// resolution instead of 9 at the output resolution plus a 2x2 sum.
+yl_status conv_dgrad_upsampled(yl_ctx* ctx, const float* dy, int ldy, int cout, int n, int sh,
+                               int sw, const float* wd, int rows, const ConvEpilogue& e) {
+  if (cout % 32 != 0 || ldy % 4 != 0 || ((uintptr_t)dy & 15) != 0 || sh < 1 || sw < 1 ||
+      e.n_total <= 0 || e.ldo < e.n_total)
+    return YL_ERR_UNSUPPORTED;
+  void* wsb = nullptr;
+  YL_TRY(scratch_get(ctx, (size_t)rows * 16 * cout * sizeof(float), &wsb));
+  float* wm = (float*)wsb;
+  up_merge_dgrad_weights_kernel<<<grid_1d(16LL * rows * cout, 256), 256, 0, ctx->stream>>>(
+      wd, wm, rows, cout);
+  YL_TRY(check_launch("up_merge_dgrad_weights_kernel"));
+  View v[4];
+  for (int ph = 0; ph < 4; ++ph)
+    v[ph] = phase_view(dy, cout, 2 * sw, 2 * sh, n, ldy, ph >> 1, ph & 1);
+  ConvPlan p{};
+  p.cpt = cout / 32;
+  p.n_img = n;
+  p.gh = sh; p.gw = sw; p.out_h = sh; p.out_w = sw; p.ys = p.xs = 1;
+  TapPhase& tp = p.ph[0];
+  tp.ntaps = 16;
+  for (int pt = 0; pt < 16; ++pt) {
+    const int ph = pt >> 2, t = pt & 3;
+    tp.map[pt] = (int8_t)ph;
+    tp.dy[pt] = (int8_t)(1 - (ph >> 1) - (t >> 1));
+    tp.dx[pt] = (int8_t)(1 - (ph & 1) - (t & 1));
+  }
+  return run_plan(ctx, v, 4, wm, rows, 16 * cout, p, 1, e);
+}
+
 // Tile shape of the TMA wgrad for a cout x n_total filter gradient
 // (n_total = taps * cin); mt = 0 means no TMA tile divides n_total.
 struct WgTile {
@@ -871,28 +933,75 @@ struct WgTile {
 
 static WgTile wgrad_tile(int cout, int n_total) {
   if (cout % 256 == 0 && n_total % 256 == 0) return {2, 1, 256, 16};
+  if (cout <= 128 && n_total % 512 == 0) return {1, 2, 256, 16};
   if (n_total % 384 == 0) return {1, 2, 192, 16};
   if (n_total % 256 == 0) return {1, 1, 256, 16};
   if (n_total % 128 == 0) return {1, 1, 128, 32};
   return {0, 0, 0, 0};
 }
 
+// How a filter gradient runs: mode (-1: the cp.async gather kernel), the tile,
+// the GEMM width per column group (WG_UP: 4 merged taps per output phase),
+// the workspace row length and the number of output tiles.
+struct WgShape {
+  int mode = -1;
+  WgTile tile{0, 0, 0, 0};
+  int sw = 0, sh = 0;
+  long long gemm_n = 0, ws_cols = 0, tiles = 0, kblocks = 0;
+};
+
+static WgShape wgrad_shape(const ConvGather& g, int cout, const float* dy, int ldy) {
+  WgShape r;
+  const bool k3p1 = g.ksize == 3 && g.pad == 1;
+  if (!(g.cin % 32 == 0 && (cout <= 32 || cout % 32 == 0) && cout % 4 == 0 && g.m_total > 0 &&
+        g.oh > 0 && g.ow > 0 && g.m_total % (g.oh * g.ow) == 0 && ((uintptr_t)g.src & 15) == 0 &&
+        ((uintptr_t)dy & 15) == 0 && g.ps % 4 == 0 && ldy % 4 == 0 &&
+        source_dims(g, &r.sw, &r.sh)))
+    return r;
+  int mode = -1;
+  if (g.stride == 1 && !g.up && r.sw == g.wv && r.sh == g.hv) mode = WG_PLAIN;
+  else if (g.stride == 2 && !g.up && k3p1 && r.sw == g.wv && r.sh == g.hv && r.sw >= 2 &&
+           r.sh >= 2)
+    mode = WG_STRIDE2;
+  else if (g.stride == 1 && g.up && k3p1 && g.hv == 2 * r.sh && g.wv == 2 * r.sw &&
+           g.oh == g.hv && g.ow == g.wv)
+    mode = WG_UP;
+  if (mode < 0) return r;
+  r.gemm_n = mode == WG_UP ? 4LL * g.cin : g.k_total;
+  r.tile = wgrad_tile(cout, (int)r.gemm_n);
+  if (!r.tile.mt) return r;
+  r.mode = mode;
+  r.ws_cols = mode == WG_UP ? 16LL * g.cin : g.k_total;
+  const long long mblk = (cout + r.tile.mt * kBM - 1) / (r.tile.mt * kBM);
+  r.tiles = mblk * (r.ws_cols / r.tile.bn());
+  const int gw = mode == WG_UP ? r.sw : g.ow, gh = mode == WG_UP ? r.sh : g.oh;
+  r.kblocks = (long long)(g.m_total / (g.oh * g.ow)) * gh * ((gw + r.tile.bkp - 1) / r.tile.bkp);
+  return r;
+}
+
 // Split-K factor: one wave of CTAs (tiles * splits <= SM count), at least
 // four k-blocks per split.
-int conv_wgrad_pick_splits(yl_ctx* ctx, int cout, int k_total, int m_total) {
-  WgTile t = wgrad_tile(cout, k_total);
-  if (!t.mt) t = {1, 1, 128, 32};
-  const long long tiles =
-      (long long)((cout + t.mt * kBM - 1) / (t.mt * kBM)) * ((k_total + t.bn() - 1) / t.bn());
-  const long long kblocks = ((long long)m_total + t.bkp - 1) / t.bkp;
-  long long splits = std::max(1LL, ctx->num_sms / tiles);
+int conv_wgrad_pick_splits(yl_ctx* ctx, int cout, const ConvGather& g, const float* dy, int ldy) {
+  WgShape sh = wgrad_shape(g, cout, dy, ldy);
+  long long tiles = sh.tiles, kblocks = sh.kblocks;
+  if (sh.mode < 0) {  // gather kernel: 128 x 128 tiles, 32-pixel k-blocks
+    tiles = (long long)((cout + kBM - 1) / kBM) * ((g.k_total + 127) / 128);
+    kblocks = ((long long)g.m_total + kBK - 1) / kBK;
+  }
+  long long splits = std::max(1LL, ctx->num_sms / std::max(1LL, tiles));
   splits = std::min(splits, std::max(1LL, kblocks / 4));
   return (int)std::min(splits, 512LL);
 }
 
+size_t conv_wgrad_ws_floats(const ConvGather& g, int cout, const float* dy, int ldy, int splits) {
+  WgShape sh = wgrad_shape(g, cout, dy, ldy);
+  const long long cols = sh.mode < 0 ? g.k_total : sh.ws_cols;
+  return (size_t)splits * cout * cols;
+}
+
 template <int MT, int NSUB, int NW, int BKP>
 static yl_status launch_wgrad(yl_ctx* ctx, const View* av, int nav, const View* bv, int nbv,
-                              WgradPlan& w, int splits) {
+                              WgradPlan& w, int splits, int col_blocks) {
   using Cfg = WgradCfg<MT, NSUB, NW, BKP>;
   // A box: all of the tile's dy atoms at once when cout is whole atoms; B box:
   // four atoms (128 input channels of one tap) when the taps allow it
@@ -906,37 +1015,49 @@ static yl_status launch_wgrad(yl_ctx* ctx, const View* av, int nav, const View* 
                           CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B));
   }
   w.xblocks = (w.gw + BKP - 1) / BKP;
-  w.blocks_per_kp = (long long)w.n_img * w.gh * w.xblocks;
-  w.blocks = w.blocks_per_kp * w.nkp;
+  w.blocks = (long long)w.n_img * w.gh * w.xblocks;
   w.per_split = (w.blocks + splits - 1) / splits;
   YL_CUDA(cudaFuncSetAttribute(conv_tma_wgrad_kernel<MT, NSUB, NW, BKP>,
                                cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes));
-  dim3 grid((w.cout + MT * kBM - 1) / (MT * kBM), w.n_total / Cfg::kBN, splits);
+  dim3 grid((w.cout + MT * kBM - 1) / (MT * kBM), col_blocks, splits);
   conv_tma_wgrad_kernel<MT, NSUB, NW, BKP><<<grid, kThreads, Cfg::kSmemBytes, ctx->stream>>>(
       ta[0], ta[1], ta[2], ta[3], tb[0], tb[1], tb[2], tb[3], w, ctx->dev_err);
   return check_launch("conv_tma_wgrad_kernel");
 }
 
+// dw[co][ky*3+kx][ci] (+)= sum over splits and output phases (a, b) of the
+// merged gradient of the 2x2 tap (ty, tx) that kernel tap (ky, kx) belongs to
+// in that phase (the adjoint of up_merge_weights_kernel), fixed order.
+__global__ void wgrad_unmerge_kernel(const float* __restrict__ ws, int splits, long long stride,
+                                     int cout, int cin, float* __restrict__ dw, int accumulate) {
+  const long long n = (long long)cout * 9 * cin;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int ci = (int)(i % cin);
+    const long long r = i / cin;
+    const int tap = (int)(r % 9), co = (int)(r / 9);
+    const int ky = tap / 3, kx = tap % 3;
+    const float* row = ws + (long long)co * 16 * cin + ci;
+    float s = 0.f;
+    for (int a = 0; a < 2; ++a) {
+      const int ty = up_row_in(a, 0, ky) ? 0 : 1;
+      for (int b = 0; b < 2; ++b) {
+        const int tx = up_row_in(b, 0, kx) ? 0 : 1;
+        const long long col = (long long)(((a * 2 + b) * 4 + ty * 2 + tx) * cin);
+        for (int sp = 0; sp < splits; ++sp) s += row[sp * stride + col];
+      }
+    }
+    dw[i] = accumulate ? dw[i] + s : s;
+  }
+}
+
 yl_status conv_wgrad_ws(yl_ctx* ctx, const float* dy, int ldy, int cout, const ConvGather& g,
                         float* dw, int accumulate, float* ws, int splits) {
-  int sw = 0, sh = 0;
-  const bool k3p1 = g.ksize == 3 && g.pad == 1;
-  const WgTile tile = wgrad_tile(cout, g.k_total);
-  const bool base_ok = tile.mt > 0 && g.cin % 32 == 0 && (cout <= 32 || cout % 32 == 0) &&
-                       cout % 4 == 0 && g.m_total > 0 &&
-                       g.m_total % (g.oh * g.ow) == 0 && ((uintptr_t)g.src & 15) == 0 &&
-                       ((uintptr_t)dy & 15) == 0 && g.ps % 4 == 0 && ldy % 4 == 0 &&
-                       source_dims(g, &sw, &sh) && splits >= 1;
-  int mode = -1;
-  if (base_ok) {
-    if (g.stride == 1 && !g.up && sw == g.wv && sh == g.hv) mode = WG_PLAIN;
-    else if (g.stride == 2 && !g.up && k3p1 && sw == g.wv && sh == g.hv && sw >= 2 && sh >= 2)
-      mode = WG_STRIDE2;
-    else if (g.stride == 1 && g.up && k3p1 && g.hv == 2 * sh && g.wv == 2 * sw && g.oh % 2 == 0 &&
-             g.ow % 2 == 0)
-      mode = WG_UP;
-  }
-  if (mode < 0) return conv_wgrad_gather(ctx, dy, ldy, cout, g, dw, accumulate, ws, splits);
+  const WgShape shp = wgrad_shape(g, cout, dy, ldy);
+  if (shp.mode < 0 || splits < 1)
+    return conv_wgrad_gather(ctx, dy, ldy, cout, g, dw, accumulate, ws, splits);
+  const int mode = shp.mode, sw = shp.sw, sh = shp.sh;
+  const WgTile tile = shp.tile;
   const int n_img = g.m_total / (g.oh * g.ow);
   View av[4], bv[4];
   int nav = 1, nbv = 1;
@@ -946,16 +1067,17 @@ yl_status conv_wgrad_ws(yl_ctx* ctx, const float* dy, int ldy, int cout, const C
   w.pad = g.pad;
   w.cin = g.cin;
   w.cout = cout;
-  w.n_total = g.k_total;
+  w.n_total = (int)shp.ws_cols;
   w.n_img = n_img;
+  int col_blocks = (int)(shp.ws_cols / tile.bn());
   if (mode == WG_UP) {
     for (int ph = 0; ph < 4; ++ph)
       av[ph] = phase_view(dy, cout, g.ow, g.oh, n_img, ldy, ph >> 1, ph & 1);
     nav = 4;
     bv[0] = plain_view(g.src, g.cin, sw, sh, n_img, g.ps);
-    w.nkp = 4;
-    w.gh = g.oh / 2;
-    w.gw = g.ow / 2;
+    w.nblk_ph = (int)(shp.gemm_n / tile.bn());
+    w.gh = sh;
+    w.gw = sw;
   } else {
     av[0] = plain_view(dy, cout, g.ow, g.oh, n_img, ldy);
     if (mode == WG_STRIDE2) {
@@ -966,16 +1088,28 @@ yl_status conv_wgrad_ws(yl_ctx* ctx, const float* dy, int ldy, int cout, const C
     } else {
       bv[0] = plain_view(g.src, g.cin, sw, sh, n_img, g.ps);
     }
-    w.nkp = 1;
+    w.nblk_ph = col_blocks;
     w.gh = g.oh;
     w.gw = g.ow;
   }
   w.ws = ws;
-  w.ws_split_stride = (long long)cout * g.k_total;
-  if (tile.mt == 2) YL_TRY((launch_wgrad<2, 1, 256, 16>(ctx, av, nav, bv, nbv, w, splits)));
-  else if (tile.nsub == 2) YL_TRY((launch_wgrad<1, 2, 192, 16>(ctx, av, nav, bv, nbv, w, splits)));
-  else if (tile.nw == 256) YL_TRY((launch_wgrad<1, 1, 256, 16>(ctx, av, nav, bv, nbv, w, splits)));
-  else YL_TRY((launch_wgrad<1, 1, 128, 32>(ctx, av, nav, bv, nbv, w, splits)));
+  w.ws_split_stride = (long long)cout * shp.ws_cols;
+  if (tile.mt == 2)
+    YL_TRY((launch_wgrad<2, 1, 256, 16>(ctx, av, nav, bv, nbv, w, splits, col_blocks)));
+  else if (tile.nsub == 2 && tile.nw == 256)
+    YL_TRY((launch_wgrad<1, 2, 256, 16>(ctx, av, nav, bv, nbv, w, splits, col_blocks)));
+  else if (tile.nsub == 2)
+    YL_TRY((launch_wgrad<1, 2, 192, 16>(ctx, av, nav, bv, nbv, w, splits, col_blocks)));
+  else if (tile.nw == 256)
+    YL_TRY((launch_wgrad<1, 1, 256, 16>(ctx, av, nav, bv, nbv, w, splits, col_blocks)));
+  else
+    YL_TRY((launch_wgrad<1, 1, 128, 32>(ctx, av, nav, bv, nbv, w, splits, col_blocks)));
+  if (mode == WG_UP) {
+    const long long n = (long long)cout * 9 * g.cin;
+    wgrad_unmerge_kernel<<<grid_1d(n, 256), 256, 0, ctx->stream>>>(ws, splits, w.ws_split_stride,
+                                                                   cout, g.cin, dw, accumulate);
+    return check_launch("wgrad_unmerge_kernel");
+  }
   const long long n = (long long)cout * g.k_total;
   splitk_reduce_kernel<<<grid_1d(n / 4 + 1, 256), 256, 0, ctx->stream>>>(ws, splits, n, dw, n,
                                                                          accumulate);

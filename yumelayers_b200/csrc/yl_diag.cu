@@ -106,9 +106,9 @@ yl_status yl_profile_conv(yl_ctx* ctx, int n, int c, int h, int w, int oc, int k
   ed.out = dx;
   ed.ldo = c;
   ed.n_total = c;
-  const int splits = conv_wgrad_pick_splits(ctx, oc, g.k_total, g.m_total);
+  const int splits = conv_wgrad_pick_splits(ctx, oc, g, dy, oc);
   float* ws;
-  YL_TRY(b.get((size_t)splits * oc * g.k_total, &ws));
+  YL_TRY(b.get(conv_wgrad_ws_floats(g, oc, dy, oc, splits), &ws));
   cudaEvent_t e0, e1;
   YL_CUDA(cudaEventCreate(&e0));
   YL_CUDA(cudaEventCreate(&e1));
@@ -117,7 +117,13 @@ yl_status yl_profile_conv(yl_ctx* ctx, int n, int c, int h, int w, int oc, int k
     for (int r = -1; r < reps; ++r) {  // r = -1 is an untimed warm-up
       if (r == 0) YL_CUDA(cudaEventRecord(e0, ctx->stream));
       if (mode == 0) YL_TRY(conv_fprop(ctx, g, wt, oc, e));
-      if (mode == 1) YL_TRY(conv_fprop(ctx, gd, wd, c, ed));
+      if (mode == 1) {
+        // an upsample conv's dX at the source resolution, as the executor runs it
+        yl_status st = up ? conv_dgrad_upsampled(ctx, dy, oc, oc, n, h, w, wd, c, ed)
+                          : YL_ERR_UNSUPPORTED;
+        if (st == YL_ERR_UNSUPPORTED) st = conv_fprop(ctx, gd, wd, c, ed);
+        YL_TRY(st);
+      }
       if (mode == 2) YL_TRY(conv_wgrad_ws(ctx, dy, oc, oc, g, dw, 0, ws, splits));
     }
     YL_CUDA(cudaEventRecord(e1, ctx->stream));

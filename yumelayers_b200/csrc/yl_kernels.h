@@ -47,15 +47,23 @@ struct ConvEpilogue {
 yl_status conv_fprop(yl_ctx* ctx, const ConvGather& g, const float* w, int n_rows,
                      const ConvEpilogue& e);
 
+// dX (n x sh x sw, into e) of a nearest-x2 upsample + 3x3 pad-1 conv from its
+// output gradient dy (n x 2sh x 2sw x cout, pixel stride ldy) and the dgrad
+// weights wd [rows][9][cout].  YL_ERR_UNSUPPORTED (nothing launched) when the
+// shapes do not fit the merged-tap path.
+yl_status conv_dgrad_upsampled(yl_ctx* ctx, const float* dy, int ldy, int cout, int n, int sh,
+                               int sw, const float* wd, int rows, const ConvEpilogue& e);
+
 // dW[co][k] (+)= sum_p dy[p][co] * gather(p, k), p over all m_total pixels.
 // dy is [m_total][ldy]; dw is [cout][k_total].  Uses ctx scratch for split-K.
 yl_status conv_wgrad(yl_ctx* ctx, const float* dy, int ldy, int cout, const ConvGather& g,
                      float* dw, int accumulate);
-// Same contraction with an explicit split-K workspace and split count
-// (workspace must hold splits * cout * k_total floats).
+// Same contraction with an explicit split-K workspace and split count; the
+// workspace must hold conv_wgrad_ws_floats(g, cout, dy, ldy, splits) floats.
 yl_status conv_wgrad_ws(yl_ctx* ctx, const float* dy, int ldy, int cout, const ConvGather& g,
                         float* dw, int accumulate, float* workspace, int splits);
-int conv_wgrad_pick_splits(yl_ctx* ctx, int cout, int k_total, int m_total);
+int conv_wgrad_pick_splits(yl_ctx* ctx, int cout, const ConvGather& g, const float* dy, int ldy);
+size_t conv_wgrad_ws_floats(const ConvGather& g, int cout, const float* dy, int ldy, int splits);
 
 // Column sums of dy [images * hw][ldy] over pixels: db[c] (and, when
 // db_img != nullptr, db_img[img][c]).  Deterministic (fixed order).

@@ -266,6 +266,20 @@ yl_status ConvL::backward(Net& net, const Act& x, const Act& dy, const Act* dx,
   net.prof_end(2, 2.0 * g.m_total * cout * cin * k * k);
   YL_TRY(channel_sums(ctx, dy.p, dy.n, (long long)dy.h * dy.w, dy.ld, cout_p, gb, dbias2d, 0));
   if (!dx) return YL_OK;
+  if (up && !dx_addend && hv == 2 * x.h && wv == 2 * x.w && k == 3 && pad == 1 && stride == 1) {
+    // dX at the source resolution through the 16 merged phase taps
+    ConvEpilogue e;
+    e.out = dx->p;
+    e.ldo = dx->ld;
+    e.n_total = cin_p;
+    e.round_tf32 = 1;
+    net.prof_begin(1);
+    const yl_status st =
+        conv_dgrad_upsampled(ctx, dy.p, dy.ld, cout_p, x.n, x.h, x.w, Wd, cin_p, e);
+    net.prof_end(1, 2.0 * (double)x.n * hv * wv * cout * cin * k * k);
+    if (st == YL_OK) return YL_OK;
+    if (st != YL_ERR_UNSUPPORTED) return st;
+  }
   // dX: the same implicit GEMM over dy with the dgrad weights
   const int oh = up ? hv : x.h, ow = up ? wv : x.w;
   float* target = dx->p;
