@@ -28,6 +28,8 @@ CASES = [
     ("up_crop", 2, 8, 16, 5, 6, 3, 1, 1, True, (9, 11)),
     ("conv_in_rgb", 1, 3, 32, 20, 24, 3, 1, 1, False, None),
     ("conv_out_rgb", 1, 32, 3, 20, 24, 3, 1, 1, False, None),
+    ("conv_in_rgb_c128", 2, 3, 128, 24, 40, 3, 1, 1, False, None),
+    ("conv_out_rgb_c128", 2, 128, 3, 24, 40, 3, 1, 1, False, None),
     ("skip1x1", 2, 64, 128, 12, 10, 1, 1, 0, False, None),
     ("c128", 2, 128, 128, 24, 20, 3, 1, 1, False, None),
     ("c256", 1, 256, 256, 16, 18, 3, 1, 1, False, None),

@@ -86,31 +86,47 @@ def test_free_running_trajectories_stay_close():
 
 
 def test_vae_gradients_match_oracle():
-    """One VAE step's full gradient vector (before Adam) against the oracle's."""
+    """One VAE step's full gradient vector (before Adam) against the oracle's.
+
+    The L1 gradient is sign(recon - target): wherever the two sides' recon
+    straddles the target, tf32 forward noise flips that pixel's gradient, and
+    with ~0.1% of pixels flipped the weight gradients differ by ~1%.  The test
+    keeps every pixel away from a tie -- targets of +-0.9 against a
+    reconstruction held near zero by a scaled-down output conv -- so what it
+    measures is the backward arithmetic itself."""
     from yumelayers_b200.trainer import Trainer, default_config
     import nets
     tr = Trainer(default_config(batch=2, height=32, width=48, seed=5, train_motion=0,
                                 lr_vae=0.0))
-    vp = nets.Params(tr.param_table(0), tr.download(0))
+    table = tr.param_table(0)
+    flat = tr.download(0)
+    for e in table:
+        if e.name.startswith("dec.conv_out"):
+            n = int(np.prod([d for d in e.shape if d > 0]))
+            flat[e.offset:e.offset + n] *= 0.01
+    tr.upload(0, flat)
+    vp = nets.Params(table, flat)
     ops = nets.Ops()
     vae = nets.VAE(ops, vp)
     rng = np.random.default_rng(1)
-    x = np.clip(rng.standard_normal((3, 2, 3, 32, 48)) * 0.5, -1, 1).astype(np.float32)
+    x = np.where(rng.standard_normal((3, 2, 3, 32, 48)) > 0, 0.9, -0.9).astype(np.float32)
     gpu_loss = tr.step_host(x, np.full(2, 0.5, np.float32))
     g_gpu = tr.download(0, kind=1)
     loss, g, _ = vae.train_forward_backward(x[2], 1, 1e-6)
     g_ref = vp.to_flat(g, g_gpu.size)
     assert abs(gpu_loss[0] - loss) / loss < LOSS_TOL
     rel = np.linalg.norm(g_gpu - g_ref) / np.linalg.norm(g_ref)
-    assert rel < 1e-2, rel
-    # per-tensor check on the larger tensors (tf32 error compounds through depth)
-    worst = 0.0
+    # per-tensor errors on the larger tensors (tf32 error compounds through depth)
+    per = []
     for e in vp.table:
         n = int(np.prod([d for d in e.shape if d > 0]))
         if n < 4096:
             continue
         a = np.asarray(vp._get(e, g_gpu))
         b = np.asarray(vp._get(e, g_ref))
-        worst = max(worst, float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30)))
-    assert worst < 2e-2, worst
+        per.append((float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30)), e.name))
+    per.sort(reverse=True)
+    detail = f"global {rel:.3e}; worst tensors " + ", ".join(f"{n} {r:.2e}" for r, n in per[:6])
+    assert rel < 1e-2, detail
+    assert per[0][0] < 2e-2, detail
     tr.close()

@@ -782,40 +782,56 @@ static bool source_dims(const ConvGather& g, int* sw, int* sh) {
 yl_status conv_fprop(yl_ctx* ctx, const ConvGather& g, const float* w, int n_rows,
                      const ConvEpilogue& e) {
   int sw = 0, sh = 0;
-  const bool tma_ok = g.cin % 32 == 0 && g.m_total > 0 && g.m_total % (g.oh * g.ow) == 0 &&
-                      ((uintptr_t)g.src & 15) == 0 && g.ps % 4 == 0 && source_dims(g, &sw, &sh) &&
-                      e.n_total > 0 && e.ldo >= e.n_total;
+  // fewer than 32 channels (RGB frames, the RGB head's dy): each tap reads one
+  // 32-channel box of which the channels past cin read as zero, against
+  // weights padded to 32 channels per tap
+  const bool narrow = g.cin < 32 && 32 % g.cin == 0;
+  const bool tma_ok = (g.cin % 32 == 0 || narrow) && g.m_total > 0 &&
+                      g.m_total % (g.oh * g.ow) == 0 && ((uintptr_t)g.src & 15) == 0 &&
+                      g.ps % 4 == 0 && source_dims(g, &sw, &sh) && e.n_total > 0 &&
+                      e.ldo >= e.n_total;
   if (!tma_ok) return conv_fprop_gather(ctx, g, w, n_rows, e);
   const int n_img = g.m_total / (g.oh * g.ow);
   ConvPlan p{};
-  p.cpt = g.cin / 32;
+  p.cpt = narrow ? 1 : g.cin / 32;
   p.n_img = n_img;
   const bool k3p1 = g.ksize == 3 && g.pad == 1;
+  const int taps = g.ksize * g.ksize;
+  const bool plain_s1 = g.stride == 1 && sw == g.wv && sh == g.hv && (g.mode == MODE_DGRAD || !g.up);
+  if (narrow) {
+    if (!plain_s1) return conv_fprop_gather(ctx, g, w, n_rows, e);
+    void* wsb = nullptr;
+    YL_TRY(scratch_get(ctx, (size_t)n_rows * taps * 32 * sizeof(float), &wsb));
+    YL_TRY(weight_permute(ctx, w, (float*)wsb, n_rows, taps, 32, g.cin, (long long)taps * g.cin,
+                          g.cin, 1, 0));
+    w = (const float*)wsb;
+  }
+  const int kcols = taps * (narrow ? 32 : g.cin);
   if (g.mode == MODE_FPROP && g.stride == 1 && !g.up && sw == g.wv && sh == g.hv) {
     // plain stride-1 conv: tap (ky, kx) reads offset (ky - pad, kx - pad)
     View v = plain_view(g.src, g.cin, sw, sh, n_img, g.ps);
     p.gh = g.oh; p.gw = g.ow; p.out_h = g.oh; p.out_w = g.ow; p.ys = p.xs = 1;
     TapPhase& ph = p.ph[0];
-    ph.ntaps = g.ksize * g.ksize;
+    ph.ntaps = taps;
     for (int t = 0; t < ph.ntaps; ++t) {
       ph.map[t] = 0;
       ph.dy[t] = (int8_t)(t / g.ksize - g.pad);
       ph.dx[t] = (int8_t)(t % g.ksize - g.pad);
     }
-    return run_plan(ctx, &v, 1, w, n_rows, g.k_total, p, 1, e);
+    return run_plan(ctx, &v, 1, w, n_rows, kcols, p, 1, e);
   }
   if (g.mode == MODE_DGRAD && g.stride == 1 && sw == g.wv && sh == g.hv) {
     // stride-1 dX: the flipped taps over dy
     View v = plain_view(g.src, g.cin, sw, sh, n_img, g.ps);
     p.gh = g.oh; p.gw = g.ow; p.out_h = g.oh; p.out_w = g.ow; p.ys = p.xs = 1;
     TapPhase& ph = p.ph[0];
-    ph.ntaps = g.ksize * g.ksize;
+    ph.ntaps = taps;
     for (int t = 0; t < ph.ntaps; ++t) {
       ph.map[t] = 0;
       ph.dy[t] = (int8_t)(g.pad - t / g.ksize);
       ph.dx[t] = (int8_t)(g.pad - t % g.ksize);
     }
-    return run_plan(ctx, &v, 1, w, n_rows, g.k_total, p, 1, e);
+    return run_plan(ctx, &v, 1, w, n_rows, kcols, p, 1, e);
   }
   if (g.mode == MODE_FPROP && g.stride == 2 && !g.up && k3p1 && sw == g.wv && sh == g.hv &&
       sw >= 2 && sh >= 2) {
@@ -932,6 +948,7 @@ struct WgTile {
 };
 
 static WgTile wgrad_tile(int cout, int n_total) {
+  if (n_total == 288) return {1, 3, 96, 16};  // 9 taps of one (padded) 32-channel atom
   if (cout % 256 == 0 && n_total % 256 == 0) return {2, 1, 256, 16};
   if (cout <= 128 && n_total % 512 == 0) return {1, 2, 256, 16};
   if (n_total % 384 == 0) return {1, 2, 192, 16};
@@ -945,6 +962,7 @@ static WgTile wgrad_tile(int cout, int n_total) {
 // the workspace row length and the number of output tiles.
 struct WgShape {
   int mode = -1;
+  bool narrow = false;  // cin < 32: one zero-padded 32-channel atom per tap
   WgTile tile{0, 0, 0, 0};
   int sw = 0, sh = 0;
   long long gemm_n = 0, ws_cols = 0, tiles = 0, kblocks = 0;
@@ -953,7 +971,9 @@ struct WgShape {
 static WgShape wgrad_shape(const ConvGather& g, int cout, const float* dy, int ldy) {
   WgShape r;
   const bool k3p1 = g.ksize == 3 && g.pad == 1;
-  if (!(g.cin % 32 == 0 && (cout <= 32 || cout % 32 == 0) && cout % 4 == 0 && g.m_total > 0 &&
+  const bool narrow = g.cin < 32 && 32 % g.cin == 0;
+  if (!((g.cin % 32 == 0 || narrow) && (cout <= 32 || cout % 32 == 0) && cout % 4 == 0 &&
+        g.m_total > 0 &&
         g.oh > 0 && g.ow > 0 && g.m_total % (g.oh * g.ow) == 0 && ((uintptr_t)g.src & 15) == 0 &&
         ((uintptr_t)dy & 15) == 0 && g.ps % 4 == 0 && ldy % 4 == 0 &&
         source_dims(g, &r.sw, &r.sh)))
@@ -966,12 +986,13 @@ static WgShape wgrad_shape(const ConvGather& g, int cout, const float* dy, int l
   else if (g.stride == 1 && g.up && k3p1 && g.hv == 2 * r.sh && g.wv == 2 * r.sw &&
            g.oh == g.hv && g.ow == g.wv)
     mode = WG_UP;
-  if (mode < 0) return r;
-  r.gemm_n = mode == WG_UP ? 4LL * g.cin : g.k_total;
+  if (mode < 0 || (narrow && (mode != WG_PLAIN || g.ksize != 3))) return r;
+  r.narrow = narrow;
+  r.gemm_n = narrow ? 9 * 32 : mode == WG_UP ? 4LL * g.cin : g.k_total;
   r.tile = wgrad_tile(cout, (int)r.gemm_n);
   if (!r.tile.mt) return r;
   r.mode = mode;
-  r.ws_cols = mode == WG_UP ? 16LL * g.cin : g.k_total;
+  r.ws_cols = mode == WG_UP ? 16LL * g.cin : r.gemm_n;
   const long long mblk = (cout + r.tile.mt * kBM - 1) / (r.tile.mt * kBM);
   r.tiles = mblk * (r.ws_cols / r.tile.bn());
   const int gw = mode == WG_UP ? r.sw : g.ow, gh = mode == WG_UP ? r.sh : g.oh;
@@ -1051,6 +1072,23 @@ __global__ void wgrad_unmerge_kernel(const float* __restrict__ ws, int splits, l
   }
 }
 
+// dw[co][t][ci] (+)= sum over splits of ws[split][co][t * 32 + ci] (the
+// narrow-input layout with one zero-padded 32-channel atom per tap).
+__global__ void wgrad_unpad_kernel(const float* __restrict__ ws, int splits, long long stride,
+                                   int cout, int cin, float* __restrict__ dw, int accumulate) {
+  const long long n = (long long)cout * 9 * cin;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int ci = (int)(i % cin);
+    const long long r = i / cin;
+    const int t = (int)(r % 9), co = (int)(r / 9);
+    const float* src = ws + (long long)co * 288 + t * 32 + ci;
+    float s = 0.f;
+    for (int sp = 0; sp < splits; ++sp) s += src[sp * stride];
+    dw[i] = accumulate ? dw[i] + s : s;
+  }
+}
+
 yl_status conv_wgrad_ws(yl_ctx* ctx, const float* dy, int ldy, int cout, const ConvGather& g,
                         float* dw, int accumulate, float* ws, int splits) {
   const WgShape shp = wgrad_shape(g, cout, dy, ldy);
@@ -1065,7 +1103,7 @@ yl_status conv_wgrad_ws(yl_ctx* ctx, const float* dy, int ldy, int cout, const C
   w.mode = mode;
   w.ksize = g.ksize;
   w.pad = g.pad;
-  w.cin = g.cin;
+  w.cin = shp.narrow ? 32 : g.cin;  // the column layout's channels per tap
   w.cout = cout;
   w.n_total = (int)shp.ws_cols;
   w.n_img = n_img;
@@ -1094,7 +1132,9 @@ yl_status conv_wgrad_ws(yl_ctx* ctx, const float* dy, int ldy, int cout, const C
   }
   w.ws = ws;
   w.ws_split_stride = (long long)cout * shp.ws_cols;
-  if (tile.mt == 2)
+  if (tile.nsub == 3)
+    YL_TRY((launch_wgrad<1, 3, 96, 16>(ctx, av, nav, bv, nbv, w, splits, col_blocks)));
+  else if (tile.mt == 2)
     YL_TRY((launch_wgrad<2, 1, 256, 16>(ctx, av, nav, bv, nbv, w, splits, col_blocks)));
   else if (tile.nsub == 2 && tile.nw == 256)
     YL_TRY((launch_wgrad<1, 2, 256, 16>(ctx, av, nav, bv, nbv, w, splits, col_blocks)));
@@ -1104,6 +1144,12 @@ yl_status conv_wgrad_ws(yl_ctx* ctx, const float* dy, int ldy, int cout, const C
     YL_TRY((launch_wgrad<1, 1, 256, 16>(ctx, av, nav, bv, nbv, w, splits, col_blocks)));
   else
     YL_TRY((launch_wgrad<1, 1, 128, 32>(ctx, av, nav, bv, nbv, w, splits, col_blocks)));
+  if (shp.narrow) {
+    const long long n = (long long)cout * 9 * g.cin;
+    wgrad_unpad_kernel<<<grid_1d(n, 256), 256, 0, ctx->stream>>>(ws, splits, w.ws_split_stride,
+                                                                 cout, g.cin, dw, accumulate);
+    return check_launch("wgrad_unpad_kernel");
+  }
   if (mode == WG_UP) {
     const long long n = (long long)cout * 9 * g.cin;
     wgrad_unmerge_kernel<<<grid_1d(n, 256), 256, 0, ctx->stream>>>(ws, splits, w.ws_split_stride,
