@@ -496,11 +496,11 @@ yl_status conv_wgrad_gather(yl_ctx* ctx, const float* dy, int ldy, int cout,
 }
 
 yl_status conv_wgrad(yl_ctx* ctx, const float* dy, int ldy, int cout, const ConvGather& g,
-                     float* dw, int accumulate) {
+                     float* dw, int accumulate, float* db) {
   const int splits = conv_wgrad_pick_splits(ctx, cout, g, dy, ldy);
   void* ws = nullptr;
   YL_TRY(scratch_get(ctx, conv_wgrad_ws_floats(g, cout, dy, ldy, splits) * sizeof(float), &ws));
-  return conv_wgrad_ws(ctx, dy, ldy, cout, g, dw, accumulate, (float*)ws, splits);
+  return conv_wgrad_ws(ctx, dy, ldy, cout, g, dw, accumulate, (float*)ws, splits, db);
 }
 
 // ------------------------------------------------------------------ reductions / layouts

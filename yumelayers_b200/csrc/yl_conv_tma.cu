@@ -357,6 +357,9 @@ struct WgradPlan {
   int ga, gb;             // 32-channel atoms per A (dy) / B (input) TMA box
   float* ws;
   long long ws_split_stride;
+  // optional bias gradient: the first column block of each (phase, split)
+  // also sums its dy tiles per channel into db_ws[phase * splits + split][cout]
+  float* db_ws;
 };
 
 // dW tile: MT x 128 output channels (rows) by NSUB x NW columns of
@@ -443,11 +446,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   const long long b_begin = blockIdx.z * w.per_split;
   const long long b_end = min(w.blocks, b_begin + w.per_split);
   const int nk = b_end > b_begin ? (int)(b_end - b_begin) : 0;
+  // the epilogue warps read every dy stage for the bias gradient and release
+  // it together with the MMA warp
+  const bool with_db = w.db_ws != nullptr && n0 == 0;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1);
+      mbar_init(&empty[s], with_db ? 1 + 128 : 1);
     }
     mbar_init(accum, 1);
     fence_barrier_init();
@@ -527,6 +533,40 @@ __global__ void __launch_bounds__(kThreads, 1)
         umma_commit(&empty[s]);
       }
       umma_commit(accum);
+    }
+  }
+
+  if (warp < 4 && with_db) {
+    // thread t sums channels m0 + t (+ 128) over the pixel rows of every stage;
+    // channel c sits in atom c / 32, 16-byte chunk (c % 32) / 4 of each row
+    const int t = threadIdx.x;
+    float sum[MT];
+#pragma unroll
+    for (int m = 0; m < MT; ++m) sum[m] = 0.f;
+    for (int kb = 0; kb < nk; ++kb) {
+      const int s = kb % S;
+      if (!mbar_wait(&full[s], (kb / S) & 1)) {
+        report_error(err, YL_DEVERR_TIMEOUT);
+        break;
+      }
+      const uint8_t* a_tile = smem + s * Cfg::kStage;
+#pragma unroll
+      for (int m = 0; m < MT; ++m) {
+        const int c = m * kBM + t;
+        const uint8_t* atom = a_tile + (c >> 5) * Cfg::kAtomBytes + ((c & 3) << 2);
+        float acc = 0.f;
+#pragma unroll
+        for (int r = 0; r < BKP; ++r)
+          acc += *reinterpret_cast<const float*>(atom + b32_swizzle(r, (c & 31) >> 2));
+        sum[m] += acc;
+      }
+      mbar_arrive(&empty[s]);
+    }
+    const long long row = (long long)(phase * gridDim.z + blockIdx.z) * w.cout;
+#pragma unroll
+    for (int m = 0; m < MT; ++m) {
+      const int co = m0 + m * kBM + t;
+      if (co < w.cout) w.db_ws[row + co] = sum[m];
     }
   }
 
@@ -762,7 +802,7 @@ static yl_status run_plan(yl_ctx* ctx, const View* views, int nviews, const floa
     return launch_plan<64, 1>(ctx, views, nviews, w, w_rows, w_cols, p, nphase, e);
   }
   if (e.n_total <= 128 || e.n_total % 256 != 0) {
-    if (tall && e.n_total <= 128 && min_nk >= 16)
+    if (tall && e.n_total <= 128 && min_nk >= 9)
       return launch_plan<128, 2, true>(ctx, views, nviews, w, w_rows, w_cols, p, nphase, e);
     if (tall) return launch_plan<128, 2>(ctx, views, nviews, w, w_rows, w_cols, p, nphase, e);
     return launch_plan<128, 1>(ctx, views, nviews, w, w_rows, w_cols, p, nphase, e);
@@ -1017,7 +1057,19 @@ int conv_wgrad_pick_splits(yl_ctx* ctx, int cout, const ConvGather& g, const flo
 size_t conv_wgrad_ws_floats(const ConvGather& g, int cout, const float* dy, int ldy, int splits) {
   WgShape sh = wgrad_shape(g, cout, dy, ldy);
   const long long cols = sh.mode < 0 ? g.k_total : sh.ws_cols;
-  return (size_t)splits * cout * cols;
+  // + the bias-gradient partials (up to four phases per split), 64-float aligned
+  const size_t main = ((size_t)splits * cout * cols + 63) & ~size_t(63);
+  return main + (size_t)4 * splits * cout;
+}
+
+// db[c] (+)= sum over rows of part[rows][c], fixed order.
+__global__ void db_reduce_kernel(const float* __restrict__ part, int rows, int c,
+                                 float* __restrict__ db, int accumulate) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= c) return;
+  float s = 0.f;
+  for (int r = 0; r < rows; ++r) s += part[(long long)r * c + i];
+  db[i] = accumulate ? db[i] + s : s;
 }
 
 template <int MT, int NSUB, int NW, int BKP>
@@ -1090,10 +1142,13 @@ __global__ void wgrad_unpad_kernel(const float* __restrict__ ws, int splits, lon
 }
 
 yl_status conv_wgrad_ws(yl_ctx* ctx, const float* dy, int ldy, int cout, const ConvGather& g,
-                        float* dw, int accumulate, float* ws, int splits) {
+                        float* dw, int accumulate, float* ws, int splits, float* db) {
   const WgShape shp = wgrad_shape(g, cout, dy, ldy);
-  if (shp.mode < 0 || splits < 1)
-    return conv_wgrad_gather(ctx, dy, ldy, cout, g, dw, accumulate, ws, splits);
+  if (shp.mode < 0 || splits < 1) {
+    YL_TRY(conv_wgrad_gather(ctx, dy, ldy, cout, g, dw, accumulate, ws, splits));
+    if (!db) return YL_OK;
+    return channel_sums(ctx, dy, 1, g.m_total, ldy, cout, db, nullptr, accumulate);
+  }
   const int mode = shp.mode, sw = shp.sw, sh = shp.sh;
   const WgTile tile = shp.tile;
   const int n_img = g.m_total / (g.oh * g.ow);
@@ -1132,6 +1187,8 @@ yl_status conv_wgrad_ws(yl_ctx* ctx, const float* dy, int ldy, int cout, const C
   }
   w.ws = ws;
   w.ws_split_stride = (long long)cout * shp.ws_cols;
+  const size_t db_off = ((size_t)splits * cout * shp.ws_cols + 63) & ~size_t(63);
+  w.db_ws = db ? ws + db_off : nullptr;
   if (tile.nsub == 3)
     YL_TRY((launch_wgrad<1, 3, 96, 16>(ctx, av, nav, bv, nbv, w, splits, col_blocks)));
   else if (tile.mt == 2)
@@ -1144,6 +1201,12 @@ yl_status conv_wgrad_ws(yl_ctx* ctx, const float* dy, int ldy, int cout, const C
     YL_TRY((launch_wgrad<1, 1, 256, 16>(ctx, av, nav, bv, nbv, w, splits, col_blocks)));
   else
     YL_TRY((launch_wgrad<1, 1, 128, 32>(ctx, av, nav, bv, nbv, w, splits, col_blocks)));
+  if (db) {
+    const int rows = (mode == WG_UP ? 4 : 1) * splits;
+    db_reduce_kernel<<<(cout + 127) / 128, 128, 0, ctx->stream>>>(w.db_ws, rows, cout, db,
+                                                                 accumulate);
+    YL_TRY(check_launch("db_reduce_kernel"));
+  }
   if (shp.narrow) {
     const long long n = (long long)cout * 9 * g.cin;
     wgrad_unpad_kernel<<<grid_1d(n, 256), 256, 0, ctx->stream>>>(ws, splits, w.ws_split_stride,

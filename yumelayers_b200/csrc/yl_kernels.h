@@ -54,14 +54,16 @@ yl_status conv_fprop(yl_ctx* ctx, const ConvGather& g, const float* w, int n_row
 yl_status conv_dgrad_upsampled(yl_ctx* ctx, const float* dy, int ldy, int cout, int n, int sh,
                                int sw, const float* wd, int rows, const ConvEpilogue& e);
 
-// dW[co][k] (+)= sum_p dy[p][co] * gather(p, k), p over all m_total pixels.
+// dW[co][k] (+)= sum_p dy[p][co] * gather(p, k), p over all m_total pixels,
+// and, when db != nullptr, db[co] (+)= sum_p dy[p][co] from the same reads.
 // dy is [m_total][ldy]; dw is [cout][k_total].  Uses ctx scratch for split-K.
 yl_status conv_wgrad(yl_ctx* ctx, const float* dy, int ldy, int cout, const ConvGather& g,
-                     float* dw, int accumulate);
+                     float* dw, int accumulate, float* db = nullptr);
 // Same contraction with an explicit split-K workspace and split count; the
 // workspace must hold conv_wgrad_ws_floats(g, cout, dy, ldy, splits) floats.
 yl_status conv_wgrad_ws(yl_ctx* ctx, const float* dy, int ldy, int cout, const ConvGather& g,
-                        float* dw, int accumulate, float* workspace, int splits);
+                        float* dw, int accumulate, float* workspace, int splits,
+                        float* db = nullptr);
 int conv_wgrad_pick_splits(yl_ctx* ctx, int cout, const ConvGather& g, const float* dy, int ldy);
 size_t conv_wgrad_ws_floats(const ConvGather& g, int cout, const float* dy, int ldy, int splits);
 

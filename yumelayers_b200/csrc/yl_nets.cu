@@ -262,9 +262,11 @@ yl_status ConvL::backward(Net& net, const Act& x, const Act& dy, const Act* dx,
   // dW (split-K tcgen05, MN-major operands) and db (fixed-order column sums)
   ConvGather g = gather(x, dy.h, dy.w, up, hv, wv);
   net.prof_begin(2);
-  YL_TRY(conv_wgrad(ctx, dy.p, dy.ld, cout_p, g, gW, 0));
+  // db comes out of the filter-gradient pass unless per-image sums are needed
+  YL_TRY(conv_wgrad(ctx, dy.p, dy.ld, cout_p, g, gW, 0, dbias2d ? nullptr : gb));
   net.prof_end(2, 2.0 * g.m_total * cout * cin * k * k);
-  YL_TRY(channel_sums(ctx, dy.p, dy.n, (long long)dy.h * dy.w, dy.ld, cout_p, gb, dbias2d, 0));
+  if (dbias2d)
+    YL_TRY(channel_sums(ctx, dy.p, dy.n, (long long)dy.h * dy.w, dy.ld, cout_p, gb, dbias2d, 0));
   if (!dx) return YL_OK;
   if (up && !dx_addend && hv == 2 * x.h && wv == 2 * x.w && k == 3 && pad == 1 && stride == 1) {
     // dX at the source resolution through the 16 merged phase taps
