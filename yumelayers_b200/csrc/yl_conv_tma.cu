@@ -15,6 +15,7 @@
 // Shapes the tap tables do not cover fall back to the cp.async gathers of
 // yl_conv.cu.
 #include "yl_conv_common.cuh"
+#include "yl_norm.h"
 
 namespace yl {
 
@@ -73,6 +74,43 @@ __device__ __forceinline__ FpropTile fprop_tile(const ConvPlan& p, int t) {
   c.ty = r % p.tiles_y;
   c.img = r / p.tiles_y;
   return c;
+}
+
+// GroupNorm statistics from the conv epilogue.  Partial (sum, sum of squares)
+// per (tile, slot, group of the tile's channel block) go to e.gn_part; a
+// slot is one epilogue warp's share of the tile (one warp per lattice row
+// and subtile without TR, the whole tile with TR).
+template <int CG>
+__device__ __forceinline__ void gn_chunk_partials(const float (&v)[32], bool valid,
+                                                  float2* part_row, int g0, int lane) {
+#pragma unroll
+  for (int k = 0; k < 32 / CG; ++k) {
+    float s = 0.f, ss = 0.f;
+    if (valid) {
+#pragma unroll
+      for (int i = 0; i < CG; ++i) {
+        const float x = v[k * CG + i];
+        s += x;
+        ss += x * x;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      s += __shfl_xor_sync(0xffffffffu, s, o);
+      ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    }
+    if (lane == 0) part_row[g0 + k] = make_float2(s, ss);
+  }
+}
+
+__device__ __forceinline__ void gn_chunk_partials_any(int cg, const float (&v)[32], bool valid,
+                                                      float2* part_row, int g0, int lane) {
+  switch (cg) {
+    case 4: gn_chunk_partials<4>(v, valid, part_row, g0, lane); break;
+    case 8: gn_chunk_partials<8>(v, valid, part_row, g0, lane); break;
+    case 16: gn_chunk_partials<16>(v, valid, part_row, g0, lane); break;
+    default: gn_chunk_partials<32>(v, valid, part_row, g0, lane); break;
+  }
 }
 
 // Persistent: each CTA walks tiles blockIdx.x, blockIdx.x + gridDim.x, ...
@@ -228,6 +266,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (cval && e.bias2d) badd += __ldg(e.bias2d + (long long)c.img * e.n_total + co);
         const uint32_t tbase =
             tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)(buf * Cfg::kAccCols);
+        float gs = 0.f, gss = 0.f;  // GroupNorm partials of this channel
 #pragma unroll 1
         for (int j = 0; j < kRows; ++j) {
           uint32_t r[32];
@@ -257,9 +296,23 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int q = 0; q < 32; ++q) {
             const int gx = c.tx * 32 + q;
             const int X = gx * p.xs + ph.xa;
-            if (gx < p.gw && X < p.out_w)
-              e.out[(rowp + X) * e.ldo + co] = e.round_tf32 ? round_tf32(v[q]) : v[q];
+            if (gx < p.gw && X < p.out_w) {
+              const float o = e.round_tf32 ? round_tf32(v[q]) : v[q];
+              e.out[(rowp + X) * e.ldo + co] = o;
+              gs += o;
+              gss += o * o;
+            }
           }
+        }
+        if (e.gn_part) {
+          // the cg lanes of a group are consecutive: butterfly over them
+          for (int o = 1; o < e.gn_cg; o <<= 1) {
+            gs += __shfl_xor_sync(0xffffffffu, gs, o);
+            gss += __shfl_xor_sync(0xffffffffu, gss, o);
+          }
+          const int gpb = BN / e.gn_cg;
+          if ((lane & (e.gn_cg - 1)) == 0)
+            e.gn_part[(long long)tile * gpb + (warp * 32 + lane) / e.gn_cg] = make_float2(gs, gss);
         }
         tc_fence_before();
         mbar_arrive(&acc_empty[buf]);
@@ -279,50 +332,56 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint32_t r[32];
           tmem_ld_32x32b_x32(tbase + (uint32_t)c0, r);
           tmem_ld_wait();
-          if (!mval) continue;
           const int nb = n0 + c0;
           float v[32];
 #pragma unroll
           for (int q = 0; q < 32; ++q) v[q] = __uint_as_float(r[q]);
-          if (e.bias) {
+          if (mval) {
+            if (e.bias) {
 #pragma unroll
-            for (int q = 0; q < 32; ++q)
-              if (nb + q < e.n_total) v[q] += __ldg(e.bias + nb + q);
-          }
-          if (e.bias2d) {
-            const float* b2 = e.bias2d + (long long)c.img * e.n_total + nb;
+              for (int q = 0; q < 32; ++q)
+                if (nb + q < e.n_total) v[q] += __ldg(e.bias + nb + q);
+            }
+            if (e.bias2d) {
+              const float* b2 = e.bias2d + (long long)c.img * e.n_total + nb;
 #pragma unroll
-            for (int q = 0; q < 32; ++q)
-              if (nb + q < e.n_total) v[q] += __ldg(b2 + q);
-          }
-          const bool full32 = (nb + 32 <= e.n_total);
-          if (e.residual) {
-            const float* rp = e.residual + mrow * e.ldr + nb;
-            if (full32 && (e.ldr & 3) == 0) {
+              for (int q = 0; q < 32; ++q)
+                if (nb + q < e.n_total) v[q] += __ldg(b2 + q);
+            }
+            const bool full32 = (nb + 32 <= e.n_total);
+            if (e.residual) {
+              const float* rp = e.residual + mrow * e.ldr + nb;
+              if (full32 && (e.ldr & 3) == 0) {
 #pragma unroll
-              for (int q = 0; q < 32; q += 4) {
-                float4 rv = *reinterpret_cast<const float4*>(rp + q);
-                v[q] += rv.x; v[q + 1] += rv.y; v[q + 2] += rv.z; v[q + 3] += rv.w;
+                for (int q = 0; q < 32; q += 4) {
+                  float4 rv = *reinterpret_cast<const float4*>(rp + q);
+                  v[q] += rv.x; v[q + 1] += rv.y; v[q + 2] += rv.z; v[q + 3] += rv.w;
+                }
+              } else {
+#pragma unroll
+                for (int q = 0; q < 32; ++q)
+                  if (nb + q < e.n_total) v[q] += rp[q];
               }
+            }
+            if (e.round_tf32) {
+#pragma unroll
+              for (int q = 0; q < 32; ++q) v[q] = round_tf32(v[q]);
+            }
+            float* op = e.out + mrow * e.ldo + nb;
+            if (full32 && (e.ldo & 3) == 0) {
+#pragma unroll
+              for (int q = 0; q < 32; q += 4)
+                *reinterpret_cast<float4*>(op + q) = make_float4(v[q], v[q + 1], v[q + 2], v[q + 3]);
             } else {
 #pragma unroll
               for (int q = 0; q < 32; ++q)
-                if (nb + q < e.n_total) v[q] += rp[q];
+                if (nb + q < e.n_total) op[q] = v[q];
             }
           }
-          if (e.round_tf32) {
-#pragma unroll
-            for (int q = 0; q < 32; ++q) v[q] = round_tf32(v[q]);
-          }
-          float* op = e.out + mrow * e.ldo + nb;
-          if (full32 && (e.ldo & 3) == 0) {
-#pragma unroll
-            for (int q = 0; q < 32; q += 4)
-              *reinterpret_cast<float4*>(op + q) = make_float4(v[q], v[q + 1], v[q + 2], v[q + 3]);
-          } else {
-#pragma unroll
-            for (int q = 0; q < 32; ++q)
-              if (nb + q < e.n_total) op[q] = v[q];
+          if (e.gn_part) {
+            const int gpb = BN / e.gn_cg;
+            float2* row = e.gn_part + ((long long)tile * (MT * 4) + m * 4 + warp) * gpb;
+            gn_chunk_partials_any(e.gn_cg, v, mval, row, c0 / e.gn_cg, lane);
           }
         }
       }
@@ -761,6 +820,48 @@ static yl_status make_atom_tmap(CUtensorMap* tm, const View& v, int box_w, int a
   return YL_OK;
 }
 
+bool conv_gn_stats_supported(int n_total, int groups) {
+  if (groups <= 0 || n_total % groups) return false;
+  const int cg = n_total / groups;
+  return cg == 4 || cg == 8 || cg == 16 || cg == 32;
+}
+
+// mean/rstd per (image, group) from the per-tile partials: one warp per
+// (image, group), fixed-order double sums over the image's tiles and slots.
+__global__ void gn_tile_stats_kernel(const float2* __restrict__ part, ConvPlan p, int nphase,
+                                     int slots, int gpb, int groups, int cg, float eps,
+                                     float* __restrict__ mean, float* __restrict__ rstd) {
+  const int idx = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  const int lane = threadIdx.x & 31;
+  if (idx >= p.n_img * groups) return;
+  const int img = idx / groups, g = idx % groups;
+  const int nb = g / gpb, gb = g % gpb;
+  const int tpi = p.tiles_x * p.tiles_y;
+  const long long items = (long long)nphase * tpi * slots;
+  double s = 0.0, ss = 0.0;
+  for (long long i = lane; i < items; i += 32) {
+    const int z = (int)(i / ((long long)tpi * slots));
+    const long long rem = i - (long long)z * tpi * slots;
+    const int pix = img * tpi + (int)(rem / slots), slot = (int)(rem % slots);
+    const long long tile = ((long long)z * p.pix_tiles + pix) * p.n_nblk + nb;
+    const float2 v = part[(tile * slots + slot) * gpb + gb];
+    s += v.x;
+    ss += v.y;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    s += __shfl_xor_sync(0xffffffffu, s, o);
+    ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  }
+  if (lane) return;
+  const double cnt = (double)p.out_h * p.out_w * cg;
+  const double m = s / cnt;
+  double var = ss / cnt - m * m;
+  if (var < 0) var = 0;
+  mean[idx] = (float)m;
+  rstd[idx] = (float)(1.0 / sqrt(var + (double)eps));
+}
+
 template <int BN, int MT, bool TR = false>
 static yl_status launch_plan(yl_ctx* ctx, const View* views, int nviews, const float* w, int w_rows,
                              int w_cols, ConvPlan& p, int nphase, const ConvEpilogue& e) {
@@ -777,12 +878,30 @@ static yl_status launch_plan(yl_ctx* ctx, const View* views, int nviews, const f
   const long long tiles = (long long)p.pix_tiles * p.n_nblk * nphase;
   YL_CHECK(tiles > 0 && tiles < (1LL << 31), YL_ERR_SHAPE, "conv: %lld tiles", tiles);
   p.n_tiles = (int)tiles;
+  ConvEpilogue ek = e;
+  const int slots = TR ? 1 : MT * 4;
+  int gpb = 0;
+  if (e.gn_mean) {
+    YL_CHECK(conv_gn_stats_supported(e.n_total, e.gn_groups) && BN % (e.n_total / e.gn_groups) == 0,
+             YL_ERR_UNSUPPORTED, "conv: GroupNorm statistics for %d channels in %d groups",
+             e.n_total, e.gn_groups);
+    ek.gn_cg = e.n_total / e.gn_groups;
+    gpb = BN / ek.gn_cg;
+    void* part = nullptr;
+    YL_TRY(scratch_get(ctx, (size_t)p.n_tiles * slots * gpb * sizeof(float2), &part, 2));
+    ek.gn_part = (float2*)part;
+  }
   YL_CUDA(cudaFuncSetAttribute(conv_tma_fprop_kernel<BN, MT, TR>,
                                cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes));
   const int grid = p.n_tiles < ctx->num_sms ? p.n_tiles : ctx->num_sms;
   conv_tma_fprop_kernel<BN, MT, TR><<<grid, kThreads, Cfg::kSmemBytes, ctx->stream>>>(
-      ta[0], ta[1], ta[2], ta[3], tw, p, e, ctx->dev_err);
-  return check_launch("conv_tma_fprop_kernel");
+      ta[0], ta[1], ta[2], ta[3], tw, p, ek, ctx->dev_err);
+  YL_TRY(check_launch("conv_tma_fprop_kernel"));
+  if (!e.gn_mean) return YL_OK;
+  const int warps = p.n_img * e.gn_groups;
+  gn_tile_stats_kernel<<<(warps + 7) / 8, 256, 0, ctx->stream>>>(
+      ek.gn_part, p, nphase, slots, gpb, e.gn_groups, ek.gn_cg, e.gn_eps, e.gn_mean, e.gn_rstd);
+  return check_launch("gn_tile_stats_kernel");
 }
 
 // Tile choice: BN covers the output channels in as few blocks as possible;
@@ -819,6 +938,17 @@ static bool source_dims(const ConvGather& g, int* sw, int* sh) {
   return true;
 }
 
+// The cp.async gather path, plus a separate statistics pass when the caller
+// asked for the output's GroupNorm statistics.
+static yl_status gather_fprop(yl_ctx* ctx, const ConvGather& g, const float* w, int n_rows,
+                              const ConvEpilogue& e) {
+  YL_TRY(conv_fprop_gather(ctx, g, w, n_rows, e));
+  if (!e.gn_mean) return YL_OK;
+  const int n_img = g.m_total / (g.oh * g.ow);
+  return gn_stats(ctx, e.out, n_img, e.n_total, e.gn_groups, (long long)g.oh * g.ow, e.ldo,
+                  e.gn_eps, 0, e.gn_mean, e.gn_rstd);
+}
+
 yl_status conv_fprop(yl_ctx* ctx, const ConvGather& g, const float* w, int n_rows,
                      const ConvEpilogue& e) {
   int sw = 0, sh = 0;
@@ -830,7 +960,7 @@ yl_status conv_fprop(yl_ctx* ctx, const ConvGather& g, const float* w, int n_row
                       g.m_total % (g.oh * g.ow) == 0 && ((uintptr_t)g.src & 15) == 0 &&
                       g.ps % 4 == 0 && source_dims(g, &sw, &sh) && e.n_total > 0 &&
                       e.ldo >= e.n_total;
-  if (!tma_ok) return conv_fprop_gather(ctx, g, w, n_rows, e);
+  if (!tma_ok) return gather_fprop(ctx, g, w, n_rows, e);
   const int n_img = g.m_total / (g.oh * g.ow);
   ConvPlan p{};
   p.cpt = narrow ? 1 : g.cin / 32;
@@ -839,7 +969,7 @@ yl_status conv_fprop(yl_ctx* ctx, const ConvGather& g, const float* w, int n_row
   const int taps = g.ksize * g.ksize;
   const bool plain_s1 = g.stride == 1 && sw == g.wv && sh == g.hv && (g.mode == MODE_DGRAD || !g.up);
   if (narrow) {
-    if (!plain_s1) return conv_fprop_gather(ctx, g, w, n_rows, e);
+    if (!plain_s1) return gather_fprop(ctx, g, w, n_rows, e);
     void* wsb = nullptr;
     YL_TRY(scratch_get(ctx, (size_t)n_rows * taps * 32 * sizeof(float), &wsb));
     YL_TRY(weight_permute(ctx, w, (float*)wsb, n_rows, taps, 32, g.cin, (long long)taps * g.cin,
@@ -943,7 +1073,7 @@ yl_status conv_fprop(yl_ctx* ctx, const ConvGather& g, const float* w, int n_row
     }
     return run_plan(ctx, &v, 1, wp, 4 * n_rows, 4 * g.cin, p, 4, e);
   }
-  return conv_fprop_gather(ctx, g, w, n_rows, e);
+  return gather_fprop(ctx, g, w, n_rows, e);
 }
 
 // dX of a nearest-x2 upsample + 3x3 conv (pad 1) at the source resolution

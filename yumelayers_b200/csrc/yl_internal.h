@@ -60,8 +60,10 @@ struct yl_ctx {
   int* dev_err = nullptr;  // device error word, zeroed at creation
   // Scratch slots: 0 = temporaries of one internal kernel sequence (split-K
   // partials, reduction partials); 1 = layout conversions of a C-ABI call.
-  void* scratch[2] = {nullptr, nullptr};
-  size_t scratch_bytes[2] = {0, 0};
+  // slot 0: operator temporaries; 1: NCHW<->NHWC staging of the batched
+  // C-ABI entry points; 2: GroupNorm statistics partials written by a conv
+  void* scratch[3] = {nullptr, nullptr, nullptr};
+  size_t scratch_bytes[3] = {0, 0, 0};
 };
 
 namespace yl {

@@ -40,7 +40,21 @@ struct ConvEpilogue {
   const float* residual = nullptr;  // residual[m * ldr + n], may alias out
   int ldr = 0;
   int round_tf32 = 1;        // round outputs to tf32 (they feed another conv)
+  // GroupNorm statistics of the output for the GroupNorm that reads it: when
+  // gn_mean is set, conv_fprop also writes mean/rstd per (image, group) of the
+  // stored values (torch semantics: biased variance + eps).  Needs
+  // n_total = gn_groups * 2^k channels (k >= 2); otherwise YL_ERR_UNSUPPORTED.
+  float* gn_mean = nullptr;
+  float* gn_rstd = nullptr;
+  int gn_groups = 0;
+  float gn_eps = 1e-6f;
+  // set by conv_fprop: per-tile partial sums (float2) and channels per group
+  float2* gn_part = nullptr;
+  int gn_cg = 0;
 };
+
+// True when conv_fprop can produce GroupNorm statistics for this epilogue.
+bool conv_gn_stats_supported(int n_total, int groups);
 
 // out = gather(A) x W^T (+ bias, bias2d, residual); W is [n_rows][k_total]
 // row-major (n_rows >= n_total; rows past n_rows read as zero).

@@ -238,7 +238,7 @@ ConvGather ConvL::gather(const Act& x, int oh, int ow, int up, int hv, int wv) c
 }
 
 yl_status ConvL::forward(Net& net, const Act& x, const Act& y, const float* residual, int ldr,
-                         const float* bias2d, int up, int hv, int wv) {
+                         const float* bias2d, int up, int hv, int wv, GNL* gn_next) {
   ConvGather g = gather(x, y.h, y.w, up, hv, wv);
   ConvEpilogue e;
   e.out = y.p;
@@ -249,9 +249,17 @@ yl_status ConvL::forward(Net& net, const Act& x, const Act& y, const float* resi
   e.residual = residual;
   e.ldr = ldr;
   e.round_tf32 = 1;
+  const bool fuse_gn = gn_next && gn_next->c == cout_p && conv_gn_stats_supported(cout_p, gn_next->G);
+  if (fuse_gn) {
+    e.gn_mean = gn_next->mean;
+    e.gn_rstd = gn_next->rstd;
+    e.gn_groups = gn_next->G;
+    e.gn_eps = 1e-6f;
+  }
   net.prof_begin(0);
   yl_status st = conv_fprop(net.ctx, g, Wr, cout_p, e);
   net.prof_end(0, 2.0 * g.m_total * cout * cin * k * k);
+  if (st == YL_OK && fuse_gn) gn_next->stats_ready = true;
   return st;
 }
 
@@ -351,9 +359,18 @@ yl_status GNL::init(yl_ctx* ctx, uint64_t seed) {
 }
 yl_status GNL::forward(Net& net, const Act& x, const Act& y) {
   net.prof_begin(3);
-  yl_status st = gn_silu_forward(net.ctx, x.p, x.n, c, G, (long long)x.h * x.w, x.ld, 1e-6f, 0,
-                                 gamma, beta, 1, y.p, y.ld, 1, mean, rstd);
-  net.prof_end(3, 0.0, 2.0 * 4.0 * x.n * x.h * x.w * c + 4.0 * x.n * x.h * x.w * c);
+  const double e4 = 4.0 * x.n * x.h * x.w * c;
+  yl_status st;
+  if (stats_ready) {  // the producing conv wrote mean/rstd: one read + one write
+    st = gn_silu_apply(net.ctx, x.p, x.n, c, G, (long long)x.h * x.w, x.ld, mean, rstd, gamma,
+                       beta, 1, y.p, y.ld, 1);
+    net.prof_end(3, 0.0, 2.0 * e4);
+  } else {
+    st = gn_silu_forward(net.ctx, x.p, x.n, c, G, (long long)x.h * x.w, x.ld, 1e-6f, 0, gamma,
+                         beta, 1, y.p, y.ld, 1, mean, rstd);
+    net.prof_end(3, 0.0, 3.0 * e4);
+  }
+  stats_ready = false;
   return st;
 }
 yl_status GNL::backward(Net& net, const Act& x, const Act& dy, const Act& dx, const float* addend,
@@ -426,15 +443,15 @@ yl_status RB::init(yl_ctx* ctx, uint64_t seed) {
   if (has_skip) YL_TRY(skip.init(ctx, seed + 5));
   return YL_OK;
 }
-yl_status RB::forward(Net& net, const Act& x, const float* proj) {
+yl_status RB::forward(Net& net, const Act& x, const float* proj, GNL* gn_next) {
   YL_TRY(gn1.forward(net, x, h1));
-  YL_TRY(c1.forward(net, h1, c1o, nullptr, 0, proj));
+  YL_TRY(c1.forward(net, h1, c1o, nullptr, 0, proj, 0, 0, 0, &gn2));
   YL_TRY(gn2.forward(net, c1o, h2));
   if (has_skip) {
     YL_TRY(skip.forward(net, x, y));
-    return c2.forward(net, h2, y, y.p, y.ld);
+    return c2.forward(net, h2, y, y.p, y.ld, nullptr, 0, 0, 0, gn_next);
   }
-  return c2.forward(net, h2, y, x.p, x.ld);
+  return c2.forward(net, h2, y, x.p, x.ld, nullptr, 0, 0, 0, gn_next);
 }
 yl_status RB::backward(Net& net, const Act& x, const Act& dy, const Act& dx) {
   Act dh2 = h2, dc1 = c1o, dh1 = h1;
@@ -604,31 +621,31 @@ yl_status VAE::build(yl_ctx* c, int n, int h, int w, uint64_t seed) {
 }
 
 yl_status VAE::encode() {
-  YL_TRY(conv_in.forward(*this, x_in, a0));
-  YL_TRY(e1a.forward(*this, a0));
+  YL_TRY(conv_in.forward(*this, x_in, a0, nullptr, 0, nullptr, 0, 0, 0, &e1a.gn1));
+  YL_TRY(e1a.forward(*this, a0, nullptr, &e1b.gn1));
   YL_TRY(e1b.forward(*this, e1a.y));
-  YL_TRY(down1.forward(*this, e1b.y, a1));
-  YL_TRY(e2a.forward(*this, a1));
+  YL_TRY(down1.forward(*this, e1b.y, a1, nullptr, 0, nullptr, 0, 0, 0, &e2a.gn1));
+  YL_TRY(e2a.forward(*this, a1, nullptr, &e2b.gn1));
   YL_TRY(e2b.forward(*this, e2a.y));
-  YL_TRY(down2.forward(*this, e2b.y, a2));
-  YL_TRY(e3a.forward(*this, a2));
+  YL_TRY(down2.forward(*this, e2b.y, a2, nullptr, 0, nullptr, 0, 0, 0, &e3a.gn1));
+  YL_TRY(e3a.forward(*this, a2, nullptr, &e3b.gn1));
   YL_TRY(e3b.forward(*this, e3a.y));
-  YL_TRY(down3.forward(*this, e3b.y, a3));
+  YL_TRY(down3.forward(*this, e3b.y, a3, nullptr, 0, nullptr, 0, 0, 0, &gn_eo));
   YL_TRY(gn_eo.forward(*this, a3, hg));
   return conv_eo.forward(*this, hg, e);
 }
 
 yl_status VAE::decode() {
   YL_TRY(conv_z.forward(*this, z, b0));
-  YL_TRY(up1.forward(*this, b0, b1, nullptr, 0, nullptr, 1, b1.h, b1.w));
-  YL_TRY(d1a.forward(*this, b1));
+  YL_TRY(up1.forward(*this, b0, b1, nullptr, 0, nullptr, 1, b1.h, b1.w, &d1a.gn1));
+  YL_TRY(d1a.forward(*this, b1, nullptr, &d1b.gn1));
   YL_TRY(d1b.forward(*this, d1a.y));
-  YL_TRY(up2.forward(*this, d1b.y, b2, nullptr, 0, nullptr, 1, b2.h, b2.w));
-  YL_TRY(d2a.forward(*this, b2));
+  YL_TRY(up2.forward(*this, d1b.y, b2, nullptr, 0, nullptr, 1, b2.h, b2.w, &d2a.gn1));
+  YL_TRY(d2a.forward(*this, b2, nullptr, &d2b.gn1));
   YL_TRY(d2b.forward(*this, d2a.y));
-  YL_TRY(up3.forward(*this, d2b.y, b3, nullptr, 0, nullptr, 1, b3.h, b3.w));
-  YL_TRY(d3a.forward(*this, b3));
-  YL_TRY(d3b.forward(*this, d3a.y));
+  YL_TRY(up3.forward(*this, d2b.y, b3, nullptr, 0, nullptr, 1, b3.h, b3.w, &d3a.gn1));
+  YL_TRY(d3a.forward(*this, b3, nullptr, &d3b.gn1));
+  YL_TRY(d3b.forward(*this, d3a.y, nullptr, &gn_do));
   YL_TRY(gn_do.forward(*this, d3b.y, hd));
   return conv_do.forward(*this, hd, recon);
 }
@@ -827,28 +844,28 @@ yl_status UNet::forward() {
   for (int i = 0; i < kBlocks; ++i)
     YL_TRY(linear_forward(ctx, ts, proj[i].W, proj[i].b, pj[i], N, kTime, blocks[i]->cout));
   // down path
-  YL_TRY(conv_in.forward(*this, inp, h0));
-  YL_TRY(r1a.forward(*this, h0, pj[0]));
+  YL_TRY(conv_in.forward(*this, inp, h0, nullptr, 0, nullptr, 0, 0, 0, &r1a.gn1));
+  YL_TRY(r1a.forward(*this, h0, pj[0], &r1b.gn1));
   YL_TRY(r1b.forward(*this, r1a.y, pj[1]));
-  YL_TRY(dn1.forward(*this, r1b.y, p1));
-  YL_TRY(r2a.forward(*this, p1, pj[2]));
+  YL_TRY(dn1.forward(*this, r1b.y, p1, nullptr, 0, nullptr, 0, 0, 0, &r2a.gn1));
+  YL_TRY(r2a.forward(*this, p1, pj[2], &r2b.gn1));
   YL_TRY(r2b.forward(*this, r2a.y, pj[3]));
-  YL_TRY(dn2.forward(*this, r2b.y, p2));
-  YL_TRY(r3a.forward(*this, p2, pj[4]));
+  YL_TRY(dn2.forward(*this, r2b.y, p2, nullptr, 0, nullptr, 0, 0, 0, &r3a.gn1));
+  YL_TRY(r3a.forward(*this, p2, pj[4], &r3b.gn1));
   YL_TRY(r3b.forward(*this, r3a.y, pj[5]));
   // up path: up + conv written into the first half of the concat buffer, skip copied after it
   Act c1lo = cat1;
   c1lo.c = 256;
   YL_TRY(upc1.forward(*this, r3b.y, c1lo, nullptr, 0, nullptr, 1, cat1.h, cat1.w));
   YL_TRY(copy_slice(ctx, r2b.y.p, r2b.y.ld, cat1.p + 256, cat1.ld, cat1.pixels(), 256, 0));
-  YL_TRY(r4a.forward(*this, cat1, pj[6]));
+  YL_TRY(r4a.forward(*this, cat1, pj[6], &r4b.gn1));
   YL_TRY(r4b.forward(*this, r4a.y, pj[7]));
   Act c2lo = cat2;
   c2lo.c = 128;
   YL_TRY(upc2.forward(*this, r4b.y, c2lo, nullptr, 0, nullptr, 1, cat2.h, cat2.w));
   YL_TRY(copy_slice(ctx, r1b.y.p, r1b.y.ld, cat2.p + 128, cat2.ld, cat2.pixels(), 128, 0));
-  YL_TRY(r5a.forward(*this, cat2, pj[8]));
-  YL_TRY(r5b.forward(*this, r5a.y, pj[9]));
+  YL_TRY(r5a.forward(*this, cat2, pj[8], &r5b.gn1));
+  YL_TRY(r5b.forward(*this, r5a.y, pj[9], &gn_o));
   YL_TRY(gn_o.forward(*this, r5b.y, ho));
   // prediction = lerp(zA, zB, t) + net output (MotionMLP.swift:39-55), the fp32
   // lerp added in the epilogue

@@ -68,9 +68,11 @@ struct ConvL {
   yl_status init(yl_ctx* ctx, uint64_t seed, bool zero = false);
   yl_status prepare(yl_ctx* ctx);
   ConvGather gather(const Act& x, int oh, int ow, int up, int hv, int wv) const;
+  // gn_next: the GroupNorm that reads y; its statistics come out of this
+  // conv's epilogue when the channel grouping allows it
   yl_status forward(Net& net, const Act& x, const Act& y, const float* residual = nullptr,
                     int ldr = 0, const float* bias2d = nullptr, int up = 0, int hv = 0,
-                    int wv = 0);
+                    int wv = 0, struct GNL* gn_next = nullptr);
   yl_status backward(Net& net, const Act& x, const Act& dy, const Act* dx,
                      const float* dx_addend = nullptr, int ld_addend = 0,
                      float* dbias2d = nullptr, int up = 0, int hv = 0, int wv = 0);
@@ -82,6 +84,7 @@ struct GNL {
   size_t off_g = 0, off_b = 0;
   float *gamma = nullptr, *beta = nullptr, *ggamma = nullptr, *gbeta = nullptr;
   float *mean = nullptr, *rstd = nullptr;
+  bool stats_ready = false;  // mean/rstd already written by the producing conv
   void setup(Net& net, const char* name, int c);
   yl_status bind(Net& net, int n);
   yl_status init(yl_ctx* ctx, uint64_t seed);
@@ -114,7 +117,9 @@ struct RB {
   void setup(Net& net, const std::string& name, int cin, int cout, bool temb = false);
   yl_status bind(Net& net, int n, int h, int w);
   yl_status init(yl_ctx* ctx, uint64_t seed);
-  yl_status forward(Net& net, const Act& x, const float* proj = nullptr);
+  // gn_next: the GroupNorm that reads this block's output (statistics fused)
+  yl_status forward(Net& net, const Act& x, const float* proj = nullptr,
+                    GNL* gn_next = nullptr);
   yl_status backward(Net& net, const Act& x, const Act& dy, const Act& dx);
 };
 

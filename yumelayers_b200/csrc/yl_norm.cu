@@ -465,6 +465,15 @@ yl_status gn_silu_forward(yl_ctx* ctx, const float* x, int n, int c, int g, long
                          y, ldy);
 }
 
+yl_status gn_silu_apply(yl_ctx* ctx, const float* x, int n, int c, int g, long long hw, int ps,
+                        const float* mean, const float* rstd, const float* gamma,
+                        const float* beta, int silu, float* y, int ldy, int round) {
+  YL_TRY(gn_check(n, c, g, hw, ps));
+  YL_CHECK(ldy % 4 == 0, YL_ERR_SHAPE, "groupnorm: output stride must be a multiple of 4");
+  return gn_apply_launch(ctx, x, gn_geom(n, c, g, hw, ps), mean, rstd, gamma, beta, silu, round,
+                         y, ldy);
+}
+
 yl_status gn_silu_backward(yl_ctx* ctx, const float* x, const float* dy, int lddy, int n, int c,
                            int g, long long hw, int ps, const float* mean, const float* rstd,
                            const float* gamma, const float* beta, int silu, const float* addend,

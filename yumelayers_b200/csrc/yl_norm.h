@@ -15,6 +15,11 @@ yl_status gn_stats(yl_ctx* ctx, const float* x, int n, int c, int g, long long h
 yl_status gn_silu_forward(yl_ctx* ctx, const float* x, int n, int c, int g, long long hw, int ps,
                           float eps, int mode, const float* gamma, const float* beta, int silu,
                           float* y, int ldy, int round, float* mean, float* rstd);
+// The forward's second pass alone, with mean/rstd already computed (by the
+// convolution that produced x).
+yl_status gn_silu_apply(yl_ctx* ctx, const float* x, int n, int c, int g, long long hw, int ps,
+                        const float* mean, const float* rstd, const float* gamma,
+                        const float* beta, int silu, float* y, int ldy, int round);
 // dx = d/dx of the forward given dy (+ addend); dgamma/dbeta overwritten or
 // accumulated.
 yl_status gn_silu_backward(yl_ctx* ctx, const float* x, const float* dy, int lddy, int n, int c,
