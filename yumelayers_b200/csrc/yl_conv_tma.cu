@@ -920,6 +920,8 @@ static yl_status run_plan(yl_ctx* ctx, const View* views, int nviews, const floa
     if (tall) return launch_plan<64, 2>(ctx, views, nviews, w, w_rows, w_cols, p, nphase, e);
     return launch_plan<64, 1>(ctx, views, nviews, w, w_rows, w_cols, p, nphase, e);
   }
+  if (tall && e.n_total % 128 == 0 && min_nk >= 9)
+    return launch_plan<128, 2, true>(ctx, views, nviews, w, w_rows, w_cols, p, nphase, e);
   if (e.n_total <= 128 || e.n_total % 256 != 0) {
     if (tall && e.n_total <= 128 && min_nk >= 9)
       return launch_plan<128, 2, true>(ctx, views, nviews, w, w_rows, w_cols, p, nphase, e);
