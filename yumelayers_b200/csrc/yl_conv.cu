@@ -579,6 +579,78 @@ yl_status weight_permute(yl_ctx* ctx, const float* in, float* out, int O, int T,
   return check_launch("weight_permute_kernel");
 }
 
+// 3x3 neighbourhoods of a 4-channel NHWC tensor as 64-channel pixels:
+// out[p][t * 4 + c] = src[p + sign * (ky - 1, kx - 1)][c] for tap t = ky * 3 + kx
+// (zero outside the image), channels 36..63 zero.  With sign +1 a 3x3 conv of
+// src becomes a 1x1 conv of out; with sign -1 (src = an output gradient) the
+// same patches give the conv's dX and dW as 1x1 GEMMs.
+__global__ void rgb_patches_kernel(const float* __restrict__ src, int ld, int n, int h, int w,
+                                   int sign, int round, float* __restrict__ out) {
+  const long long total = (long long)n * h * w * 16;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int t = (int)(i & 15);
+    const long long pix = i >> 4;
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (t < 9) {
+      const int x = (int)(pix % w);
+      const long long r = pix / w;
+      const int y = (int)(r % h);
+      const long long img = r / h;
+      const int yy = y + sign * (t / 3 - 1), xx = x + sign * (t % 3 - 1);
+      if (yy >= 0 && yy < h && xx >= 0 && xx < w) {
+        v = __ldg(reinterpret_cast<const float4*>(src + ((img * h + yy) * w + xx) * ld));
+        if (round) v = make_float4(round_tf32(v.x), round_tf32(v.y), round_tf32(v.z), round_tf32(v.w));
+      }
+    }
+    reinterpret_cast<float4*>(out)[i] = v;
+  }
+}
+
+yl_status rgb_patches(yl_ctx* ctx, const float* src, int ld, int n, int h, int w, int sign,
+                      int round, float* out) {
+  YL_CHECK(ld % 4 == 0 && ((uintptr_t)src & 15) == 0 && ((uintptr_t)out & 15) == 0, YL_ERR_SHAPE,
+           "rgb_patches: 16-byte pixels required");
+  rgb_patches_kernel<<<grid_1d((long long)n * h * w * 16, 256), 256, 0, ctx->stream>>>(
+      src, ld, n, h, w, sign, round, out);
+  return check_launch("rgb_patches_kernel");
+}
+
+// y[p][c] = bias[c] + sum_t z[p + (ky - 1, kx - 1)][t * 4 + c]: the tap sum
+// that turns the 36-channel 1x1 product z = x * W[t][c] into the 3x3 conv
+// with 4 output channels.
+__global__ void rgb_tap_sum_kernel(const float* __restrict__ z, int n, int h, int w,
+                                   const float* __restrict__ bias, float* __restrict__ y,
+                                   int ldy) {
+  const long long total = (long long)n * h * w;
+  for (long long pix = blockIdx.x * (long long)blockDim.x + threadIdx.x; pix < total;
+       pix += (long long)gridDim.x * blockDim.x) {
+    const int x = (int)(pix % w);
+    const long long r = pix / w;
+    const int yv = (int)(r % h);
+    const long long img = r / h;
+    float4 acc = bias ? make_float4(bias[0], bias[1], bias[2], bias[3])
+                      : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int t = 0; t < 9; ++t) {
+      const int yy = yv + t / 3 - 1, xx = x + t % 3 - 1;
+      if (yy < 0 || yy >= h || xx < 0 || xx >= w) continue;
+      const float4 v = __ldg(reinterpret_cast<const float4*>(z + ((img * h + yy) * w + xx) * 36) + t);
+      acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+    }
+    *reinterpret_cast<float4*>(y + pix * ldy) = acc;
+  }
+}
+
+yl_status rgb_tap_sum(yl_ctx* ctx, const float* z, int n, int h, int w, const float* bias,
+                      float* y, int ldy) {
+  YL_CHECK(ldy % 4 == 0 && ((uintptr_t)z & 15) == 0 && ((uintptr_t)y & 15) == 0, YL_ERR_SHAPE,
+           "rgb_tap_sum: 16-byte pixels required");
+  rgb_tap_sum_kernel<<<grid_1d((long long)n * h * w, 256), 256, 0, ctx->stream>>>(z, n, h, w, bias,
+                                                                                 y, ldy);
+  return check_launch("rgb_tap_sum_kernel");
+}
+
 // 32 x 32 tiled transposes between [n][c][hw] and [n][hw][ps].
 __global__ void nchw_to_nhwc_kernel(const float* __restrict__ in, float* __restrict__ out, int c,
                                     long long hw, int ps, int round) {

@@ -83,8 +83,13 @@ __device__ __forceinline__ FpropTile fprop_tile(const ConvPlan& p, int t) {
 template <int CG>
 __device__ __forceinline__ void gn_chunk_partials(const float (&v)[32], bool valid,
                                                   float2* part_row, int g0, int lane) {
+  // per-lane (sum, sumsq) of each of the chunk's 32/CG groups, then a
+  // transposing butterfly: every exchange halves the values a lane keeps until
+  // one group is left, then plain xor steps finish that group's sum
+  constexpr int NG = 32 / CG;
+  float val[2 * NG];
 #pragma unroll
-  for (int k = 0; k < 32 / CG; ++k) {
+  for (int k = 0; k < NG; ++k) {
     float s = 0.f, ss = 0.f;
     if (valid) {
 #pragma unroll
@@ -94,13 +99,30 @@ __device__ __forceinline__ void gn_chunk_partials(const float (&v)[32], bool val
         ss += x * x;
       }
     }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      s += __shfl_xor_sync(0xffffffffu, s, o);
-      ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    }
-    if (lane == 0) part_row[g0 + k] = make_float2(s, ss);
+    val[2 * k] = s;
+    val[2 * k + 1] = ss;
   }
+  int grp = 0;
+#pragma unroll
+  for (int o = 16, n = 2 * NG; o >= 1; o >>= 1) {
+    if (n > 2) {
+      const bool upper = (lane & o) != 0;
+#pragma unroll
+      for (int i = 0; i < n / 2; ++i) {
+        const float send = upper ? val[i] : val[i + n / 2];
+        const float keep = upper ? val[i + n / 2] : val[i];
+        val[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+      }
+      grp = grp * 2 + (upper ? 1 : 0);
+      n /= 2;
+    } else {
+      val[0] += __shfl_xor_sync(0xffffffffu, val[0], o);
+      val[1] += __shfl_xor_sync(0xffffffffu, val[1], o);
+    }
+  }
+  // lanes that differ only in the plain-reduction bits hold the same group
+  constexpr int kSplitBits = NG == 8 ? 3 : NG == 4 ? 2 : NG == 2 ? 1 : 0;
+  if ((lane & ((1 << (5 - kSplitBits)) - 1)) == 0) part_row[g0 + grp] = make_float2(val[0], val[1]);
 }
 
 __device__ __forceinline__ void gn_chunk_partials_any(int cg, const float (&v)[32], bool valid,
@@ -826,20 +848,20 @@ bool conv_gn_stats_supported(int n_total, int groups) {
   return cg == 4 || cg == 8 || cg == 16 || cg == 32;
 }
 
-// mean/rstd per (image, group) from the per-tile partials: one warp per
-// (image, group), fixed-order double sums over the image's tiles and slots.
-__global__ void gn_tile_stats_kernel(const float2* __restrict__ part, ConvPlan p, int nphase,
-                                     int slots, int gpb, int groups, int cg, float eps,
-                                     float* __restrict__ mean, float* __restrict__ rstd) {
-  const int idx = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
-  const int lane = threadIdx.x & 31;
-  if (idx >= p.n_img * groups) return;
+// mean/rstd per (image, group) from the per-tile partials: one 128-thread
+// block per (image, group); each thread sums a fixed strided subset of the
+// image's (tile, slot) entries in double, then a fixed shared-memory tree.
+__global__ void __launch_bounds__(128) gn_tile_stats_kernel(
+    const float2* __restrict__ part, ConvPlan p, int nphase, int slots, int gpb, int groups,
+    int cg, float eps, float* __restrict__ mean, float* __restrict__ rstd) {
+  __shared__ double sh[2][128];
+  const int idx = blockIdx.x;  // img * groups + g
   const int img = idx / groups, g = idx % groups;
   const int nb = g / gpb, gb = g % gpb;
   const int tpi = p.tiles_x * p.tiles_y;
   const long long items = (long long)nphase * tpi * slots;
   double s = 0.0, ss = 0.0;
-  for (long long i = lane; i < items; i += 32) {
+  for (long long i = threadIdx.x; i < items; i += blockDim.x) {
     const int z = (int)(i / ((long long)tpi * slots));
     const long long rem = i - (long long)z * tpi * slots;
     const int pix = img * tpi + (int)(rem / slots), slot = (int)(rem % slots);
@@ -848,15 +870,20 @@ __global__ void gn_tile_stats_kernel(const float2* __restrict__ part, ConvPlan p
     s += v.x;
     ss += v.y;
   }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    s += __shfl_xor_sync(0xffffffffu, s, o);
-    ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  sh[0][threadIdx.x] = s;
+  sh[1][threadIdx.x] = ss;
+  __syncthreads();
+  for (int o = 64; o > 0; o >>= 1) {
+    if (threadIdx.x < o) {
+      sh[0][threadIdx.x] += sh[0][threadIdx.x + o];
+      sh[1][threadIdx.x] += sh[1][threadIdx.x + o];
+    }
+    __syncthreads();
   }
-  if (lane) return;
+  if (threadIdx.x) return;
   const double cnt = (double)p.out_h * p.out_w * cg;
-  const double m = s / cnt;
-  double var = ss / cnt - m * m;
+  const double m = sh[0][0] / cnt;
+  double var = sh[1][0] / cnt - m * m;
   if (var < 0) var = 0;
   mean[idx] = (float)m;
   rstd[idx] = (float)(1.0 / sqrt(var + (double)eps));
@@ -898,8 +925,7 @@ static yl_status launch_plan(yl_ctx* ctx, const View* views, int nviews, const f
       ta[0], ta[1], ta[2], ta[3], tw, p, ek, ctx->dev_err);
   YL_TRY(check_launch("conv_tma_fprop_kernel"));
   if (!e.gn_mean) return YL_OK;
-  const int warps = p.n_img * e.gn_groups;
-  gn_tile_stats_kernel<<<(warps + 7) / 8, 256, 0, ctx->stream>>>(
+  gn_tile_stats_kernel<<<p.n_img * e.gn_groups, 128, 0, ctx->stream>>>(
       ek.gn_part, p, nphase, slots, gpb, e.gn_groups, ek.gn_cg, e.gn_eps, e.gn_mean, e.gn_rstd);
   return check_launch("gn_tile_stats_kernel");
 }
@@ -1121,6 +1147,7 @@ struct WgTile {
 
 static WgTile wgrad_tile(int cout, int n_total) {
   if (n_total == 288) return {1, 3, 96, 16};  // 9 taps of one (padded) 32-channel atom
+  if (n_total == 64) return {1, 1, 64, 32};   // 1x1 over 64-channel patches
   if (cout % 256 == 0 && n_total % 256 == 0) return {2, 1, 256, 16};
   if (cout <= 128 && n_total % 512 == 0) return {1, 2, 256, 16};
   if (n_total % 384 == 0) return {1, 2, 192, 16};
@@ -1323,6 +1350,8 @@ yl_status conv_wgrad_ws(yl_ctx* ctx, const float* dy, int ldy, int cout, const C
   w.db_ws = db ? ws + db_off : nullptr;
   if (tile.nsub == 3)
     YL_TRY((launch_wgrad<1, 3, 96, 16>(ctx, av, nav, bv, nbv, w, splits, col_blocks)));
+  else if (tile.nw == 64)
+    YL_TRY((launch_wgrad<1, 1, 64, 32>(ctx, av, nav, bv, nbv, w, splits, col_blocks)));
   else if (tile.mt == 2)
     YL_TRY((launch_wgrad<2, 1, 256, 16>(ctx, av, nav, bv, nbv, w, splits, col_blocks)));
   else if (tile.nsub == 2 && tile.nw == 256)

@@ -98,6 +98,15 @@ yl_status nchw_to_nhwc(yl_ctx* ctx, const float* in, float* out, int n, int c, l
 yl_status nhwc_to_nchw(yl_ctx* ctx, const float* in, float* out, int n, int c, long long hw,
                        int ps);
 
+// 3x3 patches of a 4-channel NHWC tensor (pixel stride ld) as 64-channel
+// pixels [n*h*w][64]: out[p][t*4 + c] = src[p + sign*(ky-1, kx-1)][c].
+yl_status rgb_patches(yl_ctx* ctx, const float* src, int ld, int n, int h, int w, int sign,
+                      int round, float* out);
+// y[p][0..3] = bias + sum over the 9 taps t of z[p + (ky-1, kx-1)][t*4 + 0..3]
+// (z is [n*h*w][36]).
+yl_status rgb_tap_sum(yl_ctx* ctx, const float* z, int n, int h, int w, const float* bias,
+                      float* y, int ldy);
+
 // dst[img][y][x][c] += / = sum of the 2x2 block of src (an up x2 grid of
 // uh x uw, cropped) -- the adjoint of nearest upsampling into (h, w).
 yl_status downsample_sum_nhwc(yl_ctx* ctx, const float* src, int uh, int uw, float* dst, int n,

@@ -185,6 +185,7 @@ void ConvL::setup(Net& net, const char* nm, int cin_, int cout_, int k_, int str
   k = k_;
   stride = stride_;
   pad = pad_;
+  rgb = (k == 3 && stride == 1 && pad == 1) ? (cin_p == 4 ? 1 : cout_p == 4 ? 2 : 0) : 0;
   off_w = net.params.reserve((size_t)cout_p * k * k * cin_p);
   off_b = net.params.reserve(cout_p);
   net.param_table.push_back({name + ".weight", off_w, cout, cin, k, k});
@@ -198,6 +199,11 @@ yl_status ConvL::bind(Net& net) {
   gb = net.params.g + off_b;
   YL_TRY(net.arena.alloc((size_t)cout_p * k * k * cin_p, &Wr));
   YL_TRY(net.arena.alloc((size_t)cin_p * k * k * cout_p, &Wd));
+  if (rgb == 1) YL_TRY(net.arena.alloc((size_t)cout_p * 64, &Wx));
+  if (rgb == 2) {
+    YL_TRY(net.arena.alloc((size_t)36 * cin_p, &Wx));
+    YL_TRY(net.arena.alloc((size_t)cin_p * 64, &Wx2));
+  }
   return YL_OK;
 }
 yl_status ConvL::init(yl_ctx* ctx, uint64_t seed, bool zero) {
@@ -213,7 +219,36 @@ yl_status ConvL::init(yl_ctx* ctx, uint64_t seed, bool zero) {
 yl_status ConvL::prepare(yl_ctx* ctx) {
   const int kk = k * k;
   YL_TRY(weight_permute(ctx, W, Wr, cout_p, kk, cin_p, cin_p, (long long)kk * cin_p, cin_p, 1, 1));
-  return weight_permute(ctx, W, Wd, cin_p, kk, cout_p, cout_p, 1, cin_p, (long long)kk * cin_p, 1);
+  YL_TRY(weight_permute(ctx, W, Wd, cin_p, kk, cout_p, cout_p, 1, cin_p, (long long)kk * cin_p, 1));
+  if (rgb == 1)  // [cout][t*4 + ci], zero-padded to 64 columns
+    YL_TRY(weight_permute(ctx, Wr, Wx, cout_p, 1, 64, 36, 36, 0, 1, 0));
+  if (rgb == 2) {
+    // [t*4 + co][ci] = W[co][t][ci] and [ci][t*4 + co] (from the dgrad copy), padded
+    YL_TRY(weight_permute(ctx, Wr, Wx, 9, 4, cin_p, cin_p, cin_p, 9LL * cin_p, 1, 0));
+    YL_TRY(weight_permute(ctx, Wd, Wx2, cin_p, 1, 64, 36, 36, 0, 1, 0));
+  }
+  return YL_OK;
+}
+
+// A 1x1 gather over an NHWC tensor of ps floats per pixel (c channels).
+static ConvGather pointwise(const float* src, int n, int h, int w, int ps, int c) {
+  ConvGather g;
+  g.src = src;
+  g.img_stride = (long long)h * w * ps;
+  g.row_stride = w * ps;
+  g.ps = ps;
+  g.cin = c;
+  g.hv = h;
+  g.wv = w;
+  g.mode = MODE_FPROP;
+  g.ksize = 1;
+  g.stride = 1;
+  g.pad = 0;
+  g.oh = h;
+  g.ow = w;
+  g.m_total = n * h * w;
+  g.k_total = c;
+  return g;
 }
 
 ConvGather ConvL::gather(const Act& x, int oh, int ow, int up, int hv, int wv) const {
@@ -239,6 +274,51 @@ ConvGather ConvL::gather(const Act& x, int oh, int ow, int up, int hv, int wv) c
 
 yl_status ConvL::forward(Net& net, const Act& x, const Act& y, const float* residual, int ldr,
                          const float* bias2d, int up, int hv, int wv, GNL* gn_next) {
+  if (rgb == 2 && !residual && !bias2d && !up && !gn_next) {
+    // 4 output channels: z[p][t*4 + co] = x[p] . W[co][t] as one 1x1 GEMM, then the tap sum
+    float* z = nullptr;
+    YL_TRY(net.pool.get((size_t)x.n * x.h * x.w * 36, &z));
+    ConvEpilogue e;
+    e.out = z;
+    e.ldo = 36;
+    e.n_total = 36;
+    e.round_tf32 = 0;
+    net.prof_begin(0);
+    YL_TRY(conv_fprop(net.ctx, pointwise(x.p, x.n, x.h, x.w, x.ld, cin_p), Wx, 36, e));
+    YL_TRY(rgb_tap_sum(net.ctx, z, x.n, x.h, x.w, b, y.p, y.ld));
+    net.prof_end(0, 2.0 * x.pixels() * cout * cin * k * k);
+    net.pool.put(z);
+    return YL_OK;
+  }
+  if (rgb == 1 && !up) {
+    // 4 input channels: a 1x1 GEMM over the 64-channel 3x3 patches of x
+    float* xp = nullptr;
+    YL_TRY(net.pool.get((size_t)x.n * x.h * x.w * 64, &xp));
+    YL_TRY(rgb_patches(net.ctx, x.p, x.ld, x.n, x.h, x.w, 1, 1, xp));
+    ConvEpilogue e;
+    e.out = y.p;
+    e.ldo = y.ld;
+    e.n_total = cout_p;
+    e.bias = b;
+    e.bias2d = bias2d;
+    e.residual = residual;
+    e.ldr = ldr;
+    e.round_tf32 = 1;
+    const bool fuse_gn =
+        gn_next && gn_next->c == cout_p && conv_gn_stats_supported(cout_p, gn_next->G);
+    if (fuse_gn) {
+      e.gn_mean = gn_next->mean;
+      e.gn_rstd = gn_next->rstd;
+      e.gn_groups = gn_next->G;
+    }
+    net.prof_begin(0);
+    yl_status st =
+        conv_fprop(net.ctx, pointwise(xp, x.n, x.h, x.w, 64, 64), Wx, cout_p, e);
+    net.prof_end(0, 2.0 * x.pixels() * cout * cin * k * k);
+    net.pool.put(xp);
+    if (st == YL_OK && fuse_gn) gn_next->stats_ready = true;
+    return st;
+  }
   ConvGather g = gather(x, y.h, y.w, up, hv, wv);
   ConvEpilogue e;
   e.out = y.p;
@@ -267,6 +347,51 @@ yl_status ConvL::backward(Net& net, const Act& x, const Act& dy, const Act* dx,
                           const float* dx_addend, int ld_addend, float* dbias2d, int up, int hv,
                           int wv) {
   yl_ctx* ctx = net.ctx;
+  if (rgb == 1 && !up && !dbias2d) {
+    // dW[co][t*4 + ci] = sum_p dy[p][co] * patches(x)[p][t*4 + ci]; db fused
+    float *xp = nullptr, *dw = nullptr;
+    YL_TRY(net.pool.get((size_t)x.n * x.h * x.w * 64, &xp));
+    YL_TRY(net.pool.get((size_t)cout_p * 64, &dw));
+    YL_TRY(rgb_patches(ctx, x.p, x.ld, x.n, x.h, x.w, 1, 1, xp));
+    net.prof_begin(2);
+    YL_TRY(conv_wgrad(ctx, dy.p, dy.ld, cout_p, pointwise(xp, x.n, x.h, x.w, 64, 64), dw, 0, gb));
+    net.prof_end(2, 2.0 * x.pixels() * cout * cin * k * k);
+    YL_TRY(weight_permute(ctx, dw, gW, cout_p, 1, 36, 36, 64, 0, 1, 0));
+    net.pool.put(xp);
+    net.pool.put(dw);
+    if (dx) return set_error(YL_ERR_UNSUPPORTED, "%s: dX of a 4-channel input", name.c_str());
+    return YL_OK;
+  }
+  if (rgb == 2 && !up && !dbias2d && dx) {
+    // d[p][t*4 + co] = dy[p - (ky-1, kx-1)][co]: dX = d . Wx2^T and
+    // dW[t*4 + co][ci] = sum_p d[p][t*4 + co] x[p][ci], both 1x1 GEMMs
+    float *d = nullptr, *dw = nullptr, *db = nullptr;
+    YL_TRY(net.pool.get((size_t)x.n * x.h * x.w * 64, &d));
+    YL_TRY(net.pool.get((size_t)64 * cin_p, &dw));
+    YL_TRY(net.pool.get(64, &db));
+    YL_TRY(rgb_patches(ctx, dy.p, dy.ld, x.n, x.h, x.w, -1, 1, d));
+    net.prof_begin(2);
+    YL_TRY(conv_wgrad(ctx, d, 64, 64, pointwise(x.p, x.n, x.h, x.w, x.ld, cin_p), dw, 0, db));
+    net.prof_end(2, 2.0 * x.pixels() * cout * cin * k * k);
+    YL_TRY(weight_permute(ctx, dw, gW, 4, 9, cin_p, cin_p, cin_p, 4LL * cin_p, 1, 0));
+    // the bias gradient is the centre tap's column sums (t = 4: no shift)
+    YL_CUDA(cudaMemcpyAsync(gb, db + 16, 4 * sizeof(float), cudaMemcpyDeviceToDevice,
+                            ctx->stream));
+    ConvEpilogue e;
+    e.out = dx->p;
+    e.ldo = dx->ld;
+    e.n_total = cin_p;
+    e.residual = dx_addend;
+    e.ldr = ld_addend;
+    e.round_tf32 = 1;
+    net.prof_begin(1);
+    YL_TRY(conv_fprop(ctx, pointwise(d, x.n, x.h, x.w, 64, 64), Wx2, cin_p, e));
+    net.prof_end(1, 2.0 * x.pixels() * cout * cin * k * k);
+    net.pool.put(d);
+    net.pool.put(dw);
+    net.pool.put(db);
+    return YL_OK;
+  }
   // dW (split-K tcgen05, MN-major operands) and db (fixed-order column sums)
   ConvGather g = gather(x, dy.h, dy.w, up, hv, wv);
   net.prof_begin(2);
