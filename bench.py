@@ -285,6 +285,12 @@ def run_native(args):
                 "unit": "TFLOP/s", "frac": achieved / tf32_peak, "traffic": None,
                 "peak_note": (f"tf32 peak = 1/2 of the {peak_src} dense bf16 "
                               f"{bf16:.1f} TFLOP/s (no tf32 peak is measured)"),
+                "flops_note": ("achieved counts 2*N*Cout*Cin*k*k*OH*OW per conv pass; "
+                               "upsample convs execute 16/36 of that through merged "
+                               "phase taps"),
+                "traffic_note": ("per-launch DRAM bytes of the dominant launch type are in "
+                                 "profiles/conv_tma_fprop_128ch_2x480x856.md (equal to the "
+                                 "algorithmic bytes); the class mixes layer shapes"),
                 "all_convs": {"achieved": conv_flops / (conv_ms * 1e-3) / 1e12,
                               "frac": conv_flops / (conv_ms * 1e-3) / 1e12 / tf32_peak}}
     act_gb = tr.activation_bytes() / 1e9
