@@ -380,6 +380,9 @@ typedef struct yl_conv_profile {
 } yl_conv_profile;
 yl_status yl_profile_conv(yl_ctx* ctx, int n, int c, int h, int w, int oc, int k, int stride,
                           int up, int reps, yl_conv_profile* out);
+/* One multi-tensor Adam step over n parameters split into `tensors` (<= 48)
+ * tensors; *ms = average device time of one step.  Diagnostic only. */
+yl_status yl_profile_adam(yl_ctx* ctx, long long n, int tensors, int reps, double* ms);
 /* GroupNorm(32)+SiLU forward and backward on an n x h x w x c NHWC tensor. */
 yl_status yl_profile_groupnorm(yl_ctx* ctx, int n, int c, int h, int w, int reps, double* fwd_ms,
                                double* bwd_ms);

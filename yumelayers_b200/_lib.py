@@ -198,3 +198,4 @@ class ConvProfile(C.Structure):
 
 SIGNATURES["yl_profile_conv"] = [P, I, I, I, I, I, I, I, I, I, C.POINTER(ConvProfile)]
 SIGNATURES["yl_profile_groupnorm"] = [P, I, I, I, I, I, C.POINTER(D), C.POINTER(D)]
+SIGNATURES["yl_profile_adam"] = [P, C.c_longlong, I, I, C.POINTER(D)]

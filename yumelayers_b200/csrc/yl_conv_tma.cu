@@ -573,9 +573,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_arrive_expect_tx(&full[s], Cfg::kStage);
         for (int a = 0; a < Cfg::kAAtoms; a += w.ga)
           tma_load_5d(a_dst + a * Cfg::kAtomBytes, amap, &full[s], 0, gx0, gy, m0 / 32 + a, im);
-        for (int j = 0; j < Cfg::kBAtoms; j += w.gb)
-          tma_load_5d(b_dst + j * Cfg::kAtomBytes, bmaps[at[j].map], &full[s], 0,
-                      gx0 + at[j].bx, gy + at[j].by, at[j].ci / 32, im);
+        // the atom table stays in registers: both loops have constant trip counts
+        if (w.gb == 4) {
+#pragma unroll
+          for (int j = 0; j < Cfg::kBAtoms; j += 4)
+            tma_load_5d(b_dst + j * Cfg::kAtomBytes, bmaps[at[j].map], &full[s], 0,
+                        gx0 + at[j].bx, gy + at[j].by, at[j].ci / 32, im);
+        } else {
+#pragma unroll
+          for (int j = 0; j < Cfg::kBAtoms; ++j)
+            tma_load_5d(b_dst + j * Cfg::kAtomBytes, bmaps[at[j].map], &full[s], 0,
+                        gx0 + at[j].bx, gy + at[j].by, at[j].ci / 32, im);
+        }
         if (++xb == w.xblocks) {
           xb = 0;
           if (++gy == w.gh) {

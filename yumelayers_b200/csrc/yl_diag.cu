@@ -2,6 +2,7 @@
 // reference's profileConv / runGpuBench (Diagnostics.swift:83-201), timing
 // one conv shape's forward, dX and dW kernels (and GroupNorm+SiLU) with CUDA
 // events on NHWC buffers the call allocates itself.
+#include <algorithm>
 #include <vector>
 
 #include "yl_kernels.h"
@@ -139,6 +140,44 @@ yl_status yl_profile_conv(yl_ctx* ctx, int n, int c, int h, int w, int oc, int k
   out->wgrad_ms = ms[2];
   out->flops = 2.0 * n * oh * ow * (double)oc * c * k * k;
   out->wgrad_splits = splits;
+  return yl_ctx_check_device_errors(ctx);
+}
+
+yl_status yl_profile_adam(yl_ctx* ctx, long long n, int tensors, int reps, double* ms_out) {
+  YL_CHECK(ctx && ms_out && reps >= 1 && n > 0 && tensors >= 1 && tensors <= 48, YL_ERR_INVALID,
+           "yl_profile_adam: bad argument");
+  DevBufs b;
+  float *p, *g, *m, *v;
+  YL_TRY(b.get((size_t)n, &p));
+  YL_TRY(b.get((size_t)n, &g));
+  YL_TRY(b.get((size_t)n, &m));
+  YL_TRY(b.get((size_t)n, &v));
+  fill_kernel<<<1024, 256, 0, ctx->stream>>>(p, n, 9, 1.f);
+  fill_kernel<<<1024, 256, 0, ctx->stream>>>(g, n, 10, 0.1f);
+  YL_CUDA(cudaMemsetAsync(m, 0, (size_t)n * sizeof(float), ctx->stream));
+  YL_CUDA(cudaMemsetAsync(v, 0, (size_t)n * sizeof(float), ctx->stream));
+  YL_TRY(check_launch("fill_kernel"));
+  // the flat buffer split into `tensors` consecutive tensors, like a model's table
+  AdamTensor table[48];
+  // tensor sizes rounded up to 4 floats, as every tensor of the models is
+  const long long per = ((n + tensors - 1) / tensors + 3) & ~3LL;
+  int count = 0;
+  for (long long o = 0; o < n; o += per, ++count)
+    table[count] = AdamTensor{p + o, g + o, m + o, v + o, std::min(per, n - o)};
+  cudaEvent_t e0, e1;
+  YL_CUDA(cudaEventCreate(&e0));
+  YL_CUDA(cudaEventCreate(&e1));
+  for (int rr = -1; rr < reps; ++rr) {
+    if (rr == 0) YL_CUDA(cudaEventRecord(e0, ctx->stream));
+    YL_TRY(adam_multi(ctx, table, count, 2e-4f, 0.9f, 0.999f, 1e-8f, rr + 2, 1.f, 0.f, 0, nullptr));
+  }
+  YL_CUDA(cudaEventRecord(e1, ctx->stream));
+  YL_CUDA(cudaEventSynchronize(e1));
+  float t = 0.f;
+  YL_CUDA(cudaEventElapsedTime(&t, e0, e1));
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  *ms_out = t / reps;
   return yl_ctx_check_device_errors(ctx);
 }
 

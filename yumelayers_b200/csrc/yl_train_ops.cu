@@ -19,7 +19,8 @@ namespace yl {
 constexpr int kMaxAdamTensors = 48;
 struct AdamPack {
   AdamTensor t[kMaxAdamTensors];
-  long long start[kMaxAdamTensors + 1];  // element prefix sums
+  long long start[kMaxAdamTensors + 1];   // element prefix sums
+  long long istart[kMaxAdamTensors + 1];  // work-item prefix sums (update kernel)
   int count;
 };
 
@@ -68,6 +69,20 @@ __global__ void adam_norm_final_kernel(const double* part, int nb, float* norm) 
   }
 }
 
+__device__ __forceinline__ void adam_elem(float& p, float& m, float& v, float graw, float lr,
+                                          float b1, float b2, float eps, float c1, float c2,
+                                          float scale, int sanitize, float clipf) {
+  const float g = sanitize_scale(graw, scale, sanitize) * clipf;
+  m = b1 * m + (1.f - b1) * g;
+  v = b2 * v + (1.f - b2) * g * g;
+  p -= lr * (m / c1) / (sqrtf(v / c2) + eps);
+}
+
+// Work items of kAdamChunk consecutive elements of one tensor; a block walks
+// items with a grid stride and updates four elements per thread and step
+// (16-byte loads) when the item's four arrays are 16-byte aligned.
+constexpr long long kAdamChunk = 8192;
+
 __global__ void adam_update_kernel(const __grid_constant__ AdamPack p, float lr, float b1, float b2,
                                    float eps, float c1, float c2, float scale, int sanitize,
                                    float clip, const float* norm) {
@@ -76,18 +91,38 @@ __global__ void adam_update_kernel(const __grid_constant__ AdamPack p, float lr,
     const float nv = *norm;
     if (nv > clip) clipf = clip / nv;
   }
-  const long long total = p.start[p.count];
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
-       i += (long long)gridDim.x * blockDim.x) {
-    const int k = adam_find(p, i);
-    const long long j = i - p.start[k];
+  const long long items = p.istart[p.count];
+  for (long long it = blockIdx.x; it < items; it += gridDim.x) {
+    int k = 0;
+    while (k + 1 < p.count && p.istart[k + 1] <= it) ++k;
     const AdamTensor& t = p.t[k];
-    const float g = sanitize_scale(t.grad[j], scale, sanitize) * clipf;
-    const float m = b1 * t.m[j] + (1.f - b1) * g;
-    const float v = b2 * t.v[j] + (1.f - b2) * g * g;
-    t.m[j] = m;
-    t.v[j] = v;
-    t.param[j] -= lr * (m / c1) / (sqrtf(v / c2) + eps);
+    const long long c0 = (it - p.istart[k]) * kAdamChunk;
+    const long long c1e = min(t.n, c0 + kAdamChunk);
+    float *pp = t.param + c0, *mp = t.m + c0, *vp = t.v + c0;
+    const float* gp = t.grad + c0;
+    const long long len = c1e - c0;
+    const bool vec = ((reinterpret_cast<uintptr_t>(pp) | reinterpret_cast<uintptr_t>(mp) |
+                       reinterpret_cast<uintptr_t>(vp) | reinterpret_cast<uintptr_t>(gp)) &
+                      15) == 0;
+    long long done = 0;
+    if (vec) {
+      const long long n4 = len >> 2;
+      for (long long q = threadIdx.x; q < n4; q += blockDim.x) {
+        float4 P = reinterpret_cast<float4*>(pp)[q], M = reinterpret_cast<float4*>(mp)[q];
+        float4 V = reinterpret_cast<float4*>(vp)[q];
+        const float4 G = __ldg(reinterpret_cast<const float4*>(gp) + q);
+        adam_elem(P.x, M.x, V.x, G.x, lr, b1, b2, eps, c1, c2, scale, sanitize, clipf);
+        adam_elem(P.y, M.y, V.y, G.y, lr, b1, b2, eps, c1, c2, scale, sanitize, clipf);
+        adam_elem(P.z, M.z, V.z, G.z, lr, b1, b2, eps, c1, c2, scale, sanitize, clipf);
+        adam_elem(P.w, M.w, V.w, G.w, lr, b1, b2, eps, c1, c2, scale, sanitize, clipf);
+        reinterpret_cast<float4*>(pp)[q] = P;
+        reinterpret_cast<float4*>(mp)[q] = M;
+        reinterpret_cast<float4*>(vp)[q] = V;
+      }
+      done = n4 << 2;
+    }
+    for (long long j = done + threadIdx.x; j < len; j += blockDim.x)
+      adam_elem(pp[j], mp[j], vp[j], gp[j], lr, b1, b2, eps, c1, c2, scale, sanitize, clipf);
   }
 }
 
@@ -109,11 +144,13 @@ yl_status adam_multi(yl_ctx* ctx, const AdamTensor* tensors, int count, float lr
     AdamPack p;
     p.count = count - base < kMaxAdamTensors ? count - base : kMaxAdamTensors;
     p.start[0] = 0;
+    p.istart[0] = 0;
     for (int k = 0; k < p.count; ++k) {
       p.t[k] = tensors[base + k];
       YL_CHECK(p.t[k].param && p.t[k].grad && p.t[k].m && p.t[k].v, YL_ERR_INVALID,
                "adam_multi: NULL pointer in tensor %d", base + k);
       p.start[k + 1] = p.start[k] + p.t[k].n;
+      p.istart[k + 1] = p.istart[k] + (p.t[k].n + kAdamChunk - 1) / kAdamChunk;
     }
     if (p.start[p.count] == 0) continue;
     if (need_norm) {
@@ -125,7 +162,9 @@ yl_status adam_multi(yl_ctx* ctx, const AdamTensor* tensors, int count, float lr
       adam_norm_final_kernel<<<1, 32, 0, ctx->stream>>>((double*)ws, nb, norm);
       YL_TRY(check_launch("adam_norm_final_kernel"));
     }
-    adam_update_kernel<<<grid_1d(p.start[p.count], 256, ctx->num_sms * 8), 256, 0, ctx->stream>>>(
+    const long long items = p.istart[p.count];
+    const int grid = (int)std::min<long long>(items, (long long)ctx->num_sms * 8);
+    adam_update_kernel<<<grid, 256, 0, ctx->stream>>>(
         p, lr, b1, b2, eps, c1, c2, grad_scale, sanitize, clip_max_norm, need_norm ? norm : nullptr);
     YL_TRY(check_launch("adam_update_kernel"));
   }

@@ -41,6 +41,8 @@ def main(argv=None):
     ap.add_argument("--reps", type=int, default=5)
     ap.add_argument("--only", default=None)
     ap.add_argument("--groupnorm", action="store_true")
+    ap.add_argument("--adam", action="store_true",
+                    help="one multi-tensor Adam step over the joint step's 28.5 M parameters")
     a = ap.parse_args(argv)
     ctx = Context.shared(0)
     shapes = VAE_SHAPES if a.shapes == "vae" else SMALL_SHAPES
@@ -66,6 +68,12 @@ def main(argv=None):
             print(json.dumps({"groupnorm": [n, c, h, w], "fwd_ms": f.value, "bwd_ms": b.value,
                               "fwd_gbs": 3 * e / (f.value * 1e-3) / 1e9,
                               "bwd_gbs": 5 * e / (b.value * 1e-3) / 1e9}), flush=True)
+    if a.adam:
+        n, tensors = 13404612 + 15092896, 48  # VAE + motion U-Net parameter counts
+        ms = C.c_double()
+        call("yl_profile_adam", ctx.handle, n, tensors, a.reps, C.byref(ms))
+        print(json.dumps({"adam_params": n, "ms": ms.value,
+                          "gbs": 28.0 * n / (ms.value * 1e-3) / 1e9}), flush=True)
     return 0
 
 
