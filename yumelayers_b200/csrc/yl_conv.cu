@@ -29,6 +29,7 @@
 
 #include <algorithm>
 #include <mutex>
+#include <vector>
 
 #include "yl_conv_common.cuh"
 
@@ -649,6 +650,66 @@ yl_status rgb_tap_sum(yl_ctx* ctx, const float* z, int n, int h, int w, const fl
   rgb_tap_sum_kernel<<<grid_1d((long long)n * h * w, 256), 256, 0, ctx->stream>>>(z, n, h, w, bias,
                                                                                  y, ldy);
   return check_launch("rgb_tap_sum_kernel");
+}
+
+// Many weight_permute jobs in one launch: each block takes 4096-element items
+// of one job (found by binary search on the item prefix sums).
+constexpr long long kPermItem = 4096;
+
+__global__ void weight_permute_batch_kernel(const PermuteJob* __restrict__ jobs, int njobs,
+                                            const long long* __restrict__ item_start) {
+  const long long items = item_start[njobs];
+  for (long long it = blockIdx.x; it < items; it += gridDim.x) {
+    int lo = 0, hi = njobs - 1;
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (item_start[mid] <= it) lo = mid;
+      else hi = mid - 1;
+    }
+    const PermuteJob& j = jobs[lo];
+    const long long n = (long long)j.O * j.T * j.I_out;
+    const long long base = (it - item_start[lo]) * kPermItem;
+    const long long end = min(n, base + kPermItem);
+    for (long long idx = base + threadIdx.x; idx < end; idx += blockDim.x) {
+      const int i = (int)(idx % j.I_out);
+      const long long r = idx / j.I_out;
+      const int t = (int)(r % j.T);
+      const int o = (int)(r / j.T);
+      const float v = i < j.I_src ? j.in[o * j.so + t * j.st + i * j.si] : 0.f;
+      j.out[idx] = j.round ? round_tf32(v) : v;
+    }
+  }
+}
+
+yl_status weight_permute_batch(yl_ctx* ctx, const std::vector<PermuteJob>& jobs,
+                               PermuteBatchBuffers* bufs) {
+  if (jobs.empty()) return YL_OK;
+  if (!bufs->jobs) {
+    // the table lives on the device for the owner's lifetime (pointers are fixed)
+    std::vector<long long> start(jobs.size() + 1, 0);
+    for (size_t k = 0; k < jobs.size(); ++k) {
+      const long long n = (long long)jobs[k].O * jobs[k].T * jobs[k].I_out;
+      start[k + 1] = start[k] + (n + kPermItem - 1) / kPermItem;
+    }
+    YL_CUDA(cudaMalloc(&bufs->jobs, jobs.size() * sizeof(PermuteJob)));
+    YL_CUDA(cudaMalloc(&bufs->item_start, start.size() * sizeof(long long)));
+    YL_CUDA(cudaMemcpyAsync(bufs->jobs, jobs.data(), jobs.size() * sizeof(PermuteJob),
+                            cudaMemcpyHostToDevice, ctx->stream));
+    YL_CUDA(cudaMemcpyAsync(bufs->item_start, start.data(), start.size() * sizeof(long long),
+                            cudaMemcpyHostToDevice, ctx->stream));
+    YL_CUDA(cudaStreamSynchronize(ctx->stream));  // host vectors go out of scope
+    bufs->njobs = (int)jobs.size();
+    bufs->items = start.back();
+  }
+  const int grid = (int)std::min<long long>(bufs->items, (long long)ctx->num_sms * 8);
+  weight_permute_batch_kernel<<<grid, 256, 0, ctx->stream>>>(bufs->jobs, bufs->njobs,
+                                                             bufs->item_start);
+  return check_launch("weight_permute_batch_kernel");
+}
+
+PermuteBatchBuffers::~PermuteBatchBuffers() {
+  if (jobs) cudaFree(jobs);
+  if (item_start) cudaFree(item_start);
 }
 
 // 32 x 32 tiled transposes between [n][c][hw] and [n][hw][ps].

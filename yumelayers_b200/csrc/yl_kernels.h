@@ -6,6 +6,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <vector>
 
 #include "yl_internal.h"
 
@@ -91,6 +92,26 @@ yl_status channel_sums(yl_ctx* ctx, const float* dy, int images, long long hw, i
 // (out[i][t][o] layout for dgrad weights).  Optional tf32 rounding.
 yl_status weight_permute(yl_ctx* ctx, const float* in, float* out, int O, int T, int I_out,
                          int I_src, long long so, long long st, long long si, int round);
+
+// A batch of weight_permute jobs run by one launch.  The job table is copied
+// to the device on the first call and reused afterwards (the caller keeps the
+// same jobs and buffers).
+struct PermuteJob {
+  const float* in;
+  float* out;
+  int O, T, I_out, I_src;
+  long long so, st, si;
+  int round;
+};
+struct PermuteBatchBuffers {
+  PermuteJob* jobs = nullptr;
+  long long* item_start = nullptr;
+  int njobs = 0;
+  long long items = 0;
+  ~PermuteBatchBuffers();
+};
+yl_status weight_permute_batch(yl_ctx* ctx, const std::vector<PermuteJob>& jobs,
+                               PermuteBatchBuffers* bufs);
 
 // NCHW (c channels) <-> NHWC (pixel stride ps >= c, extra channels zero).
 yl_status nchw_to_nhwc(yl_ctx* ctx, const float* in, float* out, int n, int c, long long hw,

@@ -216,17 +216,26 @@ yl_status ConvL::init(yl_ctx* ctx, uint64_t seed, bool zero) {
 }
 // tf32-rounded copies of the weights in the fprop layout [cout][tap][cin] and
 // the dgrad layout [cin][tap][cout]; run once per step after the optimizer.
-yl_status ConvL::prepare(yl_ctx* ctx) {
+void ConvL::prepare_jobs(std::vector<PermuteJob>& first, std::vector<PermuteJob>& second) const {
   const int kk = k * k;
-  YL_TRY(weight_permute(ctx, W, Wr, cout_p, kk, cin_p, cin_p, (long long)kk * cin_p, cin_p, 1, 1));
-  YL_TRY(weight_permute(ctx, W, Wd, cin_p, kk, cout_p, cout_p, 1, cin_p, (long long)kk * cin_p, 1));
+  first.push_back({W, Wr, cout_p, kk, cin_p, cin_p, (long long)kk * cin_p, cin_p, 1, 1});
+  first.push_back({W, Wd, cin_p, kk, cout_p, cout_p, 1, cin_p, (long long)kk * cin_p, 1});
   if (rgb == 1)  // [cout][t*4 + ci], zero-padded to 64 columns
-    YL_TRY(weight_permute(ctx, Wr, Wx, cout_p, 1, 64, 36, 36, 0, 1, 0));
+    second.push_back({Wr, Wx, cout_p, 1, 64, 36, 36, 0, 1, 0});
   if (rgb == 2) {
     // [t*4 + co][ci] = W[co][t][ci] and [ci][t*4 + co] (from the dgrad copy), padded
-    YL_TRY(weight_permute(ctx, Wr, Wx, 9, 4, cin_p, cin_p, cin_p, 9LL * cin_p, 1, 0));
-    YL_TRY(weight_permute(ctx, Wd, Wx2, cin_p, 1, 64, 36, 36, 0, 1, 0));
+    second.push_back({Wr, Wx, 9, 4, cin_p, cin_p, cin_p, 9LL * cin_p, 1, 0});
+    second.push_back({Wd, Wx2, cin_p, 1, 64, 36, 36, 0, 1, 0});
   }
+}
+
+yl_status ConvL::prepare(yl_ctx* ctx) {
+  std::vector<PermuteJob> a, b;
+  prepare_jobs(a, b);
+  for (const auto& j : a)
+    YL_TRY(weight_permute(ctx, j.in, j.out, j.O, j.T, j.I_out, j.I_src, j.so, j.st, j.si, j.round));
+  for (const auto& j : b)
+    YL_TRY(weight_permute(ctx, j.in, j.out, j.O, j.T, j.I_out, j.I_src, j.so, j.st, j.si, j.round));
   return YL_OK;
 }
 
@@ -651,9 +660,13 @@ yl_status Net::prof_collect(double* ms, double* flops, double* bytes, int* launc
 void Net::grads_ready(size_t lo) {
   if (hook) hook(hook_arg, this, lo);
 }
+// The tf32 weight copies of every conv after each optimizer step: two launches
+// (copies of W, then the copies derived from those).
 yl_status Net::prepare_weights() {
-  for (ConvL* c : convs) YL_TRY(c->prepare(ctx));
-  return YL_OK;
+  if (perm_first.empty())
+    for (ConvL* c : convs) c->prepare_jobs(perm_first, perm_second);
+  YL_TRY(weight_permute_batch(ctx, perm_first, &perm_buf_first));
+  return weight_permute_batch(ctx, perm_second, &perm_buf_second);
 }
 
 // ------------------------------------------------------------------ VAE
@@ -1081,9 +1094,29 @@ yl_status UNet::set_inputs(const float* za, const float* zb, int ldz, const floa
 }
 
 // ------------------------------------------------------------------ frames
+// One thread per pixel: three coalesced plane reads, one 16-byte write.
+__global__ void frames_to_nhwc4_kernel(const float* __restrict__ in, long long hw, long long total,
+                                       int round, float* __restrict__ out) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const long long img = i / hw, p = i - img * hw;
+    const float* src = in + img * 3 * hw + p;
+    float r = __ldg(src), g = __ldg(src + hw), b = __ldg(src + 2 * hw);
+    if (round) {
+      r = round_tf32(r);
+      g = round_tf32(g);
+      b = round_tf32(b);
+    }
+    reinterpret_cast<float4*>(out)[i] = make_float4(r, g, b, 0.f);
+  }
+}
+
 yl_status frames_to_nhwc4(yl_ctx* ctx, const float* nchw3, int n, int h, int w, float* out,
                           int round) {
-  return nchw_to_nhwc(ctx, nchw3, out, n, 3, (long long)h * w, 4, round);
+  const long long hw = (long long)h * w, total = (long long)n * hw;
+  frames_to_nhwc4_kernel<<<grid_1d(total, 256), 256, 0, ctx->stream>>>(nchw3, hw, total, round,
+                                                                       out);
+  return check_launch("frames_to_nhwc4_kernel");
 }
 
 yl_status copy_mu(yl_ctx* ctx, const Act& e, float* dst, int c) {

@@ -72,6 +72,9 @@ struct ConvL {
   yl_status bind(Net& net);
   yl_status init(yl_ctx* ctx, uint64_t seed, bool zero = false);
   yl_status prepare(yl_ctx* ctx);
+  // the weight copies prepare() makes, as permute jobs: `first` read W, `second`
+  // read copies made by `first`
+  void prepare_jobs(std::vector<PermuteJob>& first, std::vector<PermuteJob>& second) const;
   ConvGather gather(const Act& x, int oh, int ow, int up, int hv, int wv) const;
   // gn_next: the GroupNorm that reads y; its statistics come out of this
   // conv's epilogue when the channel grouping allows it
@@ -149,6 +152,8 @@ struct Net {
     double flops, bytes;
   };
   std::vector<ProfEvent> pending, done;
+  std::vector<PermuteJob> perm_first, perm_second;
+  PermuteBatchBuffers perm_buf_first, perm_buf_second;
   std::vector<std::pair<cudaEvent_t, cudaEvent_t>> prof_ev;
 
   Net() { pool.arena = &arena; }

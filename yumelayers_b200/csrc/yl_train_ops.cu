@@ -98,8 +98,11 @@ __global__ void adam_update_kernel(const __grid_constant__ AdamPack p, float lr,
     const AdamTensor& t = p.t[k];
     const long long c0 = (it - p.istart[k]) * kAdamChunk;
     const long long c1e = min(t.n, c0 + kAdamChunk);
-    float *pp = t.param + c0, *mp = t.m + c0, *vp = t.v + c0;
-    const float* gp = t.grad + c0;
+    // the four arrays of a tensor never overlap: let the loads run ahead of the stores
+    float* __restrict__ pp = t.param + c0;
+    float* __restrict__ mp = t.m + c0;
+    float* __restrict__ vp = t.v + c0;
+    const float* __restrict__ gp = t.grad + c0;
     const long long len = c1e - c0;
     const bool vec = ((reinterpret_cast<uintptr_t>(pp) | reinterpret_cast<uintptr_t>(mp) |
                        reinterpret_cast<uintptr_t>(vp) | reinterpret_cast<uintptr_t>(gp)) &
@@ -107,6 +110,7 @@ __global__ void adam_update_kernel(const __grid_constant__ AdamPack p, float lr,
     long long done = 0;
     if (vec) {
       const long long n4 = len >> 2;
+#pragma unroll 2
       for (long long q = threadIdx.x; q < n4; q += blockDim.x) {
         float4 P = reinterpret_cast<float4*>(pp)[q], M = reinterpret_cast<float4*>(mp)[q];
         float4 V = reinterpret_cast<float4*>(vp)[q];
