@@ -347,6 +347,22 @@ yl_status yl_trainer_step_host(yl_trainer* tr, const float* frames_host, const f
 /* Replace the runtime options (learning rates, which parts train, profiling);
  * batch and frame size must match creation. */
 yl_status yl_trainer_set_config(yl_trainer* tr, const yl_trainer_config* cfg);
+/* The inference path of Interpolation.swift:263-373 without the file and
+ * video IO: frame_a, frame_b are device [3][height][width] frames (the
+ * trainer's size), times[count] (host) the frame times in [0, 1].  Writes
+ * count device frames to frames_out ([count][3][height][width]): the first and
+ * last are copies of A and B; each interior frame decodes the motion net's
+ * predicted latent for (encoder mean of A, encoder mean of B, t) (mode 0) or
+ * the smoothstep lerp of the two means (mode 1, the reference's path without
+ * a motion network, Interpolation.swift:340-343).  Interior frames are decoded
+ * in groups of the trainer's batch.  Synchronous. */
+yl_status yl_trainer_interpolate(yl_trainer* tr, const float* frame_a, const float* frame_b,
+                                 const float* times, int count, int mode, float* frames_out);
+/* interpolationFrameCount / interpolationTimes (Interpolation.swift:47-58):
+ * *count_out = max(2, round(seconds * fps)) (2 for invalid arguments); when
+ * times_out is not NULL it receives count evenly spaced times 0..1. */
+yl_status yl_interpolation_plan(double seconds, int fps, int max_count, float* times_out,
+                                int* count_out);
 /* which: 0 = VAE, 1 = motion U-Net.  Flat fp32 buffers on the device;
  * kind: 0 parameters, 1 gradients, 2 Adam m, 3 Adam v. */
 yl_status yl_trainer_param_count(yl_trainer* tr, int which, size_t* n);

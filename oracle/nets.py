@@ -268,7 +268,11 @@ class UNet:
     def __init__(self, ops: Ops, params: Params):
         self.o, self.P = ops, params
 
-    def train_forward_backward(self, za, zb, t, target):
+    def predict(self, za, zb, t):
+        """Forward only: the predicted intermediate latent for (zA, zB, t)."""
+        return self._forward(za, zb, t)[0]
+
+    def _forward(self, za, zb, t):
         o, p = self.o, self.P.p
         n, c, h, w = za.shape
         tt = t.reshape(n, 1, 1, 1)
@@ -302,6 +306,13 @@ class UNet:
         r5b, C["up2.rb_b"] = rb_fwd(o, p, "up2.rb_b", r5a, 128, 128, pj["up2.rb_b"])
         ho = o.gn(p, "norm_out", r5b)
         pred = o.conv(p, "conv_out", ho, residual=lerp)
+        return pred, (inp, emb, th, ta, temb, ts, pj, C, h0, r1a, s1, p1, r2a, s2, p2, r3a, r3b,
+                      u1, cat1, r4a, r4b, u2, cat2, r5a, r5b, ho)
+
+    def train_forward_backward(self, za, zb, t, target):
+        o, p = self.o, self.P.p
+        pred, (inp, emb, th, ta, temb, ts, pj, C, h0, r1a, s1, p1, r2a, s2, p2, r3a, r3b, u1, cat1,
+               r4a, r4b, u2, cat2, r5a, r5b, ho) = self._forward(za, zb, t)
         d = (pred.astype(np.float64) - target)
         loss = float((d * d).mean())
         dpred = (2.0 * d / d.size).astype(np.float32)

@@ -15,6 +15,7 @@
 #include <nccl.h>
 
 #include <algorithm>
+#include <cmath>
 #include <cstring>
 #include <memory>
 #include <vector>
@@ -102,6 +103,7 @@ struct yl_trainer {
   std::unique_ptr<UNet> unet;
   Overlap ov_vae, ov_unet;
   float *frames = nullptr, *tdev = nullptr, *za = nullptr, *zb = nullptr, *losses = nullptr;
+  float *ia = nullptr, *ib = nullptr;  // interpolation: latents of A and B, one copy per slot
   cudaEvent_t comm_done = nullptr;
   int64_t step = 0;
   double prof_ms[kProfClasses] = {}, prof_flops[kProfClasses] = {}, prof_bytes[kProfClasses] = {};
@@ -194,6 +196,8 @@ yl_status yl_trainer_create(yl_ctx* ctx, const yl_trainer_config* cfg, yl_comm* 
   const size_t lat = (size_t)B * tr->vae->hl * tr->vae->wl * VAE::kLatent;
   YL_TRY(tr->vae->arena.alloc(lat, &tr->za));
   YL_TRY(tr->vae->arena.alloc(lat, &tr->zb));
+  YL_TRY(tr->vae->arena.alloc(lat, &tr->ia));
+  YL_TRY(tr->vae->arena.alloc(lat, &tr->ib));
   YL_CUDA(cudaEventCreateWithFlags(&tr->comm_done, cudaEventDisableTiming));
   const size_t bucket_floats = (cfg->bucket_bytes ? cfg->bucket_bytes : (25u << 20)) / 4;
   Overlap* ovs[2] = {&tr->ov_vae, &tr->ov_unet};
@@ -315,6 +319,104 @@ yl_status yl_trainer_step_host(yl_trainer* tr, const float* frames_host, const f
                             ctx->stream));
   }
   YL_CUDA(cudaStreamSynchronize(ctx->stream));
+  return yl_ctx_check_device_errors(ctx);
+}
+
+// ------------------------------------------------------------------ inference
+// z[slot][i] = a[slot][i] + (b[slot][i] - a[slot][i]) * s[slot]
+__global__ void latent_lerp_kernel(const float* __restrict__ a, const float* __restrict__ b,
+                                   const float* __restrict__ s, long long per, int n,
+                                   float* __restrict__ z) {
+  const long long total = per * n;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const float k = s[i / per];
+    z[i] = a[i] + (b[i] - a[i]) * k;
+  }
+}
+
+static double smoothstep_d(double t) {  // Interpolation.swift:64-69
+  if (!std::isfinite(t)) return 0.0;
+  const double x = std::min(std::max(t, 0.0), 1.0);
+  return x * x * (3.0 - 2.0 * x);
+}
+
+yl_status yl_interpolation_plan(double seconds, int fps, int max_count, float* times_out,
+                                int* count_out) {
+  YL_CHECK(count_out, YL_ERR_INVALID, "yl_interpolation_plan: NULL count");
+  int count = 2;  // interpolationFrameCount (Interpolation.swift:47-51)
+  if (std::isfinite(seconds) && seconds > 0 && fps > 0)
+    count = std::max(2, (int)std::lround(seconds * (double)fps));
+  *count_out = count;
+  if (!times_out) return YL_OK;
+  YL_CHECK(max_count >= count, YL_ERR_SHAPE, "yl_interpolation_plan: %d frames, room for %d",
+           count, max_count);
+  for (int i = 0; i < count; ++i)  // interpolationTimes (Interpolation.swift:54-58)
+    times_out[i] = (float)((double)i / (double)(count - 1));
+  return YL_OK;
+}
+
+yl_status yl_trainer_interpolate(yl_trainer* tr, const float* frame_a, const float* frame_b,
+                                 const float* times, int count, int mode, float* frames_out) {
+  YL_CHECK(tr && frame_a && frame_b && times && frames_out, YL_ERR_INVALID,
+           "yl_trainer_interpolate: NULL argument");
+  YL_CHECK(count >= 2 && (mode == 0 || mode == 1), YL_ERR_INVALID,
+           "yl_trainer_interpolate: count %d, mode %d", count, mode);
+  yl_ctx* ctx = tr->ctx;
+  VAE& vae = *tr->vae;
+  UNet& unet = *tr->unet;
+  vae.profiling = unet.profiling = false;
+  const int B = tr->cfg.batch, H = tr->cfg.height, W = tr->cfg.width;
+  const size_t F = (size_t)3 * H * W, px = (size_t)H * W;
+  const size_t L = (size_t)vae.hl * vae.wl * VAE::kLatent;
+  // latents of A and B: the encoder means, deterministic (encodeLatent,
+  // Interpolation.swift:157-170); unused slots hold copies of A
+  for (int b = 0; b < B; ++b)
+    YL_TRY(frames_to_nhwc4(ctx, b == 1 ? frame_b : frame_a, 1, H, W, vae.x_in.p + b * px * 4, 1));
+  YL_TRY(vae.encode());
+  YL_TRY(copy_mu(ctx, vae.e, tr->za, VAE::kLatent));
+  const float* mu_b = tr->za + L;
+  if (B == 1) {
+    YL_TRY(frames_to_nhwc4(ctx, frame_b, 1, H, W, vae.x_in.p, 1));
+    YL_TRY(vae.encode());
+    YL_TRY(copy_mu(ctx, vae.e, tr->zb, VAE::kLatent));
+    mu_b = tr->zb;
+  }
+  for (int b = 0; b < B; ++b) {
+    YL_CUDA(cudaMemcpyAsync(tr->ia + b * L, tr->za, L * sizeof(float), cudaMemcpyDeviceToDevice,
+                            ctx->stream));
+    YL_CUDA(cudaMemcpyAsync(tr->ib + b * L, mu_b, L * sizeof(float), cudaMemcpyDeviceToDevice,
+                            ctx->stream));
+  }
+  // the first and last frames are the inputs themselves (Interpolation.swift:348-353)
+  YL_CUDA(cudaMemcpyAsync(frames_out, frame_a, F * sizeof(float), cudaMemcpyDeviceToDevice,
+                          ctx->stream));
+  YL_CUDA(cudaMemcpyAsync(frames_out + (size_t)(count - 1) * F, frame_b, F * sizeof(float),
+                          cudaMemcpyDeviceToDevice, ctx->stream));
+  std::vector<float> tv(B);
+  for (int i0 = 1; i0 < count - 1; i0 += B) {
+    const int nv = std::min(B, count - 1 - i0);
+    for (int b = 0; b < B; ++b) {
+      const double t = times[i0 + std::min(b, nv - 1)];
+      tv[b] = (float)(mode == 0 ? t : smoothstep_d(t));
+    }
+    YL_CUDA(cudaMemcpyAsync(tr->tdev, tv.data(), B * sizeof(float), cudaMemcpyHostToDevice,
+                            ctx->stream));
+    if (mode == 0) {  // the motion net's prediction (lerp + correction)
+      YL_TRY(unet.set_inputs(tr->ia, tr->ib, VAE::kLatent, tr->tdev));
+      YL_TRY(unet.forward());
+      YL_CUDA(cudaMemcpyAsync(vae.z.p, unet.pred.p, B * L * sizeof(float),
+                              cudaMemcpyDeviceToDevice, ctx->stream));
+    } else {  // smoothstep lerp of the latents (Interpolation.swift:340-343)
+      latent_lerp_kernel<<<grid_1d((long long)B * L, 256), 256, 0, ctx->stream>>>(
+          tr->ia, tr->ib, tr->tdev, (long long)L, B, vae.z.p);
+      YL_TRY(check_launch("latent_lerp_kernel"));
+    }
+    YL_TRY(vae.decode());
+    YL_TRY(nhwc_to_nchw(ctx, vae.recon.p, frames_out + (size_t)i0 * F, nv, 3, (long long)px, 4));
+    // tv is reused by the next chunk: the upload must have left the host buffer
+    YL_CUDA(cudaStreamSynchronize(ctx->stream));
+  }
   return yl_ctx_check_device_errors(ctx);
 }
 

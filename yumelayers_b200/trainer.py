@@ -175,6 +175,20 @@ class Trainer:
         _memcpy_h2d(self.ctx, self.buffer_ptr(which, kind), arr)
         call("yl_trainer_prepare_weights", self.handle)
 
+    def interpolate(self, frame_a: np.ndarray, frame_b: np.ndarray, times, mode: int = 0):
+        """Frames at `times` between A and B ([3][H][W] each, the trainer's size):
+        mode 0 decodes the motion net's prediction, mode 1 the smoothstep lerp
+        of the two encoder means.  Returns [len(times)][3][H][W]."""
+        from .session import GPUTensor
+        t = np.ascontiguousarray(np.asarray(times, np.float32).reshape(-1))
+        fa, fb = (np.ascontiguousarray(f, dtype=np.float32).reshape(-1) for f in (frame_a, frame_b))
+        h, w = self.cfg.height, self.cfg.width
+        da, db = GPUTensor(self.ctx, 1, fa.size, fa), GPUTensor(self.ctx, 1, fb.size, fb)
+        out = GPUTensor(self.ctx, 1, t.size * fa.size)
+        call("yl_trainer_interpolate", self.handle, C.c_void_p(da.ptr), C.c_void_p(db.ptr),
+             t.ctypes.data_as(C.c_void_p), t.size, int(mode), C.c_void_p(out.ptr))
+        return out.toArray()[: t.size * fa.size].reshape(t.size, 3, h, w)
+
     def kernel_stats(self, reset: bool = False) -> dict:
         st = KernelStats()
         call("yl_trainer_kernel_stats", self.handle, C.byref(st), int(reset))
@@ -185,6 +199,17 @@ class Trainer:
         b = C.c_size_t()
         call("yl_trainer_activation_bytes", self.handle, C.byref(b))
         return b.value
+
+
+def interpolation_plan(seconds: float, fps: int) -> np.ndarray:
+    """Frame times 0..1 of an interpolation of `seconds` at `fps`
+    (interpolationFrameCount / interpolationTimes, Interpolation.swift:47-58)."""
+    n = C.c_int()
+    call("yl_interpolation_plan", float(seconds), int(fps), 0, None, C.byref(n))
+    out = np.zeros(n.value, np.float32)
+    call("yl_interpolation_plan", float(seconds), int(fps), n.value,
+         out.ctypes.data_as(C.c_void_p), C.byref(n))
+    return out
 
 
 def _memcpy_d2h(ctx: Context, out: np.ndarray, dev_ptr: int) -> None:
