@@ -363,12 +363,19 @@ yl_status yl_trainer_interpolate(yl_trainer* tr, const float* frame_a, const flo
  * times_out is not NULL it receives count evenly spaced times 0..1. */
 yl_status yl_interpolation_plan(double seconds, int fps, int max_count, float* times_out,
                                 int* count_out);
+/* Steps taken so far (the Adam step counter t of the last step; the next step
+ * uses t + 1).  Setting it restores a checkpoint's optimizerStep
+ * (Train.swift:100-114: without it resumed training restarts Adam's bias
+ * correction). */
+yl_status yl_trainer_get_step(yl_trainer* tr, int64_t* step);
+yl_status yl_trainer_set_step(yl_trainer* tr, int64_t step);
 /* which: 0 = VAE, 1 = motion U-Net.  Flat fp32 buffers on the device;
  * kind: 0 parameters, 1 gradients, 2 Adam m, 3 Adam v. */
 yl_status yl_trainer_param_count(yl_trainer* tr, int which, size_t* n);
 yl_status yl_trainer_buffer(yl_trainer* tr, int which, int kind, float** dev_ptr);
 /* Parameter table (for checkpoints and tests): conv weights are stored
- * [oc][k*k][ic rounded up to 4] at `offset`; shape4 = (oc, ic, k, k). */
+ * [oc][k*k][ic rounded up to 4] at `offset` with shape4 = (oc, ic, k, k);
+ * Linear weights [oc][ic] with shape4 = (oc, ic, 0, 0); vectors (n, 1, 1, 1). */
 yl_status yl_trainer_param_entry(yl_trainer* tr, int which, int index, char* name,
                                  size_t name_len, size_t* offset, int* shape4);
 /* Re-derive the tf32 weight copies after parameters were written externally. */

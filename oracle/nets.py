@@ -41,8 +41,7 @@ class Params:
     @staticmethod
     def _get(e, flat):
         d0, d1, d2, d3 = e.shape
-        if e.name.endswith(".weight") and d2 > 1 or (e.name.endswith(".weight") and d2 == 1
-                                                     and _is_conv(e)):
+        if e.name.endswith(".weight") and d2 >= 1:  # conv (Linear weights have no kernel dims)
             k, icp = d2, _r4(d1)
             blk = flat[e.offset:e.offset + _r4(d0) * k * k * icp].reshape(_r4(d0), k * k, icp)
             return np.ascontiguousarray(
@@ -64,10 +63,6 @@ class Params:
             else:
                 out[e.offset:e.offset + v.size] = v.ravel()
         return out
-
-
-def _is_conv(e) -> bool:
-    return not (e.name.startswith("time.") or e.name.endswith("temb_proj.weight"))
 
 
 class Ops:
@@ -408,7 +403,7 @@ def _builder():
         tab.append(_Entry(name + ".beta", res(c), (c, 1, 1, 1)))
 
     def lin(name, ic, oc):
-        tab.append(_Entry(name + ".weight", res(oc * ic), (oc, ic, 1, 1)))
+        tab.append(_Entry(name + ".weight", res(oc * ic), (oc, ic, 0, 0)))
         tab.append(_Entry(name + ".bias", res(oc), (oc, 1, 1, 1)))
 
     def rb(name, cin, cout):
@@ -474,7 +469,7 @@ def init_flat(table, count, seed, zero=("conv_out",)):
             vals[e.name] = (0.02 * rng.standard_normal(d0)).astype(np.float32)
         elif e.name.endswith(".bias"):
             vals[e.name] = np.zeros(d0, np.float32)
-        elif _is_conv(e):
+        elif d2 >= 1:  # conv weight (Linear weights have no kernel dims)
             bound = np.sqrt(6.0 / (d1 * d2 * d3))
             if e.name.startswith(zero):
                 bound = 0.0

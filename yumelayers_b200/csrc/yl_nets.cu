@@ -524,7 +524,7 @@ void LinL::setup(Net& net, const char* nm, int ic_, int oc_) {
   oc = oc_;
   off_w = net.params.reserve((size_t)oc * ic);
   off_b = net.params.reserve(oc);
-  net.param_table.push_back({name + ".weight", off_w, oc, ic, 1, 1});
+  net.param_table.push_back({name + ".weight", off_w, oc, ic, 0, 0});  // 0: no spatial kernel
   net.param_table.push_back({name + ".bias", off_b, oc, 1, 1, 1});
 }
 void LinL::bind(Net& net) {

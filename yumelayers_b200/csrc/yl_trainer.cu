@@ -420,6 +420,18 @@ yl_status yl_trainer_interpolate(yl_trainer* tr, const float* frame_a, const flo
   return yl_ctx_check_device_errors(ctx);
 }
 
+yl_status yl_trainer_get_step(yl_trainer* tr, int64_t* step) {
+  YL_CHECK(tr && step, YL_ERR_INVALID, "yl_trainer_get_step: NULL argument");
+  *step = tr->step;
+  return YL_OK;
+}
+
+yl_status yl_trainer_set_step(yl_trainer* tr, int64_t step) {
+  YL_CHECK(tr && step >= 0, YL_ERR_INVALID, "yl_trainer_set_step: bad argument");
+  tr->step = step;
+  return YL_OK;
+}
+
 yl_status yl_trainer_param_count(yl_trainer* tr, int which, size_t* n) {
   YL_CHECK(tr && n && (which == 0 || which == 1), YL_ERR_INVALID, "yl_trainer_param_count");
   *n = which == 0 ? tr->vae->params.count : tr->unet->params.count;

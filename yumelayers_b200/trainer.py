@@ -140,6 +140,17 @@ class Trainer:
         call("yl_trainer_step_host", self.handle, C.c_void_p(frames_ptr), C.c_void_p(t_ptr),
              out.ctypes.data_as(C.c_void_p))
 
+    @property
+    def step(self) -> int:
+        """Adam step counter (steps taken so far)."""
+        v = C.c_int64()
+        call("yl_trainer_get_step", self.handle, C.byref(v))
+        return v.value
+
+    @step.setter
+    def step(self, value: int) -> None:
+        call("yl_trainer_set_step", self.handle, int(value))
+
     # -- parameters --
     def param_count(self, which: int) -> int:
         n = C.c_size_t()
