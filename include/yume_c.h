@@ -300,6 +300,15 @@ yl_status yl_vae_latent_head_bwd(yl_ctx* ctx, const float* e, const float* dz, i
 yl_status yl_loss_l1_kl(yl_ctx* ctx, const float* recon, const float* target, size_t n_recon,
                         const float* mu_logvar, int n, int c_lat, int h_lat, int w_lat, int layout,
                         float beta, float* drecon, float* loss_dev);
+/* Sobel edge loss of each image (encodeSobelEdgeGrad, GpuSessionEdgeLoss.swift:
+ * 10-41; sobelEdgeLoss / sobelEdgeGradCPU, LossFunctions.swift:29-66, 194-235):
+ * loss[i] = mean over h*w of (|grad luma recon| - |grad luma target|)^2 with
+ * 3x3 Sobel on the interior pixels (luma = 0.2126 R + 0.7152 G + 0.0722 B);
+ * grad = dloss/drecon in the input layout (channels 0..2 written).  recon and
+ * target are [n][3][h][w] (YL_LAYOUT_NCHW) or [n][h][w][ld] (YL_LAYOUT_NHWC,
+ * ld >= 3).  grad or loss (device, n floats) may be NULL. */
+yl_status yl_sobel_edge_loss(yl_ctx* ctx, const float* recon, const float* target, int n, int h,
+                             int w, int layout, int ld, float* grad, float* loss);
 
 /* ------------------------------------------------ data-parallel communicator
  * NCCL over NVLink/NVSwitch, one rank per GPU.  Rank 0 creates the id; the

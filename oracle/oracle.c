@@ -784,3 +784,82 @@ ORC_API double orc_l1_kl_loss(const float* recon, const float* target, long nr,
   double kl = orc_kl_sum(mu, lv, (int)nl);
   return l1 / (double)nr + (double)beta * kl / (double)nl;
 }
+
+/* ---- Sobel edge loss (LossFunctions.swift:29-66, 194-235), HWC images ---- */
+static const double kSobelGx[9] = {-1, 0, 1, -2, 0, 2, -1, 0, 1};
+static const double kSobelGy[9] = {-1, -2, -1, 0, 0, 0, 1, 2, 1};
+
+static double orc_luma(const float* img, long i) {
+  return 0.2126 * (double)img[i] + 0.7152 * (double)img[i + 1] + 0.0722 * (double)img[i + 2];
+}
+
+/* Sobel responses (sx, sy) of the luma at interior pixel (x, y). */
+static void orc_sobel_at(const float* img, int w, int x, int y, double* sx, double* sy) {
+  double ax = 0, ay = 0;
+  int k = 0;
+  for (int dy = -1; dy <= 1; ++dy)
+    for (int dx = -1; dx <= 1; ++dx, ++k) {
+      const double l = orc_luma(img, ((long)(y + dy) * w + (x + dx)) * 3);
+      ax += kSobelGx[k] * l;
+      ay += kSobelGy[k] * l;
+    }
+  *sx = ax;
+  *sy = ay;
+}
+
+/* sobelLumaGradient: |grad luma| per pixel, border pixels 0. */
+ORC_API void orc_sobel_luma(const float* img, int w, int h, float* out) {
+  for (long i = 0; i < (long)w * h; ++i) out[i] = 0.f;
+  for (int y = 1; y < h - 1; ++y)
+    for (int x = 1; x < w - 1; ++x) {
+      double sx, sy;
+      orc_sobel_at(img, w, x, y, &sx, &sy);
+      out[(long)y * w + x] = (float)sqrt(sx * sx + sy * sy);
+    }
+}
+
+/* sobelEdgeLoss: mean over w*h of (|grad R| - |grad T|)^2 (the maps in float). */
+ORC_API double orc_sobel_edge_loss(const float* recon, const float* target, int w, int h) {
+  const long n = (long)w * h;
+  float* er = (float*)malloc(n * sizeof(float));
+  float* et = (float*)malloc(n * sizeof(float));
+  orc_sobel_luma(recon, w, h, er);
+  orc_sobel_luma(target, w, h, et);
+  double s = 0;
+  for (long i = 0; i < n; ++i) {
+    const double d = (double)(er[i] - et[i]);
+    s += d * d;
+  }
+  free(er);
+  free(et);
+  return s / (double)n;
+}
+
+/* sobelEdgeGradCPU: dLoss/drecon (HWC) with scale 2/(w*h), each interior
+ * pixel q scattering its 3x3 window back onto the luma of the recon. */
+ORC_API void orc_sobel_edge_grad(const float* recon, const float* target, int w, int h,
+                                 float* grad) {
+  const long n = (long)w * h;
+  for (long i = 0; i < 3 * n; ++i) grad[i] = 0.f;
+  const double scale = 2.0 / (double)n;
+  for (int y = 1; y < h - 1; ++y)
+    for (int x = 1; x < w - 1; ++x) {
+      double sxr, syr, sxt, syt;
+      orc_sobel_at(recon, w, x, y, &sxr, &syr);
+      orc_sobel_at(target, w, x, y, &sxt, &syt);
+      const double mr = sqrt(sxr * sxr + syr * syr), mt = sqrt(sxt * sxt + syt * syt);
+      const double diff = mr - mt;
+      if (diff == 0) continue;
+      const double inv = mr > 1e-6 ? 1.0 / mr : 0.0;
+      const double dX = diff * inv * scale * sxr, dY = diff * inv * scale * syr;
+      int k = 0;
+      for (int dy = -1; dy <= 1; ++dy)
+        for (int dx = -1; dx <= 1; ++dx, ++k) {
+          const double c = dX * kSobelGx[k] + dY * kSobelGy[k];
+          const long li = ((long)(y + dy) * w + (x + dx)) * 3;
+          grad[li] += (float)(c * 0.2126);
+          grad[li + 1] += (float)(c * 0.7152);
+          grad[li + 2] += (float)(c * 0.0722);
+        }
+    }
+}

@@ -58,6 +58,9 @@ _SIGS = {
     "orc_linear_fwd": ([P, P, P, P, I, I, I, I], None),
     "orc_linear_bwd": ([P, P, P, P, P, P, I, I, I], None),
     "orc_l1_kl_loss": ([P, P, C.c_long, P, P, C.c_long, F, P], D),
+    "orc_sobel_luma": ([P, I, I, P], None),
+    "orc_sobel_edge_loss": ([P, P, I, I], D),
+    "orc_sobel_edge_grad": ([P, P, I, I, P], None),
     "orc_num_threads": ([], I),
     "orc_set_num_threads": ([I], None),
 }

@@ -202,4 +202,5 @@ SIGNATURES["yl_trainer_interpolate"] = [P, P, P, P, I, I, P]
 SIGNATURES["yl_interpolation_plan"] = [D, I, I, P, C.POINTER(I)]
 SIGNATURES["yl_trainer_get_step"] = [P, C.POINTER(C.c_int64)]
 SIGNATURES["yl_trainer_set_step"] = [P, C.c_int64]
+SIGNATURES["yl_sobel_edge_loss"] = [P, P, P, I, I, I, I, I, P, P]
 SIGNATURES["yl_profile_adam"] = [P, C.c_longlong, I, I, C.POINTER(D)]

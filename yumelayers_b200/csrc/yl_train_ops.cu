@@ -508,3 +508,143 @@ yl_status mse_head(yl_ctx* ctx, const float* pred, const float* target, long lon
 }
 
 }  // namespace yl
+
+// ------------------------------------------------------------------ Sobel edge loss
+// encodeSobelEdgeGrad (GpuSessionEdgeLoss.swift:10-41; kernels
+// MetalKernelSourcesB.swift:466-551; CPU reference LossFunctions.swift:29-66,
+// 194-235): L = (1/(h*w)) sum_q (|grad luma R|_q - |grad luma T|_q)^2 over the
+// interior pixels, per image; dL/dR through the 3x3 Sobel windows.
+namespace yl {
+
+struct ImgView {  // channel c of pixel p of image i: base + i*istride + p*pstride + c*cstride
+  const float* base;
+  long long istride, pstride, cstride;
+  __device__ __forceinline__ float at(long long i, long long p, int c) const {
+    return base[i * istride + p * pstride + c * cstride];
+  }
+};
+
+__constant__ float kSobelX[9] = {-1.f, 0.f, 1.f, -2.f, 0.f, 2.f, -1.f, 0.f, 1.f};
+__constant__ float kSobelY[9] = {-1.f, -2.f, -1.f, 0.f, 0.f, 0.f, 1.f, 2.f, 1.f};
+
+// maps[img][5][hw]: |grad R|, |grad T|, sx(R), sy(R), 1/|grad R| (0 at the border)
+__global__ void sobel_map_kernel(ImgView r, ImgView t, int h, int w, float* __restrict__ maps) {
+  const long long hw = (long long)h * w;
+  const int img = blockIdx.y;
+  for (long long p = blockIdx.x * (long long)blockDim.x + threadIdx.x; p < hw;
+       p += (long long)gridDim.x * blockDim.x) {
+    float* m = maps + (long long)img * 5 * hw + p;
+    const int y = (int)(p / w), x = (int)(p % w);
+    if (y < 1 || y >= h - 1 || x < 1 || x >= w - 1) {
+      m[0] = m[hw] = m[2 * hw] = m[3 * hw] = m[4 * hw] = 0.f;
+      continue;
+    }
+    float sxr = 0.f, syr = 0.f, sxt = 0.f, syt = 0.f;
+    int k = 0;
+    for (int dy = -1; dy <= 1; ++dy)
+      for (int dx = -1; dx <= 1; ++dx, ++k) {
+        const long long q = (long long)(y + dy) * w + (x + dx);
+        const float lr = 0.2126f * r.at(img, q, 0) + 0.7152f * r.at(img, q, 1) +
+                         0.0722f * r.at(img, q, 2);
+        const float lt = 0.2126f * t.at(img, q, 0) + 0.7152f * t.at(img, q, 1) +
+                         0.0722f * t.at(img, q, 2);
+        sxr += kSobelX[k] * lr;
+        syr += kSobelY[k] * lr;
+        sxt += kSobelX[k] * lt;
+        syt += kSobelY[k] * lt;
+      }
+    const float mr = sqrtf(sxr * sxr + syr * syr), mt = sqrtf(sxt * sxt + syt * syt);
+    m[0] = mr;
+    m[hw] = mt;
+    m[2 * hw] = sxr;
+    m[3 * hw] = syr;
+    m[4 * hw] = mr > 1e-6f ? 1.f / mr : 0.f;
+  }
+}
+
+// Gradient of each pixel from the windows of its 3x3 neighbours, and block
+// partial sums of (|grad R| - |grad T|)^2 (fixed order: part[img][block]).
+__global__ void sobel_grad_kernel(const float* __restrict__ maps, int h, int w, float scale,
+                                  float* grad, long long gi, long long gp, long long gc,
+                                  double* __restrict__ part) {
+  __shared__ double red[256];
+  const long long hw = (long long)h * w;
+  const int img = blockIdx.y;
+  const float* eR = maps + (long long)img * 5 * hw;
+  const float *eT = eR + hw, *gx = eR + 2 * hw, *gy = eR + 3 * hw, *inv = eR + 4 * hw;
+  double acc = 0.0;
+  for (long long p = blockIdx.x * (long long)blockDim.x + threadIdx.x; p < hw;
+       p += (long long)gridDim.x * blockDim.x) {
+    const float d0 = eR[p] - eT[p];
+    acc += (double)d0 * d0;
+    if (!grad) continue;
+    const int py = (int)(p / w), px = (int)(p % w);
+    float a0 = 0.f, a1 = 0.f, a2 = 0.f;
+    for (int dy = -1; dy <= 1; ++dy)
+      for (int dx = -1; dx <= 1; ++dx) {
+        const int qy = py + dy, qx = px + dx;
+        if (qy < 1 || qy >= h - 1 || qx < 1 || qx >= w - 1) continue;
+        const long long q = (long long)qy * w + qx;
+        const float diff = eR[q] - eT[q];
+        if (diff == 0.f) continue;
+        const float dX = diff * inv[q] * scale * gx[q], dY = diff * inv[q] * scale * gy[q];
+        const int k = (1 - dy) * 3 + (1 - dx);
+        const float c = dX * kSobelX[k] + dY * kSobelY[k];
+        a0 += c * 0.2126f;
+        a1 += c * 0.7152f;
+        a2 += c * 0.0722f;
+      }
+    float* g = grad + img * gi + p * gp;
+    g[0] = a0;
+    g[gc] = a1;
+    g[2 * gc] = a2;
+  }
+  red[threadIdx.x] = acc;
+  __syncthreads();
+  for (int o = blockDim.x / 2; o > 0; o >>= 1) {
+    if (threadIdx.x < o) red[threadIdx.x] += red[threadIdx.x + o];
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) part[(long long)img * gridDim.x + blockIdx.x] = red[0];
+}
+
+__global__ void sobel_loss_final_kernel(const double* __restrict__ part, int blocks, int n,
+                                        double inv_hw, float* __restrict__ loss) {
+  const int img = blockIdx.x * blockDim.x + threadIdx.x;
+  if (img >= n) return;
+  double s = 0.0;
+  for (int b = 0; b < blocks; ++b) s += part[(long long)img * blocks + b];
+  loss[img] = (float)(s * inv_hw);
+}
+
+}  // namespace yl
+
+extern "C" yl_status yl_sobel_edge_loss(yl_ctx* ctx, const float* recon, const float* target,
+                                        int n, int h, int w, int layout, int ld, float* grad,
+                                        float* loss) {
+  using namespace yl;
+  YL_CHECK(ctx && recon && target && (grad || loss), YL_ERR_INVALID,
+           "yl_sobel_edge_loss: NULL argument");
+  YL_CHECK(n >= 1 && h >= 1 && w >= 1, YL_ERR_SHAPE, "yl_sobel_edge_loss: empty input");
+  YL_CHECK(layout == YL_LAYOUT_NCHW || (layout == YL_LAYOUT_NHWC && ld >= 3), YL_ERR_INVALID,
+           "yl_sobel_edge_loss: layout %d, pixel stride %d", layout, ld);
+  const long long hw = (long long)h * w;
+  const bool nchw = layout == YL_LAYOUT_NCHW;
+  const long long istr = nchw ? 3 * hw : hw * ld, pstr = nchw ? 1 : ld, cstr = nchw ? hw : 1;
+  ImgView r{recon, istr, pstr, cstr}, t{target, istr, pstr, cstr};
+  const int blocks = (int)std::max(1LL, std::min((hw + 255) / 256, 256LL));
+  void* ws = nullptr;
+  const size_t map_bytes = (size_t)n * 5 * hw * sizeof(float);
+  YL_TRY(scratch_get(ctx, map_bytes + (size_t)n * blocks * sizeof(double) + 256, &ws));
+  float* maps = (float*)ws;
+  double* part = (double*)((char*)ws + ((map_bytes + 255) & ~size_t(255)));
+  sobel_map_kernel<<<dim3(blocks, n), 256, 0, ctx->stream>>>(r, t, h, w, maps);
+  YL_TRY(check_launch("sobel_map_kernel"));
+  sobel_grad_kernel<<<dim3(blocks, n), 256, 0, ctx->stream>>>(
+      maps, h, w, (float)(2.0 / (double)hw), grad, istr, pstr, cstr, part);
+  YL_TRY(check_launch("sobel_grad_kernel"));
+  if (!loss) return YL_OK;
+  sobel_loss_final_kernel<<<(n + 127) / 128, 128, 0, ctx->stream>>>(part, blocks, n,
+                                                                     1.0 / (double)hw, loss);
+  return check_launch("sobel_loss_final_kernel");
+}

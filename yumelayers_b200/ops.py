@@ -185,3 +185,14 @@ def loss_l1_kl(recon, target, e=None, beta=1e-6, ctx: Context | None = None):
     call("yl_loss_l1_kl", ctx.handle, _ptr(rd), _ptr(td), recon.size, _ptr(ed), n, c2 // 2, h, w,
          LAYOUT_NCHW, float(beta), _ptr(gd), _ptr(ld))
     return float(ld.toArray()[0]), gd.toArray()[: recon.size].reshape(recon.shape)
+
+
+def sobel_edge_loss(recon, target, ctx: Context | None = None):
+    """Per-image Sobel edge loss and its gradient for NCHW [n][3][h][w] arrays."""
+    ctx = ctx or Context.shared()
+    n, c, h, w = recon.shape
+    rd, td = _dev(ctx, recon), _dev(ctx, target)
+    gd, ld = _out(ctx, recon.size), _out(ctx, n)
+    call("yl_sobel_edge_loss", ctx.handle, _ptr(rd), _ptr(td), n, h, w, LAYOUT_NCHW, 0, _ptr(gd),
+         _ptr(ld))
+    return ld.toArray()[:n], gd.toArray()[: recon.size].reshape(recon.shape)
