@@ -1157,10 +1157,10 @@ struct WgTile {
 static WgTile wgrad_tile(int cout, int n_total) {
   if (n_total == 288) return {1, 3, 96, 16};  // 9 taps of one (padded) 32-channel atom
   if (n_total == 64) return {1, 1, 64, 32};   // 1x1 over 64-channel patches
-  if (cout % 256 == 0 && n_total % 256 == 0) return {2, 1, 256, 16};
+  if (cout % 256 == 0 && n_total % 256 == 0) return {2, 1, 256, 32};
   if (cout <= 128 && n_total % 512 == 0) return {1, 2, 256, 16};
   if (n_total % 384 == 0) return {1, 2, 192, 32};
-  if (n_total % 256 == 0) return {1, 1, 256, 16};
+  if (n_total % 256 == 0) return {1, 1, 256, 32};
   if (n_total % 128 == 0) return {1, 1, 128, 32};
   return {0, 0, 0, 0};
 }
@@ -1362,13 +1362,13 @@ yl_status conv_wgrad_ws(yl_ctx* ctx, const float* dy, int ldy, int cout, const C
   else if (tile.nw == 64)
     YL_TRY((launch_wgrad<1, 1, 64, 32>(ctx, av, nav, bv, nbv, w, splits, col_blocks)));
   else if (tile.mt == 2)
-    YL_TRY((launch_wgrad<2, 1, 256, 16>(ctx, av, nav, bv, nbv, w, splits, col_blocks)));
+    YL_TRY((launch_wgrad<2, 1, 256, 32>(ctx, av, nav, bv, nbv, w, splits, col_blocks)));
   else if (tile.nsub == 2 && tile.nw == 256)
     YL_TRY((launch_wgrad<1, 2, 256, 16>(ctx, av, nav, bv, nbv, w, splits, col_blocks)));
   else if (tile.nsub == 2)
     YL_TRY((launch_wgrad<1, 2, 192, 32>(ctx, av, nav, bv, nbv, w, splits, col_blocks)));
   else if (tile.nw == 256)
-    YL_TRY((launch_wgrad<1, 1, 256, 16>(ctx, av, nav, bv, nbv, w, splits, col_blocks)));
+    YL_TRY((launch_wgrad<1, 1, 256, 32>(ctx, av, nav, bv, nbv, w, splits, col_blocks)));
   else
     YL_TRY((launch_wgrad<1, 1, 128, 32>(ctx, av, nav, bv, nbv, w, splits, col_blocks)));
   if (db) {
