@@ -271,14 +271,30 @@ __global__ void __launch_bounds__(kThreads, 1)
     int tc = 0;
     for (int tile = blockIdx.x; tile < p.n_tiles; tile += gridDim.x, ++tc) {
       const int buf = tc & 1, use = tc >> 1;
+      const FpropTile c = fprop_tile(p, tile);
+      const TapPhase& ph = p.ph[c.z];
+      const int n0 = c.nb * BN;
+      if constexpr (TR) {
+        // while the accumulator is still being computed: pull this tile's
+        // residual into L2, one 128-byte line of 32 channels per thread and
+        // lattice row
+        const int t = warp * 32 + lane, q = t >> 2, ch = n0 + (t & 3) * 32;
+        const int gx = c.tx * 32 + q, X = gx * p.xs + ph.xa;
+        if (e.residual && ch < e.n_total && gx < p.gw && X < p.out_w) {
+#pragma unroll 1
+          for (int j = 0; j < kRows; ++j) {
+            const int gy = c.ty * kRows + j, Y = gy * p.ys + ph.ya;
+            if (gy >= p.gh || Y >= p.out_h) break;
+            const long long pix = ((long long)c.img * p.out_h + Y) * p.out_w + X;
+            prefetch_l2(e.residual + pix * e.ldr + ch);
+          }
+        }
+      }
       if (!mbar_wait(&acc_full[buf], use & 1)) {
         report_error(err, YL_DEVERR_TIMEOUT);
         break;
       }
       tc_fence_after();
-      const FpropTile c = fprop_tile(p, tile);
-      const TapPhase& ph = p.ph[c.z];
-      const int n0 = c.nb * BN;
       if constexpr (TR) {
         // lane row = output channel, column = pixel (lattice row j of the tile, column q)
         const int co = n0 + warp * 32 + lane;
@@ -298,31 +314,36 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int Y = gy * p.ys + ph.ya;
           if (!cval || gy >= p.gh || Y >= p.out_h) continue;
           const long long rowp = ((long long)c.img * p.out_h + Y) * p.out_w;
+          // columns q < qn are inside the lattice and the image (both bounds
+          // are monotone in q); addresses advance by a fixed 32-bit stride
+          const int X0 = c.tx * 32 * p.xs + ph.xa;
+          int qn = p.gw - c.tx * 32;
+          if (qn > 32) qn = 32;
+          const int qx = X0 < p.out_w ? (p.out_w - X0 + p.xs - 1) / p.xs : 0;
+          if (qx < qn) qn = qx;
           // all residual loads first: out may alias nothing, but the compiler
           // cannot know that and would otherwise wait on each load in turn
           float v[32];
 #pragma unroll
           for (int q = 0; q < 32; ++q) v[q] = __uint_as_float(r[q]) + badd;
           if (e.residual) {
+            const float* rrow = e.residual + (rowp + X0) * e.ldr + co;
+            const int sr = p.xs * e.ldr;
             float rv[32];
 #pragma unroll
-            for (int q = 0; q < 32; ++q) {
-              const int gx = c.tx * 32 + q;
-              const int X = gx * p.xs + ph.xa;
-              rv[q] = gx < p.gw && X < p.out_w ? e.residual[(rowp + X) * e.ldr + co] : 0.f;
-            }
+            for (int q = 0; q < 32; ++q) rv[q] = q < qn ? rrow[q * sr] : 0.f;
 #pragma unroll
             for (int q = 0; q < 32; ++q) v[q] += rv[q];
           }
+          float* orow = e.out + (rowp + X0) * e.ldo + co;
+          const int so = p.xs * e.ldo;
 #pragma unroll
           for (int q = 0; q < 32; ++q) {
-            const int gx = c.tx * 32 + q;
-            const int X = gx * p.xs + ph.xa;
-            if (gx < p.gw && X < p.out_w) {
-              const float o = e.round_tf32 ? round_tf32(v[q]) : v[q];
-              e.out[(rowp + X) * e.ldo + co] = o;
-              gs += o;
-              gss += o * o;
+            if (e.round_tf32) v[q] = round_tf32(v[q]);
+            if (q < qn) {
+              orow[q * so] = v[q];
+              gs += v[q];
+              gss += v[q] * v[q];
             }
           }
         }
