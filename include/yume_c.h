@@ -309,6 +309,21 @@ yl_status yl_loss_l1_kl(yl_ctx* ctx, const float* recon, const float* target, si
  * ld >= 3).  grad or loss (device, n floats) may be NULL. */
 yl_status yl_sobel_edge_loss(yl_ctx* ctx, const float* recon, const float* target, int n, int h,
                              int w, int layout, int ld, float* grad, float* loss);
+/* Layered 8-channel loss of each image (layered_grad_kernel,
+ * MetalKernelSourcesB.swift:414-449; layeredLoss / layeredLossGradient,
+ * LayeredVAELoss.swift:129-196).  recon and target are [n][8][plane] CHW planes
+ * (bg R G B | obj R G B | mask | light), comp is [n][3][plane] (the frame):
+ * loss[i] = layer_weight * mean over 8*plane of (recon - target)^2
+ *         + compose_weight * mean over 3*plane of
+ *           (clamp((bg*(1-m) + obj*m) * light, 0, 1) - comp)^2,
+ * grad = dloss/drecon, [n][8][plane] (the clamp passes the gradient only
+ * strictly inside (0, 1)).  grad or loss (device, n floats) may be NULL. */
+yl_status yl_layered_loss(yl_ctx* ctx, const float* recon, const float* target, const float* comp,
+                          int n, long long plane, float layer_weight, float compose_weight,
+                          float* grad, float* loss);
+/* composeCHW (LayeredVAELoss.swift:95-110): out [n][3][plane] =
+ * clamp((bg*(1-m) + obj*m) * light, 0, 1) per channel. */
+yl_status yl_layered_compose(yl_ctx* ctx, const float* recon, int n, long long plane, float* out);
 
 /* ------------------------------------------------ data-parallel communicator
  * NCCL over NVLink/NVSwitch, one rank per GPU.  Rank 0 creates the id; the
@@ -418,6 +433,9 @@ yl_status yl_profile_adam(yl_ctx* ctx, long long n, int tensors, int reps, doubl
 /* GroupNorm(32)+SiLU forward and backward on an n x h x w x c NHWC tensor. */
 yl_status yl_profile_groupnorm(yl_ctx* ctx, int n, int c, int h, int w, int reps, double* fwd_ms,
                                double* bwd_ms);
+/* Layered 8-channel loss + gradient on n images of `plane` pixels (synthetic
+ * planes); *ms = average device time of one yl_layered_loss call. */
+yl_status yl_profile_layered(yl_ctx* ctx, int n, long long plane, int reps, double* ms);
 
 #ifdef __cplusplus
 }

@@ -863,3 +863,66 @@ ORC_API void orc_sobel_edge_grad(const float* recon, const float* target, int w,
         }
     }
 }
+
+/* ---- Layered 8-channel loss (LayeredVAELoss.swift:95-196), CHW planes ----
+ * recon / target: 8 planes of n pixels (bg RGB | obj RGB | mask | light);
+ * comp: 3 planes (the composed frame). */
+
+/* composeCHW (:95-110): clamp((bg*(1-m) + obj*m) * light, 0, 1), in float. */
+ORC_API void orc_layered_compose(const float* recon, long long n, float* out) {
+  for (long long i = 0; i < n; ++i) {
+    const float m = recon[6 * n + i], l = recon[7 * n + i], im = 1.0f - m;
+    for (int c = 0; c < 3; ++c) {
+      const float v = (recon[c * n + i] * im + recon[(3 + c) * n + i] * m) * l;
+      out[c * n + i] = v < 0.0f ? 0.0f : (v > 1.0f ? 1.0f : v);
+    }
+  }
+}
+
+/* layeredLoss (:129-149): wl * MSE over the 8 planes + wc * MSE of the composed
+ * frame against comp, each mean over its own element count, sums in double. */
+ORC_API double orc_layered_loss(const float* recon, const float* target, const float* comp,
+                                long long n, float wl, float wc) {
+  double layer = 0.0, compose = 0.0;
+  for (long long i = 0; i < 8 * n; ++i) {
+    const double d = (double)(recon[i] - target[i]);
+    layer += d * d;
+  }
+  layer /= (double)(8 * n);
+  float* y = (float*)malloc((size_t)(3 * n) * sizeof(float));
+  orc_layered_compose(recon, n, y);
+  for (long long i = 0; i < 3 * n; ++i) {
+    const double d = (double)(y[i] - comp[i]);
+    compose += d * d;
+  }
+  free(y);
+  compose /= (double)(3 * n);
+  return (double)wl * layer + (double)wc * compose;
+}
+
+/* layeredLossGradient (:158-196): dL/drecon for all 8 planes; the clamp passes
+ * the gradient only strictly inside (0, 1); float composition, double chain. */
+ORC_API void orc_layered_grad(const float* recon, const float* target, const float* comp,
+                              long long n, float wl, float wc, float* g) {
+  const double dl = 2.0 * (double)wl / (double)(8 * n);
+  const double dc = 2.0 * (double)wc / (double)(3 * n);
+  for (long long i = 0; i < n; ++i) {
+    const float m = recon[6 * n + i], l = recon[7 * n + i], im = 1.0f - m;
+    double dmask = 0.0, dlight = 0.0;
+    for (int c = 0; c < 3; ++c) {
+      const float bg = recon[c * n + i], ob = recon[(3 + c) * n + i];
+      const float base = bg * im + ob * m;
+      const float v = base * l;
+      const float y = v < 0.0f ? 0.0f : (v > 1.0f ? 1.0f : v);
+      const double e = (double)(y - comp[c * n + i]);
+      const double gc = dc * e * ((v > 0.0f && v < 1.0f) ? 1.0 : 0.0);
+      g[c * n + i] = (float)(dl * (double)(bg - target[c * n + i]) + gc * (double)(l * im));
+      g[(3 + c) * n + i] =
+          (float)(dl * (double)(ob - target[(3 + c) * n + i]) + gc * (double)(l * m));
+      dmask += gc * (double)l * (double)(ob - bg);
+      dlight += gc * (double)base;
+    }
+    g[6 * n + i] = (float)(dl * (double)(m - target[6 * n + i]) + dmask);
+    g[7 * n + i] = (float)(dl * (double)(l - target[7 * n + i]) + dlight);
+  }
+}

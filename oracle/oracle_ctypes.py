@@ -16,6 +16,7 @@ P = C.c_void_p
 I = C.c_int
 F = C.c_float
 D = C.c_double
+L = C.c_longlong
 
 _SIGS = {
     "orc_matmul": ([P, P, P, I, I, I, I, I], None),
@@ -61,6 +62,9 @@ _SIGS = {
     "orc_sobel_luma": ([P, I, I, P], None),
     "orc_sobel_edge_loss": ([P, P, I, I], D),
     "orc_sobel_edge_grad": ([P, P, I, I, P], None),
+    "orc_layered_compose": ([P, L, P], None),
+    "orc_layered_loss": ([P, P, P, L, F, F], D),
+    "orc_layered_grad": ([P, P, P, L, F, F, P], None),
     "orc_num_threads": ([], I),
     "orc_set_num_threads": ([I], None),
 }

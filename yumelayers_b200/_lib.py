@@ -203,4 +203,7 @@ SIGNATURES["yl_interpolation_plan"] = [D, I, I, P, C.POINTER(I)]
 SIGNATURES["yl_trainer_get_step"] = [P, C.POINTER(C.c_int64)]
 SIGNATURES["yl_trainer_set_step"] = [P, C.c_int64]
 SIGNATURES["yl_sobel_edge_loss"] = [P, P, P, I, I, I, I, I, P, P]
+SIGNATURES["yl_layered_loss"] = [P, P, P, P, I, LL, F, F, P, P]
+SIGNATURES["yl_layered_compose"] = [P, P, I, LL, P]
 SIGNATURES["yl_profile_adam"] = [P, C.c_longlong, I, I, C.POINTER(D)]
+SIGNATURES["yl_profile_layered"] = [P, I, C.c_longlong, I, C.POINTER(D)]

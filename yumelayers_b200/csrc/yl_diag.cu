@@ -229,4 +229,36 @@ yl_status yl_profile_groupnorm(yl_ctx* ctx, int n, int c, int h, int w, int reps
   return yl_ctx_check_device_errors(ctx);
 }
 
+yl_status yl_profile_layered(yl_ctx* ctx, int n, long long plane, int reps, double* ms_out) {
+  YL_CHECK(ctx && ms_out && reps >= 1 && n >= 1 && plane >= 1, YL_ERR_INVALID,
+           "yl_profile_layered: bad argument");
+  DevBufs b;
+  float *r, *t, *c, *g, *l;
+  const long long e8 = (long long)n * 8 * plane, e3 = (long long)n * 3 * plane;
+  YL_TRY(b.get((size_t)e8, &r));
+  YL_TRY(b.get((size_t)e8, &t));
+  YL_TRY(b.get((size_t)e3, &c));
+  YL_TRY(b.get((size_t)e8, &g));
+  YL_TRY(b.get((size_t)n, &l));
+  fill_kernel<<<1024, 256, 0, ctx->stream>>>(r, e8, 11, 1.f);
+  fill_kernel<<<1024, 256, 0, ctx->stream>>>(t, e8, 12, 1.f);
+  fill_kernel<<<1024, 256, 0, ctx->stream>>>(c, e3, 13, 1.f);
+  YL_TRY(check_launch("fill_kernel"));
+  cudaEvent_t e0, e1;
+  YL_CUDA(cudaEventCreate(&e0));
+  YL_CUDA(cudaEventCreate(&e1));
+  for (int rr = -1; rr < reps; ++rr) {
+    if (rr == 0) YL_CUDA(cudaEventRecord(e0, ctx->stream));
+    YL_TRY(yl_layered_loss(ctx, r, t, c, n, plane, 1.f, 1.f, g, l));
+  }
+  YL_CUDA(cudaEventRecord(e1, ctx->stream));
+  YL_CUDA(cudaEventSynchronize(e1));
+  float tm = 0.f;
+  YL_CUDA(cudaEventElapsedTime(&tm, e0, e1));
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  *ms_out = tm / reps;
+  return yl_ctx_check_device_errors(ctx);
+}
+
 }  // extern "C"

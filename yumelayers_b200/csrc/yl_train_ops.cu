@@ -648,3 +648,202 @@ extern "C" yl_status yl_sobel_edge_loss(yl_ctx* ctx, const float* recon, const f
                                                                      1.0 / (double)hw, loss);
   return check_launch("sobel_loss_final_kernel");
 }
+
+// ------------------------------------------------------------------ layered 8-channel loss
+// layered_grad_kernel (MetalKernelSourcesB.swift:414-449) with the loss of
+// layeredLoss (LayeredVAELoss.swift:129-149) in the same pass: per image, 8
+// CHW planes (bg RGB | obj RGB | mask | light) against the target planes and
+// the composed frame clamp((bg*(1-m) + obj*m) * light, 0, 1) against comp.
+// One pass reads recon, target and comp once and writes the gradient (108 B
+// per pixel); V = 4 moves four pixels of every plane per thread in float4.
+namespace yl {
+
+template <int V>
+struct Vec;
+template <>
+struct Vec<1> {
+  static __device__ __forceinline__ void ld(const float* p, float* o) { o[0] = __ldg(p); }
+  static __device__ __forceinline__ void st(float* p, const float* v) { p[0] = v[0]; }
+};
+template <>
+struct Vec<4> {
+  static __device__ __forceinline__ void ld(const float* p, float* o) {
+    const float4 t = __ldg(reinterpret_cast<const float4*>(p));
+    o[0] = t.x;
+    o[1] = t.y;
+    o[2] = t.z;
+    o[3] = t.w;
+  }
+  static __device__ __forceinline__ void st(float* p, const float* v) {
+    *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
+  }
+};
+
+template <int V>
+__global__ void __launch_bounds__(256) layered_loss_kernel(
+    const float* __restrict__ recon, const float* __restrict__ target,
+    const float* __restrict__ comp, long long plane, float dl, float dc,
+    float* __restrict__ grad, double* __restrict__ part) {
+  const int img = blockIdx.y;
+  const float* r = recon + (long long)img * 8 * plane;
+  const float* t = target + (long long)img * 8 * plane;
+  const float* cp = comp + (long long)img * 3 * plane;
+  float* g = grad ? grad + (long long)img * 8 * plane : nullptr;
+  const long long nv = plane / V;
+  float sl = 0.f, sc = 0.f;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < nv;
+       i += (long long)gridDim.x * blockDim.x) {
+    const long long p = i * V;
+    float R[8][V], T[8][V], C3[3][V], G[8][V];
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      Vec<V>::ld(r + c * plane + p, R[c]);
+      Vec<V>::ld(t + c * plane + p, T[c]);
+    }
+#pragma unroll
+    for (int c = 0; c < 3; ++c) Vec<V>::ld(cp + c * plane + p, C3[c]);
+#pragma unroll
+    for (int k = 0; k < V; ++k) {
+      const float m = R[6][k], l = R[7][k], im = 1.f - m;
+      float dm = 0.f, dlt = 0.f;
+#pragma unroll
+      for (int c = 0; c < 3; ++c) {
+        const float bg = R[c][k], ob = R[3 + c][k];
+        const float base = bg * im + ob * m;
+        const float v = base * l;
+        const float e = fminf(fmaxf(v, 0.f), 1.f) - C3[c][k];
+        sc = fmaf(e, e, sc);
+        // the clamp passes the gradient only strictly inside (0, 1)
+        const float gc = (v > 0.f && v < 1.f) ? dc * e : 0.f;
+        G[c][k] = dl * (bg - T[c][k]) + gc * l * im;
+        G[3 + c][k] = dl * (ob - T[3 + c][k]) + gc * l * m;
+        dm += gc * l * (ob - bg);
+        dlt += gc * base;
+      }
+      G[6][k] = dl * (m - T[6][k]) + dm;
+      G[7][k] = dl * (l - T[7][k]) + dlt;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        const float d = R[c][k] - T[c][k];
+        sl = fmaf(d, d, sl);
+      }
+    }
+    if (g) {
+#pragma unroll
+      for (int c = 0; c < 8; ++c) Vec<V>::st(g + c * plane + p, G[c]);
+    }
+  }
+  // block sums in double, fixed order
+  __shared__ double red[2][256];
+  red[0][threadIdx.x] = sl;
+  red[1][threadIdx.x] = sc;
+  __syncthreads();
+  for (int o = blockDim.x / 2; o > 0; o >>= 1) {
+    if (threadIdx.x < o) {
+      red[0][threadIdx.x] += red[0][threadIdx.x + o];
+      red[1][threadIdx.x] += red[1][threadIdx.x + o];
+    }
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) {
+    double* q = part + 2 * ((long long)img * gridDim.x + blockIdx.x);
+    q[0] = red[0][0];
+    q[1] = red[1][0];
+  }
+}
+
+__global__ void layered_loss_final_kernel(const double* __restrict__ part, int blocks, int n,
+                                          double wl_8n, double wc_3n, float* __restrict__ loss) {
+  const int img = blockIdx.x * blockDim.x + threadIdx.x;
+  if (img >= n) return;
+  double sl = 0.0, sc = 0.0;
+  for (int b = 0; b < blocks; ++b) {
+    sl += part[2 * ((long long)img * blocks + b)];
+    sc += part[2 * ((long long)img * blocks + b) + 1];
+  }
+  loss[img] = (float)(wl_8n * sl + wc_3n * sc);
+}
+
+template <int V>
+__global__ void __launch_bounds__(256) layered_compose_kernel(const float* __restrict__ recon,
+                                                              long long plane,
+                                                              float* __restrict__ out) {
+  const int img = blockIdx.y;
+  const float* r = recon + (long long)img * 8 * plane;
+  float* o = out + (long long)img * 3 * plane;
+  const long long nv = plane / V;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < nv;
+       i += (long long)gridDim.x * blockDim.x) {
+    const long long p = i * V;
+    float R[8][V], Y[3][V];
+#pragma unroll
+    for (int c = 0; c < 8; ++c) Vec<V>::ld(r + c * plane + p, R[c]);
+#pragma unroll
+    for (int k = 0; k < V; ++k) {
+      const float m = R[6][k], l = R[7][k], im = 1.f - m;
+#pragma unroll
+      for (int c = 0; c < 3; ++c)
+        Y[c][k] = fminf(fmaxf((R[c][k] * im + R[3 + c][k] * m) * l, 0.f), 1.f);
+    }
+#pragma unroll
+    for (int c = 0; c < 3; ++c) Vec<V>::st(o + c * plane + p, Y[c]);
+  }
+}
+
+static bool aligned16(const void* p) { return p == nullptr || ((uintptr_t)p & 15) == 0; }
+
+// blocks per image: enough for 8 resident 256-thread blocks per SM over the batch
+static int layered_blocks(yl_ctx* ctx, long long nv, int n) {
+  const long long want = (nv + 255) / 256;
+  const long long cap = std::max(1LL, (long long)ctx->num_sms * 8 / n);
+  return (int)std::max(1LL, std::min(want, cap));
+}
+
+}  // namespace yl
+
+extern "C" yl_status yl_layered_loss(yl_ctx* ctx, const float* recon, const float* target,
+                                     const float* comp, int n, long long plane, float layer_weight,
+                                     float compose_weight, float* grad, float* loss) {
+  using namespace yl;
+  YL_CHECK(ctx && recon && target && comp && (grad || loss), YL_ERR_INVALID,
+           "yl_layered_loss: NULL argument");
+  YL_CHECK(n >= 1 && plane >= 1 && n <= 65535, YL_ERR_SHAPE,
+           "yl_layered_loss: %d images of %lld pixels", n, plane);
+  const bool v4 = plane % 4 == 0 && aligned16(recon) && aligned16(target) && aligned16(comp) &&
+                  aligned16(grad);
+  const long long nv = v4 ? plane / 4 : plane;
+  const int blocks = layered_blocks(ctx, nv, n);
+  void* ws = nullptr;
+  YL_TRY(scratch_get(ctx, (size_t)n * blocks * 2 * sizeof(double), &ws));
+  double* part = (double*)ws;
+  const float dl = (float)(2.0 * layer_weight / (8.0 * (double)plane));
+  const float dc = (float)(2.0 * compose_weight / (3.0 * (double)plane));
+  if (v4)
+    layered_loss_kernel<4><<<dim3(blocks, n), 256, 0, ctx->stream>>>(recon, target, comp, plane,
+                                                                     dl, dc, grad, part);
+  else
+    layered_loss_kernel<1><<<dim3(blocks, n), 256, 0, ctx->stream>>>(recon, target, comp, plane,
+                                                                     dl, dc, grad, part);
+  YL_TRY(check_launch("layered_loss_kernel"));
+  if (!loss) return YL_OK;
+  layered_loss_final_kernel<<<(n + 127) / 128, 128, 0, ctx->stream>>>(
+      part, blocks, n, (double)layer_weight / (8.0 * (double)plane),
+      (double)compose_weight / (3.0 * (double)plane), loss);
+  return check_launch("layered_loss_final_kernel");
+}
+
+extern "C" yl_status yl_layered_compose(yl_ctx* ctx, const float* recon, int n, long long plane,
+                                        float* out) {
+  using namespace yl;
+  YL_CHECK(ctx && recon && out, YL_ERR_INVALID, "yl_layered_compose: NULL argument");
+  YL_CHECK(n >= 1 && plane >= 1 && n <= 65535, YL_ERR_SHAPE,
+           "yl_layered_compose: %d images of %lld pixels", n, plane);
+  const bool v4 = plane % 4 == 0 && aligned16(recon) && aligned16(out);
+  const long long nv = v4 ? plane / 4 : plane;
+  const int blocks = layered_blocks(ctx, nv, n);
+  if (v4)
+    layered_compose_kernel<4><<<dim3(blocks, n), 256, 0, ctx->stream>>>(recon, plane, out);
+  else
+    layered_compose_kernel<1><<<dim3(blocks, n), 256, 0, ctx->stream>>>(recon, plane, out);
+  return check_launch("layered_compose_kernel");
+}

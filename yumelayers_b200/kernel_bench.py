@@ -41,6 +41,8 @@ def main(argv=None):
     ap.add_argument("--reps", type=int, default=5)
     ap.add_argument("--only", default=None)
     ap.add_argument("--groupnorm", action="store_true")
+    ap.add_argument("--layered", action="store_true",
+                    help="layered 8-channel loss + gradient (108 B per pixel)")
     ap.add_argument("--adam", action="store_true",
                     help="one multi-tensor Adam step over the joint step's 28.5 M parameters")
     a = ap.parse_args(argv)
@@ -74,6 +76,12 @@ def main(argv=None):
         call("yl_profile_adam", ctx.handle, n, tensors, a.reps, C.byref(ms))
         print(json.dumps({"adam_params": n, "ms": ms.value,
                           "gbs": 28.0 * n / (ms.value * 1e-3) / 1e9}), flush=True)
+    if a.layered:
+        n, plane = (8, 480 * 856) if a.shapes == "vae" else (4, 480 * 856)
+        ms = C.c_double()
+        call("yl_profile_layered", ctx.handle, n, plane, a.reps, C.byref(ms))
+        print(json.dumps({"layered_loss": [n, 8, plane], "ms": ms.value,
+                          "gbs": 108.0 * n * plane / (ms.value * 1e-3) / 1e9}), flush=True)
     return 0
 
 

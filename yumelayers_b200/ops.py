@@ -196,3 +196,28 @@ def sobel_edge_loss(recon, target, ctx: Context | None = None):
     call("yl_sobel_edge_loss", ctx.handle, _ptr(rd), _ptr(td), n, h, w, LAYOUT_NCHW, 0, _ptr(gd),
          _ptr(ld))
     return ld.toArray()[:n], gd.toArray()[: recon.size].reshape(recon.shape)
+
+
+def layered_loss(recon, target, comp, layer_weight=1.0, compose_weight=1.0,
+                 ctx: Context | None = None):
+    """Per-image layered 8-channel loss and its gradient (layeredGrad,
+    GpuSessionOps.swift:565-585, with the loss of layeredLoss): recon and
+    target [n][8][h*w] CHW planes, comp [n][3][h*w]."""
+    ctx = ctx or Context.shared()
+    n = recon.shape[0]
+    plane = recon.size // (8 * n)
+    rd, td, cd = _dev(ctx, recon), _dev(ctx, target), _dev(ctx, comp)
+    gd, ld = _out(ctx, recon.size), _out(ctx, n)
+    call("yl_layered_loss", ctx.handle, _ptr(rd), _ptr(td), _ptr(cd), n, plane,
+         float(layer_weight), float(compose_weight), _ptr(gd), _ptr(ld))
+    return ld.toArray()[:n], gd.toArray()[: recon.size].reshape(recon.shape)
+
+
+def layered_compose(recon, ctx: Context | None = None):
+    """composeCHW (LayeredVAELoss.swift:95-110) of [n][8][h*w] planes -> [n][3][h*w]."""
+    ctx = ctx or Context.shared()
+    n = recon.shape[0]
+    plane = recon.size // (8 * n)
+    rd, od = _dev(ctx, recon), _out(ctx, 3 * n * plane)
+    call("yl_layered_compose", ctx.handle, _ptr(rd), n, plane, _ptr(od))
+    return od.toArray()[: 3 * n * plane].reshape(n, 3, plane)
