@@ -59,6 +59,22 @@ struct FpropCfg {
   static_assert(kTmemCols <= 512, "accumulators exceed TMEM");
 };
 
+// HALO (transposed 128 x 256 tile of a stride-1 3x3 conv): the three taps of
+// one kernel column (same dx, dy = d, d+1, d+2) read one box of 8 + 2 lattice
+// rows, and tap j's 256-pixel operand starts j image rows (4 KB, a whole
+// number of 1024-byte swizzle atoms) into it.  The boxes and the weight tiles
+// stream through two rings so each box is fetched once per three MMAs: 40 KB
+// of pixels per 3 taps instead of 96 KB.
+struct HaloCfg {
+  static constexpr int kBoxRows = 10;
+  static constexpr int kABox = 32 * kBoxRows * 128;  // 40 KB
+  static constexpr int kWTile = 128 * 128;           // 16 KB
+  static constexpr int kAS = 3, kWS = 6;
+  static constexpr int kRing = kAS * kABox + kWS * kWTile;
+  static constexpr int kSmemBytes = kRing + (2 * (kAS + kWS) + 4) * 8 + 16 + 1024;
+  static_assert(kSmemBytes <= 227 * 1024, "halo rings exceed shared memory");
+};
+
 struct FpropTile {
   int nb, z, img, ty, tx;
 };
@@ -146,7 +162,7 @@ __device__ __forceinline__ void gn_chunk_partials_any(int cg, const float (&v)[3
 // TMEM then holds [channel][pixel]: epilogue thread = one output channel,
 // and each store instruction of a warp writes 32 consecutive channels of one
 // pixel.
-template <int BN, int MT, bool TR = false>
+template <int BN, int MT, bool TR = false, bool HALO = false>
 __global__ void __launch_bounds__(kThreads, 1)
     conv_tma_fprop_kernel(const __grid_constant__ CUtensorMap ta0,
                           const __grid_constant__ CUtensorMap ta1,
@@ -154,24 +170,25 @@ __global__ void __launch_bounds__(kThreads, 1)
                           const __grid_constant__ CUtensorMap ta3,
                           const __grid_constant__ CUtensorMap tw, ConvPlan p, ConvEpilogue e,
                           int* err) {
+  static_assert(!HALO || (TR && BN == 128 && MT == 2), "halo boxes feed the transposed tile");
   using Cfg = FpropCfg<BN, MT>;
   constexpr int S = Cfg::kStages;
   constexpr int kRows = 4 * MT;  // lattice rows per tile
+  constexpr int kRing = HALO ? HaloCfg::kRing : S * Cfg::kStage;
+  constexpr int kRingBars = HALO ? 2 * (HaloCfg::kAS + HaloCfg::kWS) : 2 * S;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * Cfg::kStage);
+  // plain: full[S], empty[S]; halo: box full/empty [kAS], weight full/empty [kWS]
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kRing);
   uint64_t* empty = full + S;
-  uint64_t* acc_full = empty + S;      // [2]: MMA -> epilogue
-  uint64_t* acc_empty = acc_full + 2;  // [2]: epilogue (128 threads) -> MMA
+  uint64_t* acc_full = full + kRingBars;  // [2]: MMA -> epilogue
+  uint64_t* acc_empty = acc_full + 2;     // [2]: epilogue (128 threads) -> MMA
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < S; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1);
-    }
+    for (int s = 0; s < kRingBars; ++s) mbar_init(&full[s], 1);
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
       mbar_init(&acc_empty[b], 128);
@@ -191,7 +208,102 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 4) {
+  if (HALO && warp == 4) {
+    if (lane == 0) {
+      // per tile: kernel column g (taps g, g+3, g+6), 32-channel chunk c:
+      // one 10-row pixel box, then the three taps' weight tiles
+      constexpr int AS = HaloCfg::kAS, WS = HaloCfg::kWS;
+      uint64_t* afull = full;
+      uint64_t* aempty = full + AS;
+      uint64_t* wfull = full + 2 * AS;
+      uint64_t* wempty = wfull + WS;
+      uint32_t ia = 0, iw = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < p.n_tiles; tile += gridDim.x) {
+        const FpropTile c = fprop_tile(p, tile);
+        const TapPhase& ph = p.ph[0];
+        const int ox0 = c.tx * 32, oy0 = c.ty * kRows, n0 = c.nb * BN;
+        for (int g = 0; ok && g < 3; ++g) {
+          const int dy0 = min(ph.dy[g], min(ph.dy[g + 3], ph.dy[g + 6]));
+          for (int ch = 0; ch < p.cpt; ++ch, ++ia) {
+            const int sa = ia % AS;
+            if (ia >= AS && !mbar_wait(&aempty[sa], ((ia / AS) - 1) & 1)) {
+              ok = false;
+              break;
+            }
+            mbar_arrive_expect_tx(&afull[sa], HaloCfg::kABox);
+            tma_load_4d(smem_u32(smem + sa * HaloCfg::kABox), &ta0, &afull[sa], ch * 32,
+                        ox0 + ph.dx[g], oy0 + dy0, c.img);
+            for (int j = 0; j < 3; ++j, ++iw) {
+              const int sw = iw % WS;
+              if (iw >= WS && !mbar_wait(&wempty[sw], ((iw / WS) - 1) & 1)) {
+                ok = false;
+                break;
+              }
+              mbar_arrive_expect_tx(&wfull[sw], HaloCfg::kWTile);
+              tma_load_2d(smem_u32(smem + AS * HaloCfg::kABox + sw * HaloCfg::kWTile), &tw,
+                          &wfull[sw], ((g + 3 * j) * p.cpt + ch) * kBK, ph.w_row0 + n0);
+            }
+            if (!ok) break;
+          }
+        }
+      }
+      if (!ok) report_error(err, YL_DEVERR_TIMEOUT);
+    }
+  } else if (HALO && warp == 5) {
+    if (lane == 0) {
+      constexpr int AS = HaloCfg::kAS, WS = HaloCfg::kWS;
+      uint64_t* afull = full;
+      uint64_t* aempty = full + AS;
+      uint64_t* wfull = full + 2 * AS;
+      uint64_t* wempty = wfull + WS;
+      constexpr uint32_t idesc = idesc_tf32(BN, MT * kBM, 0, 0);
+      uint32_t ia = 0, iw = 0;
+      int tc = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < p.n_tiles; tile += gridDim.x, ++tc) {
+        const int buf = tc & 1, use = tc >> 1;
+        if (tc >= 2 && !mbar_wait(&acc_empty[buf], (use - 1) & 1)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const TapPhase& ph = p.ph[0];
+        const uint32_t dacc = tmem + (uint32_t)(buf * Cfg::kAccCols);
+        for (int g = 0; ok && g < 3; ++g) {
+          const int dy0 = min(ph.dy[g], min(ph.dy[g + 3], ph.dy[g + 6]));
+          for (int ch = 0; ch < p.cpt; ++ch, ++ia) {
+            const int sa = ia % AS;
+            if (!mbar_wait(&afull[sa], (ia / AS) & 1)) {
+              ok = false;
+              break;
+            }
+            const uint32_t box = smem_u32(smem + sa * HaloCfg::kABox);
+            for (int j = 0; j < 3; ++j, ++iw) {
+              const int sw = iw % WS;
+              if (!mbar_wait(&wfull[sw], (iw / WS) & 1)) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+              // tap j's pixels: image row (dy - dy0) of the box, 32 px x 128 B per row
+              const uint32_t px = box + (uint32_t)((ph.dy[g + 3 * j] - dy0) * 32 * 128);
+              const uint32_t wt = smem_u32(smem + AS * HaloCfg::kABox + sw * HaloCfg::kWTile);
+#pragma unroll
+              for (int kk = 0; kk < kBK / 8; ++kk)
+                umma_tf32(dacc, sw128_desc(wt + kk * 32, 16, 1024),
+                          sw128_desc(px + kk * 32, 16, 1024), idesc, (g | ch | j | kk) != 0);
+              umma_commit(&wempty[sw]);
+            }
+            if (!ok) break;
+            umma_commit(&aempty[sa]);
+          }
+        }
+        if (ok) umma_commit(&acc_full[buf]);
+      }
+      if (!ok) report_error(err, YL_DEVERR_TIMEOUT);
+    }
+  } else if (warp == 4) {
     if (lane == 0) {
       const CUtensorMap* maps[4] = {&ta0, &ta1, &ta2, &ta3};
       uint32_t it = 0;
@@ -919,14 +1031,15 @@ __global__ void __launch_bounds__(128) gn_tile_stats_kernel(
   rstd[idx] = (float)(1.0 / sqrt(var + (double)eps));
 }
 
-template <int BN, int MT, bool TR = false>
+template <int BN, int MT, bool TR = false, bool HALO = false>
 static yl_status launch_plan(yl_ctx* ctx, const View* views, int nviews, const float* w, int w_rows,
                              int w_cols, ConvPlan& p, int nphase, const ConvEpilogue& e) {
   using Cfg = FpropCfg<BN, MT>;
+  constexpr int kSmem = HALO ? HaloCfg::kSmemBytes : Cfg::kSmemBytes;
   CUtensorMap ta[4], tw;
   for (int i = 0; i < 4; ++i)
-    YL_TRY(make_view_tmap(&ta[i], views[i < nviews ? i : 0], 32, 4 * MT,
-                          CU_TENSOR_MAP_SWIZZLE_128B));
+    YL_TRY(make_view_tmap(&ta[i], views[i < nviews ? i : 0], 32,
+                          HALO ? HaloCfg::kBoxRows : 4 * MT, CU_TENSOR_MAP_SWIZZLE_128B));
   YL_TRY(make_weight_tmap(&tw, w, w_rows, w_cols, BN));
   p.tiles_x = (p.gw + 31) / 32;
   p.tiles_y = (p.gh + 4 * MT - 1) / (4 * MT);
@@ -948,16 +1061,34 @@ static yl_status launch_plan(yl_ctx* ctx, const View* views, int nviews, const f
     YL_TRY(scratch_get(ctx, (size_t)p.n_tiles * slots * gpb * sizeof(float2), &part, 2));
     ek.gn_part = (float2*)part;
   }
-  YL_CUDA(cudaFuncSetAttribute(conv_tma_fprop_kernel<BN, MT, TR>,
-                               cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes));
+  YL_CUDA(cudaFuncSetAttribute(conv_tma_fprop_kernel<BN, MT, TR, HALO>,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem));
   const int grid = p.n_tiles < ctx->num_sms ? p.n_tiles : ctx->num_sms;
-  conv_tma_fprop_kernel<BN, MT, TR><<<grid, kThreads, Cfg::kSmemBytes, ctx->stream>>>(
+  conv_tma_fprop_kernel<BN, MT, TR, HALO><<<grid, kThreads, kSmem, ctx->stream>>>(
       ta[0], ta[1], ta[2], ta[3], tw, p, ek, ctx->dev_err);
   YL_TRY(check_launch("conv_tma_fprop_kernel"));
   if (!e.gn_mean) return YL_OK;
   gn_tile_stats_kernel<<<p.n_img * e.gn_groups, 128, 0, ctx->stream>>>(
       ek.gn_part, p, nphase, slots, gpb, e.gn_groups, ek.gn_cg, e.gn_eps, e.gn_mean, e.gn_rstd);
   return check_launch("gn_tile_stats_kernel");
+}
+
+// The halo path's tap structure: one phase over one view, 9 taps whose
+// kernel columns g (taps g, g+3, g+6) share a dx and span at most 3 rows.
+static bool halo_taps(const ConvPlan& p, int nphase, int nviews) {
+  if (nphase != 1 || nviews != 1 || p.ph[0].ntaps != 9) return false;
+  const TapPhase& ph = p.ph[0];
+  for (int g = 0; g < 3; ++g) {
+    int lo = 127, hi = -128;
+    for (int j = 0; j < 3; ++j) {
+      const int t = g + 3 * j;
+      if (ph.map[t] != 0 || ph.dx[t] != ph.dx[g]) return false;
+      lo = std::min(lo, (int)ph.dy[t]);
+      hi = std::max(hi, (int)ph.dy[t]);
+    }
+    if (hi - lo > HaloCfg::kBoxRows - 8) return false;
+  }
+  return true;
 }
 
 // Tile choice: BN covers the output channels in as few blocks as possible;
@@ -976,8 +1107,11 @@ static yl_status run_plan(yl_ctx* ctx, const View* views, int nviews, const floa
     if (tall) return launch_plan<64, 2>(ctx, views, nviews, w, w_rows, w_cols, p, nphase, e);
     return launch_plan<64, 1>(ctx, views, nviews, w, w_rows, w_cols, p, nphase, e);
   }
-  if (tall && e.n_total % 128 == 0 && min_nk >= 9)
+  if (tall && e.n_total % 128 == 0 && min_nk >= 9) {
+    if (halo_taps(p, nphase, nviews))
+      return launch_plan<128, 2, true, true>(ctx, views, nviews, w, w_rows, w_cols, p, nphase, e);
     return launch_plan<128, 2, true>(ctx, views, nviews, w, w_rows, w_cols, p, nphase, e);
+  }
   if (e.n_total <= 128 || e.n_total % 256 != 0) {
     if (tall && e.n_total <= 128 && min_nk >= 9)
       return launch_plan<128, 2, true>(ctx, views, nviews, w, w_rows, w_cols, p, nphase, e);
