@@ -680,7 +680,7 @@ struct Vec<4> {
 };
 
 template <int V>
-__global__ void __launch_bounds__(256) layered_loss_kernel(
+__global__ void __launch_bounds__(256, 4) layered_loss_kernel(
     const float* __restrict__ recon, const float* __restrict__ target,
     const float* __restrict__ comp, long long plane, float dl, float dc,
     float* __restrict__ grad, double* __restrict__ part) {
@@ -694,43 +694,55 @@ __global__ void __launch_bounds__(256) layered_loss_kernel(
   for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < nv;
        i += (long long)gridDim.x * blockDim.x) {
     const long long p = i * V;
-    float R[8][V], T[8][V], C3[3][V], G[8][V];
+    float m[V], l[V], dm[V], dlt[V];
+    Vec<V>::ld(r + 6 * plane + p, m);
+    Vec<V>::ld(r + 7 * plane + p, l);
 #pragma unroll
-    for (int c = 0; c < 8; ++c) {
-      Vec<V>::ld(r + c * plane + p, R[c]);
-      Vec<V>::ld(t + c * plane + p, T[c]);
-    }
+    for (int k = 0; k < V; ++k) dm[k] = dlt[k] = 0.f;
+    // one colour channel at a time: background and object planes, their
+    // targets and the frame channel in, both gradient planes out
 #pragma unroll
-    for (int c = 0; c < 3; ++c) Vec<V>::ld(cp + c * plane + p, C3[c]);
+    for (int c = 0; c < 3; ++c) {
+      float bg[V], ob[V], tb[V], to[V], y[V], gb[V], go[V];
+      Vec<V>::ld(r + c * plane + p, bg);
+      Vec<V>::ld(r + (3 + c) * plane + p, ob);
+      Vec<V>::ld(t + c * plane + p, tb);
+      Vec<V>::ld(t + (3 + c) * plane + p, to);
+      Vec<V>::ld(cp + c * plane + p, y);
 #pragma unroll
-    for (int k = 0; k < V; ++k) {
-      const float m = R[6][k], l = R[7][k], im = 1.f - m;
-      float dm = 0.f, dlt = 0.f;
-#pragma unroll
-      for (int c = 0; c < 3; ++c) {
-        const float bg = R[c][k], ob = R[3 + c][k];
-        const float base = bg * im + ob * m;
-        const float v = base * l;
-        const float e = fminf(fmaxf(v, 0.f), 1.f) - C3[c][k];
+      for (int k = 0; k < V; ++k) {
+        const float im = 1.f - m[k];
+        const float base = bg[k] * im + ob[k] * m[k];
+        const float v = base * l[k];
+        const float e = fminf(fmaxf(v, 0.f), 1.f) - y[k];
         sc = fmaf(e, e, sc);
         // the clamp passes the gradient only strictly inside (0, 1)
         const float gc = (v > 0.f && v < 1.f) ? dc * e : 0.f;
-        G[c][k] = dl * (bg - T[c][k]) + gc * l * im;
-        G[3 + c][k] = dl * (ob - T[3 + c][k]) + gc * l * m;
-        dm += gc * l * (ob - bg);
-        dlt += gc * base;
+        const float db = bg[k] - tb[k], dob = ob[k] - to[k];
+        sl = fmaf(db, db, fmaf(dob, dob, sl));
+        gb[k] = dl * db + gc * l[k] * im;
+        go[k] = dl * dob + gc * l[k] * m[k];
+        dm[k] += gc * l[k] * (ob[k] - bg[k]);
+        dlt[k] += gc * base;
       }
-      G[6][k] = dl * (m - T[6][k]) + dm;
-      G[7][k] = dl * (l - T[7][k]) + dlt;
-#pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        const float d = R[c][k] - T[c][k];
-        sl = fmaf(d, d, sl);
+      if (g) {
+        Vec<V>::st(g + c * plane + p, gb);
+        Vec<V>::st(g + (3 + c) * plane + p, go);
       }
     }
-    if (g) {
+    float tm[V], tl[V];
+    Vec<V>::ld(t + 6 * plane + p, tm);
+    Vec<V>::ld(t + 7 * plane + p, tl);
 #pragma unroll
-      for (int c = 0; c < 8; ++c) Vec<V>::st(g + c * plane + p, G[c]);
+    for (int k = 0; k < V; ++k) {
+      const float d6 = m[k] - tm[k], d7 = l[k] - tl[k];
+      sl = fmaf(d6, d6, fmaf(d7, d7, sl));
+      tm[k] = dl * d6 + dm[k];
+      tl[k] = dl * d7 + dlt[k];
+    }
+    if (g) {
+      Vec<V>::st(g + 6 * plane + p, tm);
+      Vec<V>::st(g + 7 * plane + p, tl);
     }
   }
   // block sums in double, fixed order
@@ -792,10 +804,10 @@ __global__ void __launch_bounds__(256) layered_compose_kernel(const float* __res
 
 static bool aligned16(const void* p) { return p == nullptr || ((uintptr_t)p & 15) == 0; }
 
-// blocks per image: enough for 8 resident 256-thread blocks per SM over the batch
+// blocks per image: one wave of 4 resident 256-thread blocks per SM over the batch
 static int layered_blocks(yl_ctx* ctx, long long nv, int n) {
   const long long want = (nv + 255) / 256;
-  const long long cap = std::max(1LL, (long long)ctx->num_sms * 8 / n);
+  const long long cap = std::max(1LL, (long long)ctx->num_sms * 4 / n);
   return (int)std::max(1LL, std::min(want, cap));
 }
 
