@@ -28,7 +28,11 @@
 
 namespace yl {
 
-__device__ __forceinline__ float silu_f(float a) { return a / (1.f + __expf(-a)); }
+// SiLU and the logistic function with the approximate divide (2 ulp): the
+// GroupNorm passes are bandwidth kernels that the IEEE divide's extra
+// instructions would otherwise make issue-bound.
+__device__ __forceinline__ float silu_f(float a) { return __fdividef(a, 1.f + __expf(-a)); }
+__device__ __forceinline__ float sigmoid_f(float a) { return __fdividef(1.f, 1.f + __expf(-a)); }
 
 // Launch geometry shared by all GroupNorm kernels.  A block is quads x rows
 // threads; thread (quad, row) owns channels [4*quad, 4*quad+4) and walks the
@@ -220,8 +224,8 @@ __device__ __forceinline__ void gn_bwd_elem(float x, float dy, float ga, float b
   float d = dy;
   if (silu) {
     const float a = fmaf(*xh, ga, be);
-    const float sg = 1.f / (1.f + __expf(-a));
-    d *= sg * (1.f + a * (1.f - sg));
+    const float sg = sigmoid_f(a);
+    d *= sg * fmaf(a, 1.f - sg, 1.f);
   }
   *da = d;
 }
@@ -271,7 +275,6 @@ __global__ void __launch_bounds__(256, 4)
         dv[u] = __ldg(reinterpret_cast<const float4*>(db + pp * lddy));
       }
     }
-    float fsd = 0.f, fsdx = 0.f;
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
       if (p + u * R >= p1) break;
@@ -281,14 +284,16 @@ __global__ void __launch_bounds__(256, 4)
       for (int k = 0; k < 4; ++k) {
         float xh, dd;
         gn_bwd_elem(xs[k], ds[k], ga[k], be[k], m, r, silu, &xh, &dd);
-        dg[k] += dd * xh;
+        dg[k] = fmaf(dd, xh, dg[k]);
         dbt[k] += dd;
-        fsd += dd * ga[k];
-        fsdx += dd * xh * ga[k];
       }
     }
-    sd += fsd;
-    sdx += fsdx;
+  }
+  // the group sums of gamma*da and gamma*da*xh follow from the channel sums
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    sd = fmaf(ga[k], dbt[k], sd);
+    sdx = fmaf(ga[k], dg[k], sdx);
   }
   if (p0 + row < p1) {
     atomicAdd(&sh[2 * grp], (double)sd);
