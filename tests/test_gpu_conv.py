@@ -44,6 +44,7 @@ CASES = [
     ("s2_odd_c128_256", 1, 128, 256, 15, 17, 3, 2, 1, False, None),
     ("c256_to_128", 1, 256, 128, 30, 54, 3, 1, 1, False, None),
     ("c128_tall_ragged", 1, 128, 128, 67, 40, 3, 1, 1, False, None),
+    ("c128_h60_wide", 2, 128, 128, 60, 300, 3, 1, 1, False, None),
 ]
 
 

@@ -41,6 +41,7 @@ struct ConvPlan {
   int n_nblk;          // BN-wide blocks of output channels
   int pix_tiles;       // tiles_x * tiles_y * n_img
   int n_tiles;         // pix_tiles * n_nblk * phases
+  int tma_out;         // non-transposed epilogue: stage rows in shared memory, TMA store
   TapPhase ph[4];      // indexed by the tile's phase
 };
 
@@ -52,11 +53,16 @@ struct FpropCfg {
   static constexpr int kATile = MT * kATileBytes;
   static constexpr int kBTile = BN * 128;
   static constexpr int kStage = kATile + kBTile;
-  static constexpr int kStages = (200 * 1024) / kStage > 8 ? 8 : (200 * 1024) / kStage;
+  // output staging of the non-transposed epilogue: 2 buffers of one lattice
+  // row (32 pixels x 32 channels, 4 KB) per epilogue warp
+  static constexpr int kOut = 4 * 2 * 4096;
+  static constexpr int kFit = (227 * 1024 - kOut - 2048) / kStage;
+  static constexpr int kStages = kFit > 8 ? 8 : kFit;
   static constexpr int kAccCols = MT * BN < 32 ? 32 : MT * BN;
   static constexpr int kTmemCols = 2 * kAccCols;  // two accumulator buffers
-  static constexpr int kSmemBytes = kStages * kStage + (2 * kStages + 4) * 8 + 16 + 1024;
+  static constexpr int kSmemBytes = kStages * kStage + kOut + (2 * kStages + 4) * 8 + 16 + 1024;
   static_assert(kTmemCols <= 512, "accumulators exceed TMEM");
+  static_assert(kSmemBytes <= 227 * 1024, "stages exceed shared memory");
 };
 
 // HALO (transposed 128 x 256 tile of a stride-1 3x3 conv): the three taps of
@@ -168,13 +174,17 @@ __global__ void __launch_bounds__(kThreads, 1)
                           const __grid_constant__ CUtensorMap ta1,
                           const __grid_constant__ CUtensorMap ta2,
                           const __grid_constant__ CUtensorMap ta3,
-                          const __grid_constant__ CUtensorMap tw, ConvPlan p, ConvEpilogue e,
+                          const __grid_constant__ CUtensorMap tw,
+                          const __grid_constant__ CUtensorMap to0,
+                          const __grid_constant__ CUtensorMap to1,
+                          const __grid_constant__ CUtensorMap to2,
+                          const __grid_constant__ CUtensorMap to3, ConvPlan p, ConvEpilogue e,
                           int* err) {
   static_assert(!HALO || (TR && BN == 128 && MT == 2), "halo boxes feed the transposed tile");
   using Cfg = FpropCfg<BN, MT>;
   constexpr int S = Cfg::kStages;
   constexpr int kRows = 4 * MT;  // lattice rows per tile
-  constexpr int kRing = HALO ? HaloCfg::kRing : S * Cfg::kStage;
+  constexpr int kRing = HALO ? HaloCfg::kRing : S * Cfg::kStage + Cfg::kOut;
   constexpr int kRingBars = HALO ? 2 * (HaloCfg::kAS + HaloCfg::kWS) : 2 * S;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
@@ -381,6 +391,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     // epilogue: warp w owns TMEM lanes 32w..32w+31 = lattice row 4m + w of subtile m
     int tc = 0;
+    uint32_t ost = 0;  // TMA-stored row chunks of this warp (staging buffer = ost & 1)
     for (int tile = blockIdx.x; tile < p.n_tiles; tile += gridDim.x, ++tc) {
       const int buf = tc & 1, use = tc >> 1;
       const FpropTile c = fprop_tile(p, tile);
@@ -522,16 +533,41 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
               for (int q = 0; q < 32; ++q) v[q] = round_tf32(v[q]);
             }
-            float* op = e.out + mrow * e.ldo + nb;
-            if (full32 && (e.ldo & 3) == 0) {
+            if (!p.tma_out) {
+              float* op = e.out + mrow * e.ldo + nb;
+              if (full32 && (e.ldo & 3) == 0) {
 #pragma unroll
-              for (int q = 0; q < 32; q += 4)
-                *reinterpret_cast<float4*>(op + q) = make_float4(v[q], v[q + 1], v[q + 2], v[q + 3]);
-            } else {
+                for (int q = 0; q < 32; q += 4)
+                  *reinterpret_cast<float4*>(op + q) =
+                      make_float4(v[q], v[q + 1], v[q + 2], v[q + 3]);
+              } else {
 #pragma unroll
-              for (int q = 0; q < 32; ++q)
-                if (nb + q < e.n_total) op[q] = v[q];
+                for (int q = 0; q < 32; ++q)
+                  if (nb + q < e.n_total) op[q] = v[q];
+              }
             }
+          }
+          if (p.tma_out) {
+            // the warp's lattice row (32 pixels x these 32 channels) through a
+            // 128-byte-swizzled staging buffer and one TMA store: whole lines
+            // per request instead of 16-byte pieces of 32 pixels' lines
+            uint8_t* ob = smem + S * Cfg::kStage + (warp * 2 + (ost & 1)) * 4096;
+            if (ost >= 2) {
+              if (lane == 0) bulk_wait_group_read<1>();
+              __syncwarp();
+            }
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+              *reinterpret_cast<float4*>(ob + lane * 128 + ((j ^ (lane & 7)) << 4)) =
+                  make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0 && gy < p.gh) {
+              const CUtensorMap* om = c.z == 0 ? &to0 : c.z == 1 ? &to1 : c.z == 2 ? &to2 : &to3;
+              tma_store_4d(om, smem_u32(ob), nb, c.tx * 32, gy, c.img);
+              bulk_commit_group();
+            }
+            ++ost;
           }
           if (e.gn_part) {
             const int gpb = BN / e.gn_cg;
@@ -543,6 +579,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       mbar_arrive(&acc_empty[buf]);
     }
+    if (p.tma_out && lane == 0) bulk_wait_group_all();
   }
 
   tc_fence_before();
@@ -1041,6 +1078,20 @@ static yl_status launch_plan(yl_ctx* ctx, const View* views, int nviews, const f
     YL_TRY(make_view_tmap(&ta[i], views[i < nviews ? i : 0], 32,
                           HALO ? HaloCfg::kBoxRows : 4 * MT, CU_TENSOR_MAP_SWIZZLE_128B));
   YL_TRY(make_weight_tmap(&tw, w, w_rows, w_cols, BN));
+  // output of each phase as a strided view of the lattice (the non-transposed
+  // epilogue stores whole lattice rows through these)
+  CUtensorMap to[4];
+  p.tma_out = !TR && (e.ldo & 3) == 0 && ((uintptr_t)e.out & 15) == 0;
+  for (int z = 0; z < 4; ++z) {
+    const TapPhase& ph = p.ph[z < nphase ? z : 0];
+    View ov{e.out + ((long long)ph.ya * p.out_w + ph.xa) * e.ldo, e.n_total,
+            std::min(p.gw, (p.out_w - ph.xa + p.xs - 1) / p.xs),
+            std::min(p.gh, (p.out_h - ph.ya + p.ys - 1) / p.ys), p.n_img,
+            (long long)p.xs * e.ldo, (long long)p.ys * p.out_w * e.ldo,
+            (long long)p.out_h * p.out_w * e.ldo};
+    if (p.tma_out) YL_TRY(make_view_tmap(&to[z], ov, 32, 1, CU_TENSOR_MAP_SWIZZLE_128B));
+    else to[z] = tw;  // unused
+  }
   p.tiles_x = (p.gw + 31) / 32;
   p.tiles_y = (p.gh + 4 * MT - 1) / (4 * MT);
   p.n_nblk = (e.n_total + BN - 1) / BN;
@@ -1065,7 +1116,7 @@ static yl_status launch_plan(yl_ctx* ctx, const View* views, int nviews, const f
                                cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem));
   const int grid = p.n_tiles < ctx->num_sms ? p.n_tiles : ctx->num_sms;
   conv_tma_fprop_kernel<BN, MT, TR, HALO><<<grid, kThreads, kSmem, ctx->stream>>>(
-      ta[0], ta[1], ta[2], ta[3], tw, p, ek, ctx->dev_err);
+      ta[0], ta[1], ta[2], ta[3], tw, to[0], to[1], to[2], to[3], p, ek, ctx->dev_err);
   YL_TRY(check_launch("conv_tma_fprop_kernel"));
   if (!e.gn_mean) return YL_OK;
   gn_tile_stats_kernel<<<p.n_img * e.gn_groups, 128, 0, ctx->stream>>>(
@@ -1097,7 +1148,14 @@ static bool halo_taps(const ConvPlan& p, int nphase, int nviews) {
 // waste little of the last tile row.
 static yl_status run_plan(yl_ctx* ctx, const View* views, int nviews, const float* w, int w_rows,
                           int w_cols, ConvPlan& p, int nphase, const ConvEpilogue& e) {
-  const bool tall = p.gh % 8 == 0 || p.gh >= 64;
+  // 8-row tiles when the last tile row wastes little: none (a multiple of 8
+  // rows), a tall lattice, or at most 1/16 of the rows while the 8-row tiles
+  // still fill the SMs
+  const int t8 = (p.gh + 7) / 8;
+  const long long tiles8 = (long long)t8 * ((p.gw + 31) / 32) * p.n_img * nphase *
+                           ((e.n_total + 127) / 128);
+  const bool tall = p.gh % 8 == 0 || p.gh >= 64 ||
+                    ((t8 * 8 - p.gh) * 16 <= t8 * 8 && tiles8 >= ctx->num_sms);
   // the transposed epilogue costs more instructions per tile: only worth it
   // when every tile has a long k loop
   int min_nk = 1 << 30;

@@ -2,7 +2,7 @@
 shapes (the B200 counterpart of the reference's profileConv, Diagnostics.swift:
 124-201).  Prints one JSON line per shape.
 
-    python -m yumelayers_b200.kernel_bench [--shapes vae|small] [--reps R] [--only NAME]
+    python -m yumelayers_b200.kernel_bench [--shapes vae|unet|epilogue|small] [--reps R] [--only NAME]
 """
 from __future__ import annotations
 
@@ -28,6 +28,19 @@ VAE_SHAPES = [
     ("up3_256_128", 8, 256, 240, 428, 128, 3, 1, 1),
     ("up2_256_256", 8, 256, 120, 214, 256, 3, 1, 1),
 ]
+# the motion U-Net's 3x3 convs on batch-8 latents of 60x107 (and its two
+# down-sampled levels)
+UNET_SHAPES = [
+    ("u60_128_128", 8, 128, 60, 107, 128, 3, 1, 0),
+    ("u30_256_256", 8, 256, 30, 54, 256, 3, 1, 0),
+    ("u15_384_384", 8, 384, 15, 27, 384, 3, 1, 0),
+    ("u30_512_256", 8, 512, 30, 54, 256, 3, 1, 0),
+]
+# pointwise GEMMs whose time is the epilogue's (one or two 32-channel k-blocks)
+EPILOGUE_SHAPES = [
+    ("pw_32_128", 8, 32, 480, 856, 128, 1, 1, 0),
+    ("pw_64_128", 8, 64, 480, 856, 128, 1, 1, 0),
+]
 SMALL_SHAPES = [
     ("small_128_128", 8, 128, 192, 192, 128, 3, 1, 0),
     ("small_256_256", 8, 256, 96, 192, 256, 3, 1, 0),
@@ -37,7 +50,7 @@ SMALL_SHAPES = [
 
 def main(argv=None):
     ap = argparse.ArgumentParser()
-    ap.add_argument("--shapes", default="vae", choices=["vae", "small"])
+    ap.add_argument("--shapes", default="vae", choices=["vae", "unet", "epilogue", "small"])
     ap.add_argument("--reps", type=int, default=5)
     ap.add_argument("--only", default=None)
     ap.add_argument("--groupnorm", action="store_true")
@@ -47,7 +60,8 @@ def main(argv=None):
                     help="one multi-tensor Adam step over the joint step's 28.5 M parameters")
     a = ap.parse_args(argv)
     ctx = Context.shared(0)
-    shapes = VAE_SHAPES if a.shapes == "vae" else SMALL_SHAPES
+    shapes = {"vae": VAE_SHAPES, "unet": UNET_SHAPES, "epilogue": EPILOGUE_SHAPES,
+              "small": SMALL_SHAPES}[a.shapes]
     for name, n, c, h, w, oc, k, s, up in shapes:
         if a.only and a.only != name:
             continue
