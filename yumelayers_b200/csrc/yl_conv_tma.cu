@@ -75,8 +75,9 @@ struct HaloCfg {
   static constexpr int kBoxRows = 10;
   static constexpr int kABox = 32 * kBoxRows * 128;  // 40 KB
   static constexpr int kWTile = 128 * 128;           // 16 KB
-  static constexpr int kAS = 3, kWS = 6;
-  static constexpr int kRing = kAS * kABox + kWS * kWTile;
+  static constexpr int kAS = 2, kWS = 6;
+  static constexpr int kOut = 4 * 2 * 4096;  // epilogue staging, as FpropCfg::kOut
+  static constexpr int kRing = kAS * kABox + kWS * kWTile + kOut;
   static constexpr int kSmemBytes = kRing + (2 * (kAS + kWS) + 4) * 8 + 16 + 1024;
   static_assert(kSmemBytes <= 227 * 1024, "halo rings exceed shared memory");
 };
@@ -185,6 +186,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr int S = Cfg::kStages;
   constexpr int kRows = 4 * MT;  // lattice rows per tile
   constexpr int kRing = HALO ? HaloCfg::kRing : S * Cfg::kStage + Cfg::kOut;
+  // epilogue staging: 2 buffers of 4 KB per epilogue warp after the operand rings
+  constexpr int kOutOff = HALO ? kRing - HaloCfg::kOut : S * Cfg::kStage;
   constexpr int kRingBars = HALO ? 2 * (HaloCfg::kAS + HaloCfg::kWS) : 2 * S;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
@@ -435,7 +438,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_ld_wait();
           const int gy = c.ty * kRows + j;
           const int Y = gy * p.ys + ph.ya;
-          if (!cval || gy >= p.gh || Y >= p.out_h) continue;
+          if (gy >= p.gh || Y >= p.out_h) continue;
           const long long rowp = ((long long)c.img * p.out_h + Y) * p.out_w;
           // columns q < qn are inside the lattice and the image (both bounds
           // are monotone in q); addresses advance by a fixed 32-bit stride
@@ -450,24 +453,50 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int q = 0; q < 32; ++q) v[q] = __uint_as_float(r[q]) + badd;
           if (e.residual) {
-            const float* rrow = e.residual + (rowp + X0) * e.ldr + co;
+            const float* rrow = e.residual + (rowp + X0) * e.ldr + (cval ? co : 0);
             const int sr = p.xs * e.ldr;
             float rv[32];
 #pragma unroll
-            for (int q = 0; q < 32; ++q) rv[q] = q < qn ? rrow[q * sr] : 0.f;
+            for (int q = 0; q < 32; ++q) rv[q] = cval && q < qn ? rrow[q * sr] : 0.f;
 #pragma unroll
             for (int q = 0; q < 32; ++q) v[q] += rv[q];
           }
-          float* orow = e.out + (rowp + X0) * e.ldo + co;
-          const int so = p.xs * e.ldo;
 #pragma unroll
           for (int q = 0; q < 32; ++q) {
             if (e.round_tf32) v[q] = round_tf32(v[q]);
-            if (q < qn) {
-              orow[q * so] = v[q];
+            if (cval && q < qn) {
               gs += v[q];
               gss += v[q] * v[q];
             }
+          }
+          if (p.tma_out) {
+            // staging row q = pixel q, this lane's channel at 4-byte column
+            // `lane` of the 128-byte row (16-byte chunks swizzled by q), then
+            // one TMA store of the warp's 32 pixels x 32 channels
+            uint8_t* ob = smem + kOutOff + (warp * 2 + (ost & 1)) * 4096;
+            if (ost >= 2) {
+              if (lane == 0) bulk_wait_group_read<1>();
+              __syncwarp();
+            }
+            const uint32_t col = (uint32_t)(lane & 3) << 2;
+#pragma unroll
+            for (int q = 0; q < 32; ++q)
+              *reinterpret_cast<float*>(ob + q * 128 + ((((lane >> 2) ^ (q & 7)) << 4) | col)) =
+                  v[q];
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              const CUtensorMap* om = c.z == 0 ? &to0 : c.z == 1 ? &to1 : c.z == 2 ? &to2 : &to3;
+              tma_store_4d(om, smem_u32(ob), n0 + warp * 32, c.tx * 32, gy, c.img);
+              bulk_commit_group();
+            }
+            ++ost;
+          } else if (cval) {
+            float* orow = e.out + (rowp + X0) * e.ldo + co;
+            const int so = p.xs * e.ldo;
+#pragma unroll
+            for (int q = 0; q < 32; ++q)
+              if (q < qn) orow[q * so] = v[q];
           }
         }
         if (e.gn_part) {
@@ -551,7 +580,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             // the warp's lattice row (32 pixels x these 32 channels) through a
             // 128-byte-swizzled staging buffer and one TMA store: whole lines
             // per request instead of 16-byte pieces of 32 pixels' lines
-            uint8_t* ob = smem + S * Cfg::kStage + (warp * 2 + (ost & 1)) * 4096;
+            uint8_t* ob = smem + kOutOff + (warp * 2 + (ost & 1)) * 4096;
             if (ost >= 2) {
               if (lane == 0) bulk_wait_group_read<1>();
               __syncwarp();
@@ -1078,10 +1107,10 @@ static yl_status launch_plan(yl_ctx* ctx, const View* views, int nviews, const f
     YL_TRY(make_view_tmap(&ta[i], views[i < nviews ? i : 0], 32,
                           HALO ? HaloCfg::kBoxRows : 4 * MT, CU_TENSOR_MAP_SWIZZLE_128B));
   YL_TRY(make_weight_tmap(&tw, w, w_rows, w_cols, BN));
-  // output of each phase as a strided view of the lattice (the non-transposed
-  // epilogue stores whole lattice rows through these)
+  // output of each phase as a strided view of the lattice (the epilogue stores
+  // 32-pixel x 32-channel pieces of lattice rows through these)
   CUtensorMap to[4];
-  p.tma_out = !TR && (e.ldo & 3) == 0 && ((uintptr_t)e.out & 15) == 0;
+  p.tma_out = (e.ldo & 3) == 0 && ((uintptr_t)e.out & 15) == 0;
   for (int z = 0; z < 4; ++z) {
     const TapPhase& ph = p.ph[z < nphase ? z : 0];
     View ov{e.out + ((long long)ph.ya * p.out_w + ph.xa) * e.ldo, e.n_total,
