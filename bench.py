@@ -45,6 +45,8 @@ METRIC = "train frame-pairs/s @854x480 at 1/2/4/8 B200; conv TFLOP/s vs tensor p
 VAE_FWD_PER_FRAME = 2.5980e12
 ENC_FWD_PER_FRAME = 1.1100e12
 MOTION_TRAIN_PER_SAMPLE = 0.1433e12
+WORKLOAD = ("joint VAE + motion-net train step at 854x480: VAE fwd+bwd on frame k, encoder fwd "
+            "on frames 0/16, U-Net fwd+bwd, all-reduce, Adam")
 
 
 def parse():
@@ -155,14 +157,18 @@ def run_reference(args):
     rank, world, _ = dist_env()
     if rank != 0:
         return
-    steps, warmup = max(1, min(args.steps, 5)), min(args.warmup, 1)
+    # each sample step takes about 2 s on the host cores: at most 5 timed and
+    # 3 warm-up steps keep the run within a minute
+    steps, warmup = max(1, min(args.steps, 5)), max(0, min(args.warmup, 3))
     cb = cpu_sample(steps, warmup)
     line = {"metric": METRIC, "value": cb["value"], "unit": "frame-pairs/s", "impl": "reference",
             "n_gpus": args.gpus, "steps": steps, "warmup": warmup,
             "ms_per_step": 1000 * cb["seconds_per_sample_step"], "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": "joint VAE + motion-net train step at 854x480, CPU oracle "
-                                   "sample", "parallelism": "host threads"},
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded 17-frame clips: blobs + gratings + 4 moving sprites)",
+            "config": {"workload": WORKLOAD, "frame": "480x856 (854 padded to 856)",
+                       "per_gpu_batch": 8, "global_batch": 8,
+                       "parallelism": "host threads on rank 0 (the oracle's CPU path)"},
             "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
             "e2e": {"value": cb["value"], "unit": "frame-pairs/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
@@ -308,9 +314,7 @@ def run_native(args):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "tf32",
             "data": "synthetic (seeded 17-frame clips: blobs + gratings + 4 moving sprites)",
-            "config": {"workload": "joint VAE + motion-net train step at 854x480: VAE fwd+bwd "
-                                   "on frame k, encoder fwd on frames 0/16, U-Net fwd+bwd, "
-                                   "all-reduce, Adam",
+            "config": {"workload": WORKLOAD,
                        "frame": f"{H}x{W} (854 padded to 856)", "per_gpu_batch": B,
                        "global_batch": B * world, "parallelism": f"dp{world}",
                        "l2": (f"working set {act_gb:.0f} GB per GPU >> 126 MB L2; "
