@@ -199,13 +199,17 @@ __global__ void __launch_bounds__(256, 4)
     const float* xb = x + (long long)img * q.hw * q.ps + c;
     float* yb = y + (long long)img * q.hw * ldy + c;
     long long p = p0 + row;
-    for (; p + R < p1; p += 2 * R) {
-      const float4 a = __ldg(reinterpret_cast<const float4*>(xb + p * q.ps));
-      const float4 b = __ldg(reinterpret_cast<const float4*>(xb + (p + R) * q.ps));
-      *reinterpret_cast<float4*>(yb + p * ldy) = gn_act4(a, sc, sf, silu, round);
-      *reinterpret_cast<float4*>(yb + (p + R) * ldy) = gn_act4(b, sc, sf, silu, round);
+    // four pixels per iteration: four 16-byte loads in flight per thread
+    for (; p + 3 * R < p1; p += 4 * R) {
+      float4 a[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        a[u] = __ldg(reinterpret_cast<const float4*>(xb + (p + u * R) * q.ps));
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        *reinterpret_cast<float4*>(yb + (p + u * R) * ldy) = gn_act4(a[u], sc, sf, silu, round);
     }
-    if (p < p1) {
+    for (; p < p1; p += R) {
       const float4 a = __ldg(reinterpret_cast<const float4*>(xb + p * q.ps));
       *reinterpret_cast<float4*>(yb + p * ldy) = gn_act4(a, sc, sf, silu, round);
     }
