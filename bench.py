@@ -45,6 +45,10 @@ METRIC = "train frame-pairs/s @854x480 at 1/2/4/8 B200; conv TFLOP/s vs tensor p
 VAE_FWD_PER_FRAME = 2.5980e12
 ENC_FWD_PER_FRAME = 1.1100e12
 MOTION_TRAIN_PER_SAMPLE = 0.1433e12
+# DRAM bytes (read + write) of one conv_tma_fprop_kernel<128, 2, 1, 1> launch
+# per image of 480x856 (3x3, 128 -> 128): ncu capture of a 2-image launch,
+# 423.0 MB read + 370.3 MB written.
+DOM_TRAFFIC_PER_IMAGE = (423.0e6 + 370.3e6) / 2
 WORKLOAD = ("joint VAE + motion-net train step at 854x480: VAE fwd+bwd on frame k, encoder fwd "
             "on frames 0/16, U-Net fwd+bwd, all-reduce, Adam")
 
@@ -283,20 +287,40 @@ def run_native(args):
             ent["gbs"] = v["bytes"] / (v["ms"] * 1e-3) / 1e9
             ent["frac_hbm"] = ent["gbs"] / hbm
         kernels[k] = ent
-    top = max(stats, key=lambda k: stats[k]["ms"])
+    classes = ("conv_fprop", "conv_dgrad", "conv_wgrad", "gn_silu_fwd", "gn_silu_bwd")
+    top = max(classes, key=lambda k: stats[k]["ms"])
     conv_flops = sum(stats[k]["flops"] for k in ("conv_fprop", "conv_dgrad", "conv_wgrad"))
     conv_ms = sum(stats[k]["ms"] for k in ("conv_fprop", "conv_dgrad", "conv_wgrad"))
-    achieved = stats[top]["flops"] / (stats[top]["ms"] * 1e-3) / 1e12
-    roofline = {"bound": "tensor", "kernel": top, "achieved": achieved, "peak": tf32_peak,
-                "unit": "TFLOP/s", "frac": achieved / tf32_peak, "traffic": None,
+    dom = stats.get("conv_3x3_128_frame", {"ms": 0.0})
+    if dom["ms"] > 0 and dom["launches"] > 0:
+        # the dominant launch type: one stride-1 3x3 128->128 pass over the batch
+        # at the frame resolution (forward or dX, the same kernel)
+        achieved = dom["flops"] / (dom["ms"] * 1e-3) / 1e12
+        per_launch_flops = dom["flops"] / dom["launches"]
+        per_launch_bytes = 2.0 * B * H * W * 128 * 4 + 128 * 128 * 9 * 4
+        kernel = (f"conv_tma_fprop_kernel<128, 2, 1, 1> (3x3 128->128, {B}x{H}x{W}, "
+                  "forward and dX passes)")
+        traffic = DOM_TRAFFIC_PER_IMAGE * B if (H, W) == (480, 856) else None
+    else:
+        achieved = stats[top]["flops"] / (stats[top]["ms"] * 1e-3) / 1e12
+        per_launch_flops = per_launch_bytes = None
+        kernel, traffic = top, None
+    roofline = {"bound": "tensor", "kernel": kernel, "achieved": achieved, "peak": tf32_peak,
+                "unit": "TFLOP/s", "frac": achieved / tf32_peak, "traffic": traffic,
+                "flops_per_launch": per_launch_flops,
+                "algorithmic_bytes_per_launch": per_launch_bytes,
                 "peak_note": (f"tf32 peak = 1/2 of the {peak_src} dense bf16 "
                               f"{bf16:.1f} TFLOP/s (no tf32 peak is measured)"),
-                "flops_note": ("achieved counts 2*N*Cout*Cin*k*k*OH*OW per conv pass; "
-                               "upsample convs execute 16/36 of that through merged "
-                               "phase taps"),
-                "traffic_note": ("per-launch DRAM bytes of the dominant launch type are in "
-                                 "profiles/conv_tma_fprop_128ch_2x480x856.md (equal to the "
-                                 "algorithmic bytes); the class mixes layer shapes"),
+                "flops_note": ("achieved = 2*N*Cout*Cin*9*OH*OW per launch over the summed "
+                               "CUDA-event time of those launches in the timed steps"),
+                "traffic_note": ("DRAM read + write bytes per launch from an ncu capture of "
+                                 "the same kernel on 2 images (profiles/"
+                                 "conv_tma_fprop_128ch_2x480x856.md), scaled to the batch; "
+                                 "below the algorithmic bytes because part of the output is "
+                                 "still in L2 when the kernel ends"),
+                "conv_fprop_class": {"achieved": stats["conv_fprop"]["flops"] /
+                                     (stats["conv_fprop"]["ms"] * 1e-3) / 1e12 if
+                                     stats["conv_fprop"]["ms"] > 0 else None},
                 "all_convs": {"achieved": conv_flops / (conv_ms * 1e-3) / 1e12,
                               "frac": conv_flops / (conv_ms * 1e-3) / 1e12 / tf32_peak}}
     act_gb = tr.activation_bytes() / 1e9

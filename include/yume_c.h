@@ -404,7 +404,10 @@ yl_status yl_trainer_param_entry(yl_trainer* tr, int which, int index, char* nam
                                  size_t name_len, size_t* offset, int* shape4);
 /* Re-derive the tf32 weight copies after parameters were written externally. */
 yl_status yl_trainer_prepare_weights(yl_trainer* tr);
-#define YL_KERNEL_CLASSES 5 /* conv fprop, conv dgrad, conv wgrad, GN+SiLU fwd, GN+SiLU bwd */
+/* conv fprop, conv dgrad, conv wgrad, GN+SiLU fwd, GN+SiLU bwd, and (also counted
+ * in classes 0/1) the forward and dX passes of the stride-1 3x3 128->128 convs at
+ * the frame resolution: the step's dominant launch type */
+#define YL_KERNEL_CLASSES 6
 typedef struct yl_kernel_stats {
   double ms[YL_KERNEL_CLASSES];
   double flops[YL_KERNEL_CLASSES];

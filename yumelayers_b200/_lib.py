@@ -48,10 +48,14 @@ class TrainerConfig(C.Structure):
                 ("train_motion", C.c_int), ("bucket_bytes", C.c_size_t), ("profile", C.c_int)]
 
 
+KERNEL_CLASSES = 6
+
+
 class KernelStats(C.Structure):
-    """``yl_kernel_stats``: conv fprop, conv dgrad, conv wgrad, GN fwd, GN bwd."""
-    _fields_ = [("ms", C.c_double * 5), ("flops", C.c_double * 5), ("bytes", C.c_double * 5),
-                ("launches", C.c_int * 5)]
+    """``yl_kernel_stats``: conv fprop, conv dgrad, conv wgrad, GN fwd, GN bwd, and the
+    dominant launch type (3x3 128->128 fprop/dX at the frame resolution, also in 0/1)."""
+    _fields_ = [("ms", C.c_double * KERNEL_CLASSES), ("flops", C.c_double * KERNEL_CLASSES),
+                ("bytes", C.c_double * KERNEL_CLASSES), ("launches", C.c_int * KERNEL_CLASSES)]
 
 
 P = C.c_void_p

@@ -84,6 +84,7 @@ struct ConvL {
   yl_status backward(Net& net, const Act& x, const Act& dy, const Act* dx,
                      const float* dx_addend = nullptr, int ld_addend = 0,
                      float* dbias2d = nullptr, int up = 0, int hv = 0, int wv = 0);
+  bool dominant(const struct Net& net, int h, int w, int up) const;
 };
 
 struct GNL {
@@ -132,8 +133,11 @@ struct RB {
 };
 
 // Kernel-class timing used by the bench (classes: 0 conv fprop, 1 conv
-// dgrad, 2 conv wgrad, 3 GN+SiLU forward, 4 GN+SiLU backward).
-constexpr int kProfClasses = 5;
+// dgrad, 2 conv wgrad, 3 GN+SiLU forward, 4 GN+SiLU backward; 5 counts again
+// the fprop and dX launches of stride-1 3x3 128->128 convs at dom_pixels
+// pixels per image, the step's dominant launch type).
+constexpr int kProfClasses = 6;
+constexpr int kProfDominant = 5;
 
 struct Net {
   yl_ctx* ctx = nullptr;
@@ -146,9 +150,10 @@ struct Net {
   void (*hook)(void* arg, Net* net, size_t lo) = nullptr;
   void* hook_arg = nullptr;
   bool profiling = false;
+  long long dom_pixels = 0;  // output pixels per image of the dominant launch type
   struct ProfEvent {
     cudaEvent_t a, b;
-    int cls;
+    int cls, cls2 = -1;  // cls2: a second class the launch also counts in
     double flops, bytes;
   };
   std::vector<ProfEvent> pending, done;
@@ -160,6 +165,8 @@ struct Net {
   virtual ~Net();
   void prof_begin(int cls);
   void prof_end(int cls, double flops, double bytes = 0.0);
+  // the open event also counts in class 5 (call between prof_begin and prof_end)
+  void prof_mark_dominant();
   yl_status prof_collect(double* ms, double* flops, double* bytes, int* launches);
   void grads_ready(size_t lo);
   yl_status prepare_weights();

@@ -186,6 +186,7 @@ yl_status yl_trainer_create(yl_ctx* ctx, const yl_trainer_config* cfg, yl_comm* 
   tr->vae = std::make_unique<VAE>();
   tr->vae->ctx = ctx;
   YL_TRY(tr->vae->build(ctx, B, cfg->height, cfg->width, cfg->seed));
+  tr->vae->dom_pixels = (long long)cfg->height * cfg->width;
   tr->unet = std::make_unique<UNet>();
   tr->unet->ctx = ctx;
   YL_TRY(tr->unet->build(ctx, B, tr->vae->hl, tr->vae->wl, cfg->seed));

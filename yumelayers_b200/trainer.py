@@ -16,7 +16,8 @@ from ._lib import KernelStats, TrainerConfig, YumeError, call, lib
 from .session import Context
 
 
-CLASS_NAMES = ["conv_fprop", "conv_dgrad", "conv_wgrad", "gn_silu_fwd", "gn_silu_bwd"]
+CLASS_NAMES = ["conv_fprop", "conv_dgrad", "conv_wgrad", "gn_silu_fwd", "gn_silu_bwd",
+               "conv_3x3_128_frame"]
 
 
 def _bind() -> C.CDLL:
@@ -204,7 +205,7 @@ class Trainer:
         st = KernelStats()
         call("yl_trainer_kernel_stats", self.handle, C.byref(st), int(reset))
         return {CLASS_NAMES[i]: {"ms": st.ms[i], "flops": st.flops[i], "bytes": st.bytes[i],
-                                 "launches": st.launches[i]} for i in range(5)}
+                                 "launches": st.launches[i]} for i in range(len(CLASS_NAMES))}
 
     def activation_bytes(self) -> int:
         b = C.c_size_t()
