@@ -45,6 +45,7 @@ CASES = [
     ("c256_to_128", 1, 256, 128, 30, 54, 3, 1, 1, False, None),
     ("c128_tall_ragged", 1, 128, 128, 67, 40, 3, 1, 1, False, None),
     ("c128_h60_wide", 2, 128, 128, 60, 300, 3, 1, 1, False, None),
+    ("c96_128", 2, 96, 128, 20, 36, 3, 1, 1, False, None),
 ]
 
 

@@ -1404,6 +1404,7 @@ static WgTile wgrad_tile(int cout, int n_total) {
   if (n_total % 384 == 0) return {1, 2, 192, 32};
   if (n_total % 256 == 0) return {1, 1, 256, 32};
   if (n_total % 128 == 0) return {1, 1, 128, 32};
+  if (n_total % 288 == 0) return {1, 3, 96, 16};  // e.g. 3x3 over 96 channels
   return {0, 0, 0, 0};
 }
 

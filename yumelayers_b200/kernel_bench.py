@@ -31,6 +31,7 @@ VAE_SHAPES = [
 # the motion U-Net's 3x3 convs on batch-8 latents of 60x107 (and its two
 # down-sampled levels)
 UNET_SHAPES = [
+    ("u60_96_128", 8, 96, 60, 107, 128, 3, 1, 0),
     ("u60_128_128", 8, 128, 60, 107, 128, 3, 1, 0),
     ("u30_256_256", 8, 256, 30, 54, 256, 3, 1, 0),
     ("u15_384_384", 8, 384, 15, 27, 384, 3, 1, 0),
