@@ -132,5 +132,8 @@ yl_status rgb_tap_sum(yl_ctx* ctx, const float* z, int n, int h, int w, const fl
 // uh x uw, cropped) -- the adjoint of nearest upsampling into (h, w).
 yl_status downsample_sum_nhwc(yl_ctx* ctx, const float* src, int uh, int uw, float* dst, int n,
                               int h, int w, int c, int ps_src, int ps_dst);
+// dst (uh x uw, uh <= 2h, uw <= 2w) = the nearest x2 upsample of src (h x w).
+yl_status upsample_nearest_nhwc(yl_ctx* ctx, const float* src, int n, int h, int w, int c,
+                                int ps_src, float* dst, int uh, int uw, int ps_dst);
 
 }  // namespace yl
