@@ -47,8 +47,8 @@ ENC_FWD_PER_FRAME = 1.1100e12
 MOTION_TRAIN_PER_SAMPLE = 0.1433e12
 # DRAM bytes (read + write) of one conv_tma_fprop_kernel<128, 2, 1, 1> launch
 # per image of 480x856 (3x3, 128 -> 128): ncu capture of a 2-image launch,
-# 423.0 MB read + 370.3 MB written.
-DOM_TRAFFIC_PER_IMAGE = (423.0e6 + 370.3e6) / 2
+# 421.7 MB read + 376.1 MB written.
+DOM_TRAFFIC_PER_IMAGE = (421.7e6 + 376.1e6) / 2
 WORKLOAD = ("joint VAE + motion-net train step at 854x480: VAE fwd+bwd on frame k, encoder fwd "
             "on frames 0/16, U-Net fwd+bwd, all-reduce, Adam")
 
