@@ -46,6 +46,9 @@ CASES = [
     ("c128_tall_ragged", 1, 128, 128, 67, 40, 3, 1, 1, False, None),
     ("c128_h60_wide", 2, 128, 128, 60, 300, 3, 1, 1, False, None),
     ("c96_128", 2, 96, 128, 20, 36, 3, 1, 1, False, None),
+    # one-row inputs: phase plans whose second row phase has no output pixels
+    ("s2_h1", 1, 32, 32, 1, 9, 3, 2, 1, False, None),
+    ("up_crop_h1", 1, 32, 32, 1, 5, 3, 1, 1, True, (1, 9)),
 ]
 
 

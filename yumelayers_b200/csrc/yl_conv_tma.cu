@@ -1110,17 +1110,22 @@ static yl_status launch_plan(yl_ctx* ctx, const View* views, int nviews, const f
   // output of each phase as a strided view of the lattice (the epilogue stores
   // 32-pixel x 32-channel pieces of lattice rows through these)
   CUtensorMap to[4];
+  // (an output the maps cannot describe -- unaligned, or a phase with no
+  // pixels -- keeps the per-thread stores)
   p.tma_out = (e.ldo & 3) == 0 && ((uintptr_t)e.out & 15) == 0;
-  for (int z = 0; z < 4; ++z) {
+  for (int z = 0; z < 4 && p.tma_out; ++z) {
     const TapPhase& ph = p.ph[z < nphase ? z : 0];
     View ov{e.out + ((long long)ph.ya * p.out_w + ph.xa) * e.ldo, e.n_total,
             std::min(p.gw, (p.out_w - ph.xa + p.xs - 1) / p.xs),
             std::min(p.gh, (p.out_h - ph.ya + p.ys - 1) / p.ys), p.n_img,
             (long long)p.xs * e.ldo, (long long)p.ys * p.out_w * e.ldo,
             (long long)p.out_h * p.out_w * e.ldo};
-    if (p.tma_out) YL_TRY(make_view_tmap(&to[z], ov, 32, 1, CU_TENSOR_MAP_SWIZZLE_128B));
-    else to[z] = tw;  // unused
+    if (ov.w < 1 || ov.h < 1 ||
+        make_view_tmap(&to[z], ov, 32, 1, CU_TENSOR_MAP_SWIZZLE_128B) != YL_OK)
+      p.tma_out = 0;
   }
+  if (!p.tma_out)
+    for (int z = 0; z < 4; ++z) to[z] = tw;  // unused by the per-thread stores
   p.tiles_x = (p.gw + 31) / 32;
   p.tiles_y = (p.gh + 4 * MT - 1) / (4 * MT);
   p.n_nblk = (e.n_total + BN - 1) / BN;
