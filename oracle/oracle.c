@@ -70,51 +70,218 @@ ORC_API void orc_matmul(const float* A, const float* B, float* C, int M, int N,
   }
 }
 
-/* Cache-blocked fp32 GEMM used by the conv composition below, so the timed
- * CPU baseline is a fair one: C[M,N] (+)= A[M,K] * B[K,N], row-major.  The
- * (M-block x N-block) tiles are spread over OpenMP threads; a KB x NB panel
- * of B stays in L2 while the rows of the tile stream through it.  It is the
- * same sum as orc_matmul (different association order). */
-enum { GEMM_MB = 32, GEMM_NB = 512, GEMM_KB = 128 };
-static void gemm_nn(const float* A, const float* B, float* C, int M, int N, int K,
-                    int accumulate) {
-  const int mt = (M + GEMM_MB - 1) / GEMM_MB, nt = (N + GEMM_NB - 1) / GEMM_NB;
-#pragma omp parallel for schedule(dynamic, 1) collapse(2)
-  for (int bm = 0; bm < mt; ++bm)
-    for (int bn = 0; bn < nt; ++bn) {
-      const int m0 = bm * GEMM_MB, m1 = m0 + GEMM_MB < M ? m0 + GEMM_MB : M;
-      const int n0 = bn * GEMM_NB, n1 = n0 + GEMM_NB < N ? n0 + GEMM_NB : N;
-      const int nw = n1 - n0;
-      if (!accumulate)
-        for (int r = m0; r < m1; ++r) memset(C + (size_t)r * N + n0, 0, sizeof(float) * nw);
-      for (int k0 = 0; k0 < K; k0 += GEMM_KB) {
-        const int k1 = k0 + GEMM_KB < K ? k0 + GEMM_KB : K;
-        for (int r = m0; r < m1; ++r) {
-          float* crow = C + (size_t)r * N + n0;
-          const float* arow = A + (size_t)r * K;
-          for (int k = k0; k < k1; ++k) {
-            const float a = arow[k];
-            if (a == 0.0f) continue;
-            const float* brow = B + (size_t)k * N + n0;
-#pragma omp simd
-            for (int c = 0; c < nw; ++c) crow[c] += a * brow[c];
+/* Packed implicit-GEMM fp32 convolution core used by the conv composition
+ * (orc_conv2d_fwd / orc_conv2d_bwd below), so that full-resolution layers
+ * (480 x 856) check in seconds and the timed CPU baseline is a fair one.
+ * It forms the same sums as im2col + matmul (forward), gradW (dW) and
+ * col2im / convBackInputS1 (dX); only the association order differs.  The
+ * per-index restatements above and below (orc_im2col, orc_matmul,
+ * orc_col2im, orc_conv_back_input_s1, orc_gradw) stay the reference's kernels
+ * one to one and pin this core in the tests.
+ *
+ * A tile is NB output pixels of one image: its im2col columns are gathered
+ * into a K x NB panel T (K = channels * taps), then a 6 x 16 register-blocked
+ * micro-kernel (twelve 8-wide fp32 accumulators, AVX2 FMA through GCC vector
+ * extensions) multiplies the weight rows into it. */
+typedef float v8f __attribute__((vector_size(32)));
+enum { TILE_NB = 64, MK_M = 6, MK_N = 16 };
+
+static inline v8f ld8(const float* p) { v8f v; memcpy(&v, p, sizeof v); return v; }
+static inline void st8(float* p, v8f v) { memcpy(p, &v, sizeof v); }
+
+/* acc[r][0..15] = sum_{i < len} A[r * lda + i] * B[i * ldb + 0..15] for r < mr
+ * (rows >= mr read row 0 and are discarded by the caller). */
+static inline void mk6x16(const float* A, long lda, int mr, const float* B, long ldb, int len,
+                          float acc[MK_M][MK_N]) {
+  const float* a[MK_M];
+  for (int r = 0; r < MK_M; ++r) a[r] = A + (r < mr ? r : 0) * lda;
+  v8f c00 = {0}, c01 = {0}, c10 = {0}, c11 = {0}, c20 = {0}, c21 = {0};
+  v8f c30 = {0}, c31 = {0}, c40 = {0}, c41 = {0}, c50 = {0}, c51 = {0};
+  for (int i = 0; i < len; ++i) {
+    const v8f b0 = ld8(B + (long)i * ldb), b1 = ld8(B + (long)i * ldb + 8);
+    v8f x;
+    x = (v8f){0} + a[0][i]; c00 += x * b0; c01 += x * b1;
+    x = (v8f){0} + a[1][i]; c10 += x * b0; c11 += x * b1;
+    x = (v8f){0} + a[2][i]; c20 += x * b0; c21 += x * b1;
+    x = (v8f){0} + a[3][i]; c30 += x * b0; c31 += x * b1;
+    x = (v8f){0} + a[4][i]; c40 += x * b0; c41 += x * b1;
+    x = (v8f){0} + a[5][i]; c50 += x * b0; c51 += x * b1;
+  }
+  st8(acc[0], c00); st8(acc[0] + 8, c01); st8(acc[1], c10); st8(acc[1] + 8, c11);
+  st8(acc[2], c20); st8(acc[2] + 8, c21); st8(acc[3], c30); st8(acc[3] + 8, c31);
+  st8(acc[4], c40); st8(acc[4] + 8, c41); st8(acc[5], c50); st8(acc[5] + 8, c51);
+}
+
+/* Y[m * ldy + p] = sum_k A[m * lda + k] * T[k * ldt + p] for m < M, p < np;
+ * T holds whole 16-column groups (ldt >= np rounded up to 16, padding zero). */
+static void gemm_a_t(const float* A, int M, long lda, const float* T, int K, long ldt, int np,
+                     float* Y, long ldy) {
+  float acc[MK_M][MK_N];
+  for (int m0 = 0; m0 < M; m0 += MK_M) {
+    const int mr = M - m0 < MK_M ? M - m0 : MK_M;
+    for (int p0 = 0; p0 < np; p0 += MK_N) {
+      const int pr = np - p0 < MK_N ? np - p0 : MK_N;
+      mk6x16(A + (long)m0 * lda, lda, mr, T + p0, ldt, K, acc);
+      for (int r = 0; r < mr; ++r) memcpy(Y + (long)(m0 + r) * ldy + p0, acc[r], sizeof(float) * pr);
+    }
+  }
+}
+
+/* Geometry of one conv as the core sees it.  Forward / dW: output pixel
+ * (oy, ox) of oh x ow reads tap (ky, kx) at (oy*s - pad + ky, ox*s - pad + kx)
+ * of the ih x iw input, which with `up` is the nearest-x2 view of the stored
+ * h x w tensor.  Transposed (dX): output pixel (iy, ix) of ih x iw gathers
+ * dy[(iy + pad - ky) / s][(ix + pad - kx) / s] when the division is exact. */
+typedef struct {
+  int C, h, w, ih, iw, k, s, pad, up, oh, ow;
+} ConvGeom;
+
+/* im2col columns of pixels [p0, p0 + np) (forward pixel order): T[c*k*k + t][j]. */
+static void pack_fwd(const float* x, const ConvGeom* g, long p0, int np, float* T, int ldt) {
+  const int kk = g->k * g->k;
+  for (int c = 0; c < g->C; ++c) {
+    const float* xc = x + (size_t)c * g->h * g->w;
+    for (int t = 0; t < kk; ++t) {
+      const int ky = t / g->k, kx = t % g->k;
+      float* row = T + (size_t)(c * kk + t) * ldt;
+      int oy = (int)(p0 / g->ow), ox = (int)(p0 % g->ow);
+      for (int j = 0; j < np; ++j) {
+        const int iy = oy * g->s - g->pad + ky, ix = ox * g->s - g->pad + kx;
+        float v = 0.0f;
+        if (iy >= 0 && iy < g->ih && ix >= 0 && ix < g->iw)
+          v = g->up ? xc[(size_t)(iy >> 1) * g->w + (ix >> 1)] : xc[(size_t)iy * g->w + ix];
+        row[j] = v;
+        if (++ox == g->ow) { ox = 0; ++oy; }
+      }
+      for (int j = np; j < ldt; ++j) row[j] = 0.0f;
+    }
+  }
+}
+
+/* Transposed columns of input-space pixels [p0, p0 + np) of ih x iw:
+ * T[o*k*k + t][j] = dy[o][oy][ox] (the col2im gather, MetalKernelSourcesB.swift:28-58). */
+static void pack_tr(const float* dy, int OC, const ConvGeom* g, long p0, int np, float* T,
+                    int ldt) {
+  const int kk = g->k * g->k;
+  for (int o = 0; o < OC; ++o) {
+    const float* dyo = dy + (size_t)o * g->oh * g->ow;
+    for (int t = 0; t < kk; ++t) {
+      const int ky = t / g->k, kx = t % g->k;
+      float* row = T + (size_t)(o * kk + t) * ldt;
+      int y = (int)(p0 / g->iw), x = (int)(p0 % g->iw);
+      for (int j = 0; j < np; ++j) {
+        const int sy = y + g->pad - ky, sx = x + g->pad - kx;
+        float v = 0.0f;
+        if (sy >= 0 && sx >= 0 && sy % g->s == 0 && sx % g->s == 0) {
+          const int oy = sy / g->s, ox = sx / g->s;
+          if (oy < g->oh && ox < g->ow) v = dyo[(size_t)oy * g->ow + ox];
+        }
+        row[j] = v;
+        if (++x == g->iw) { x = 0; ++y; }
+      }
+      for (int j = np; j < ldt; ++j) row[j] = 0.0f;
+    }
+  }
+}
+
+/* y (N, OC, oh, ow) = W (OC, C*k*k) * im2col(x) per image. */
+static void conv_core_fwd(const float* x, int N, const ConvGeom* g, const float* w, int OC,
+                          float* y) {
+  const int K = g->C * g->k * g->k;
+  const long P = (long)g->oh * g->ow, tiles = (P + TILE_NB - 1) / TILE_NB;
+#pragma omp parallel
+  {
+    float* T = (float*)malloc(sizeof(float) * (size_t)K * TILE_NB);
+#pragma omp for schedule(dynamic, 4)
+    for (long it = 0; it < (long)N * tiles; ++it) {
+      const int n = (int)(it / tiles);
+      const long p0 = (it % tiles) * TILE_NB;
+      const int np = (int)(P - p0 < TILE_NB ? P - p0 : TILE_NB);
+      pack_fwd(x + (size_t)n * g->C * g->h * g->w, g, p0, np, T, TILE_NB);
+      gemm_a_t(w, OC, K, T, K, TILE_NB, np, y + (size_t)n * OC * P + p0, P);
+    }
+    free(T);
+  }
+}
+
+/* dx (N, C, ih, iw) = col2im(W^T dy) per image: Wt[c][o*k*k + t] = W[o][c*k*k + t]. */
+static void conv_core_dgrad(const float* dy, int N, const ConvGeom* g, const float* w, int OC,
+                            float* dx) {
+  const int kk = g->k * g->k, K = OC * kk;
+  float* wt = (float*)malloc(sizeof(float) * (size_t)g->C * K);
+  for (int o = 0; o < OC; ++o)
+    for (int c = 0; c < g->C; ++c)
+      for (int t = 0; t < kk; ++t)
+        wt[(size_t)c * K + o * kk + t] = w[(size_t)o * g->C * kk + c * kk + t];
+  const long P = (long)g->ih * g->iw, tiles = (P + TILE_NB - 1) / TILE_NB;
+#pragma omp parallel
+  {
+    float* T = (float*)malloc(sizeof(float) * (size_t)K * TILE_NB);
+#pragma omp for schedule(dynamic, 4)
+    for (long it = 0; it < (long)N * tiles; ++it) {
+      const int n = (int)(it / tiles);
+      const long p0 = (it % tiles) * TILE_NB;
+      const int np = (int)(P - p0 < TILE_NB ? P - p0 : TILE_NB);
+      pack_tr(dy + (size_t)n * OC * g->oh * g->ow, OC, g, p0, np, T, TILE_NB);
+      gemm_a_t(wt, g->C, K, T, K, TILE_NB, np, dx + (size_t)n * g->C * P + p0, P);
+    }
+    free(T);
+  }
+  free(wt);
+}
+
+/* dw (OC, C*k*k) = sum over images and pixels of dy x im2col(x) (gradW,
+ * MetalKernelSourcesA.swift:122-137, summed over the batch).  Each thread
+ * sums its pixel tiles into a private [K][OC] buffer; the buffers are added
+ * in thread order, so a fixed thread count gives a fixed result. */
+static void conv_core_wgrad(const float* x, const float* dy, int N, const ConvGeom* g, int OC,
+                            float* dw) {
+  const int K = g->C * g->k * g->k;
+  const int ocp = (OC + MK_N - 1) / MK_N * MK_N;
+  const long P = (long)g->oh * g->ow, tiles = (P + TILE_NB - 1) / TILE_NB;
+  const int nth = orc_num_threads();
+  float* priv = (float*)calloc((size_t)nth * K * ocp, sizeof(float));
+#pragma omp parallel num_threads(nth)
+  {
+    int tid = 0;
+#ifdef _OPENMP
+    tid = omp_get_thread_num();
+#endif
+    float* mine = priv + (size_t)tid * K * ocp;
+    float* T = (float*)malloc(sizeof(float) * (size_t)K * TILE_NB);
+    float* dyt = (float*)malloc(sizeof(float) * (size_t)TILE_NB * ocp);
+    float acc[MK_M][MK_N];
+#pragma omp for schedule(static)
+    for (long it = 0; it < (long)N * tiles; ++it) {
+      const int n = (int)(it / tiles);
+      const long p0 = (it % tiles) * TILE_NB;
+      const int np = (int)(P - p0 < TILE_NB ? P - p0 : TILE_NB);
+      pack_fwd(x + (size_t)n * g->C * g->h * g->w, g, p0, np, T, TILE_NB);
+      const float* dyn = dy + (size_t)n * OC * P + p0;
+      for (int j = 0; j < np; ++j)
+        for (int o = 0; o < ocp; ++o) dyt[(size_t)j * ocp + o] = o < OC ? dyn[(size_t)o * P + j] : 0.0f;
+      for (int k0 = 0; k0 < K; k0 += MK_M) {
+        const int mr = K - k0 < MK_M ? K - k0 : MK_M;
+        for (int o0 = 0; o0 < ocp; o0 += MK_N) {
+          mk6x16(T + (size_t)k0 * TILE_NB, TILE_NB, mr, dyt + o0, ocp, np, acc);
+          for (int r = 0; r < mr; ++r) {
+            float* d = mine + (size_t)(k0 + r) * ocp + o0;
+            for (int q = 0; q < MK_N; ++q) d[q] += acc[r][q];
           }
         }
       }
     }
-}
-
-/* C[M,N] (+)= A[M,K] * B[N,K]^T (both K-contiguous) -- the gradW shape:
- * B is transposed once into a K x N panel and the blocked gemm_nn runs. */
-static void gemm_nt(const float* A, const float* B, float* C, int M, int N, int K,
-                    int accumulate) {
-  float* bt = (float*)malloc(sizeof(float) * (size_t)K * N);
+    free(T);
+    free(dyt);
+  }
 #pragma omp parallel for schedule(static)
-  for (int k0 = 0; k0 < K; k0 += 64)
-    for (int j = 0; j < N; ++j)
-      for (int k = k0; k < k0 + 64 && k < K; ++k) bt[(size_t)k * N + j] = B[(size_t)j * K + k];
-  gemm_nn(A, bt, C, M, N, K, accumulate);
-  free(bt);
+  for (int o = 0; o < OC; ++o)
+    for (int kx = 0; kx < K; ++kx) {
+      float s = 0.0f;
+      for (int t = 0; t < nth; ++t) s += priv[((size_t)t * K + kx) * ocp + o];
+      dw[(size_t)o * K + kx] += s;
+    }
+  free(priv);
 }
 
 /* im2col3d_kernel (MetalKernelSourcesA.swift:325-352): X (ic, ih, iw) ->
@@ -528,79 +695,59 @@ ORC_API void orc_timestep_embedding_torch(const float* t, int n, int dim, float 
  * y = W * cols + b (biasRow).  Optional nearest-x2 upsample of the input
  * (the decoder's "up + conv", ConvGPU.swift:393 / Ops:336), cropped to
  * (ih, iw) when the upsampled size is odd-cropped; optional residual add and
- * per-(image, channel) bias (time-embedding projection). */
+ * per-(image, channel) bias (time-embedding projection).  The im2col + matmul
+ * runs through the packed core above (same sums, tiled). */
 ORC_API void orc_conv2d_fwd(const float* x, int N, int C, int H, int W,
                             const float* w, const float* b, int OC, int k, int stride,
                             int pad, int up, int Hin, int Win, const float* bias2d,
                             const float* residual, float* y) {
   /* up: x has spatial (Hs, Ws) = ceil(Hin/2), ceil(Win/2) and is viewed as the
    * (Hin, Win) nearest upsample; else (H, W) = (Hin, Win). */
-  int ih = up ? Hin : H, iw = up ? Win : W;
-  int oh = (ih + 2 * pad - k) / stride + 1, ow = (iw + 2 * pad - k) / stride + 1;
-  size_t plane_in = (size_t)ih * iw, plane_out = (size_t)oh * ow;
-  float* xin = (float*)malloc(sizeof(float) * C * plane_in);
-  float* cols = (float*)malloc(sizeof(float) * (size_t)C * k * k * plane_out);
-  for (int n = 0; n < N; ++n) {
-    const float* xn = x + (size_t)n * C * H * W;
-    if (up) {
-      for (int c = 0; c < C; ++c)
-        for (int yy = 0; yy < ih; ++yy)
-          for (int xx = 0; xx < iw; ++xx)
-            xin[(size_t)c * plane_in + yy * iw + xx] = xn[((size_t)c * H + yy / 2) * W + xx / 2];
-    } else {
-      memcpy(xin, xn, sizeof(float) * C * plane_in);
-    }
-    orc_im2col(xin, cols, C, ih, iw, k, k, stride, pad);
-    float* yn = y + (size_t)n * OC * plane_out;
-    gemm_nn(w, cols, yn, OC, (int)plane_out, C * k * k, 0);
-#pragma omp parallel for schedule(static)
+  ConvGeom g;
+  g.C = C; g.h = H; g.w = W; g.k = k; g.s = stride; g.pad = pad; g.up = up;
+  g.ih = up ? Hin : H;
+  g.iw = up ? Win : W;
+  g.oh = (g.ih + 2 * pad - k) / stride + 1;
+  g.ow = (g.iw + 2 * pad - k) / stride + 1;
+  const size_t plane_out = (size_t)g.oh * g.ow;
+  conv_core_fwd(x, N, &g, w, OC, y);
+#pragma omp parallel for collapse(2) schedule(static)
+  for (int n = 0; n < N; ++n)
     for (int o = 0; o < OC; ++o) {
       float bb = (b ? b[o] : 0.0f) + (bias2d ? bias2d[(size_t)n * OC + o] : 0.0f);
-      float* row = yn + (size_t)o * plane_out;
+      float* row = y + ((size_t)n * OC + o) * plane_out;
       const float* res = residual ? residual + ((size_t)n * OC + o) * plane_out : NULL;
       for (size_t p = 0; p < plane_out; ++p) row[p] = row[p] + bb + (res ? res[p] : 0.0f);
     }
-  }
-  free(xin);
-  free(cols);
 }
 
 /* ConvLayerGPU.backward (ConvGPU.swift:66-81) summed over the batch the way
  * TrainContext.forwardBackward accumulates per-frame grads
  * (TrainConvVAE.swift:168-219): dW += gradW(dOut, cols), db += biasRowGrad,
- * dx = convBackInputS1 (stride 1) or col2im(W^T dOut) (stride 2).  With `up`,
- * dx is the downsample2x (2x2 sum, Ops:379) of the upsampled-input gradient,
+ * dx = convBackInputS1 (stride 1) or col2im(W^T dOut) (stride 2) -- one
+ * gather formula, MetalKernelSourcesB.swift:28-58 / 125-159.  With `up`, dx
+ * is the downsample2x (2x2 sum, Ops:379) of the upsampled-input gradient,
  * restricted to the cropped size.  Any of dx/dw/db may be NULL.  dw and db
  * are overwritten; dbias2d (N, OC) receives per-image channel sums. */
 ORC_API void orc_conv2d_bwd(const float* x, int N, int C, int H, int W,
                             const float* w, int OC, int k, int stride, int pad, int up,
                             int Hin, int Win, const float* dy, float* dx, float* dw,
                             float* db, float* dbias2d) {
-  int ih = up ? Hin : H, iw = up ? Win : W;
-  int oh = (ih + 2 * pad - k) / stride + 1, ow = (iw + 2 * pad - k) / stride + 1;
-  size_t plane_in = (size_t)ih * iw, plane_out = (size_t)oh * ow;
-  int kk = C * k * k;
-  float* xin = (float*)malloc(sizeof(float) * C * plane_in);
-  float* cols = (float*)malloc(sizeof(float) * (size_t)kk * plane_out);
-  float* dxin = (float*)malloc(sizeof(float) * C * plane_in);
-  if (dw) memset(dw, 0, sizeof(float) * (size_t)OC * kk);
+  ConvGeom g;
+  g.C = C; g.h = H; g.w = W; g.k = k; g.s = stride; g.pad = pad; g.up = up;
+  g.ih = up ? Hin : H;
+  g.iw = up ? Win : W;
+  g.oh = (g.ih + 2 * pad - k) / stride + 1;
+  g.ow = (g.iw + 2 * pad - k) / stride + 1;
+  const size_t plane_in = (size_t)g.ih * g.iw, plane_out = (size_t)g.oh * g.ow;
+  if (dw) {
+    memset(dw, 0, sizeof(float) * (size_t)OC * C * k * k);
+    conv_core_wgrad(x, dy, N, &g, OC, dw);
+  }
   if (db) memset(db, 0, sizeof(float) * OC);
-  for (int n = 0; n < N; ++n) {
-    const float* xn = x + (size_t)n * C * H * W;
-    const float* dyn = dy + (size_t)n * OC * plane_out;
-    if (dw) {
-      if (up) {
-        for (int c = 0; c < C; ++c)
-          for (int yy = 0; yy < ih; ++yy)
-            for (int xx = 0; xx < iw; ++xx)
-              xin[(size_t)c * plane_in + yy * iw + xx] = xn[((size_t)c * H + yy / 2) * W + xx / 2];
-      } else {
-        memcpy(xin, xn, sizeof(float) * C * plane_in);
-      }
-      orc_im2col(xin, cols, C, ih, iw, k, k, stride, pad);
-      gemm_nt(dyn, cols, dw, OC, kk, (int)plane_out, 1);
-    }
-    if (db || dbias2d) {
+  if (db || dbias2d) {
+    for (int n = 0; n < N; ++n) {
+      const float* dyn = dy + (size_t)n * OC * plane_out;
       for (int o = 0; o < OC; ++o) {
         double s = 0;
         for (size_t p = 0; p < plane_out; ++p) s += dyn[(size_t)o * plane_out + p];
@@ -608,33 +755,26 @@ ORC_API void orc_conv2d_bwd(const float* x, int N, int C, int H, int W,
         if (dbias2d) dbias2d[(size_t)n * OC + o] = (float)s;
       }
     }
-    if (dx) {
-      /* dcols = W^T * dOut (matmul transA, ConvGPU.swift:75), then the col2im
-       * gather (col2im3d / col2im3d_s1, MetalKernelSourcesB.swift:28-85); for
-       * stride 1 this equals conv_back_input_s1 (B:125-159), which the
-       * per-op tests check separately. */
-      float* dcols = cols;
-      float* wt = (float*)malloc(sizeof(float) * (size_t)kk * OC);
-      for (int o = 0; o < OC; ++o)
-        for (int r = 0; r < kk; ++r) wt[(size_t)r * OC + o] = w[(size_t)o * kk + r];
-      gemm_nn(wt, dyn, dcols, kk, (int)plane_out, OC, 0);
-      free(wt);
-      orc_col2im(dcols, dxin, C, ih, iw, k, k, stride, pad, oh, ow);
-      float* dxn = dx + (size_t)n * C * H * W;
-      if (up) {
-        memset(dxn, 0, sizeof(float) * C * H * W);
-        for (int c = 0; c < C; ++c)
-          for (int yy = 0; yy < ih; ++yy)
-            for (int xx = 0; xx < iw; ++xx)
-              dxn[((size_t)c * H + yy / 2) * W + xx / 2] += dxin[(size_t)c * plane_in + yy * iw + xx];
-      } else {
-        memcpy(dxn, dxin, sizeof(float) * C * plane_in);
-      }
+  }
+  if (dx) {
+    if (!up) {
+      conv_core_dgrad(dy, N, &g, w, OC, dx);
+    } else {
+      float* dxin = (float*)malloc(sizeof(float) * (size_t)N * C * plane_in);
+      conv_core_dgrad(dy, N, &g, w, OC, dxin);
+#pragma omp parallel for collapse(2) schedule(static)
+      for (int n = 0; n < N; ++n)
+        for (int c = 0; c < C; ++c) {
+          float* dxc = dx + ((size_t)n * C + c) * H * W;
+          const float* src = dxin + ((size_t)n * C + c) * plane_in;
+          memset(dxc, 0, sizeof(float) * H * W);
+          for (int yy = 0; yy < g.ih; ++yy)
+            for (int xx = 0; xx < g.iw; ++xx)
+              dxc[(size_t)(yy / 2) * W + xx / 2] += src[(size_t)yy * g.iw + xx];
+        }
+      free(dxin);
     }
   }
-  free(xin);
-  free(cols);
-  free(dxin);
 }
 
 /* GroupNorm with affine gamma/beta and eps (torch.nn.GroupNorm semantics, the

@@ -82,9 +82,24 @@ def f32(a):
     return np.ascontiguousarray(np.asarray(a, dtype=np.float32))
 
 
+def _keep_freed_memory():
+    """Full-resolution oracle passes allocate and free arrays of hundreds of
+    MB; glibc would hand each one back to the kernel (mmap / trim) and fault
+    its pages in again on the next allocation.  Serve them from the heap and
+    keep freed memory instead (glibc mallopt M_MMAP_MAX = 0, M_TRIM_THRESHOLD
+    = 2^62); a no-op where libc has no mallopt."""
+    try:
+        libc = C.CDLL("libc.so.6")
+        libc.mallopt(-4, 0)
+        libc.mallopt(-1, C.c_int(2**31 - 1))
+    except (OSError, AttributeError):
+        pass
+
+
 def load_oracle():
     if not ORACLE_SO.exists():
         subprocess.run(["make", "-C", str(ORACLE_DIR)], check=True, capture_output=True)
+    _keep_freed_memory()
     L = C.CDLL(str(ORACLE_SO))
     for name, (args, res) in _SIGS.items():
         fn = getattr(L, name)
@@ -102,7 +117,7 @@ def conv2d_fwd(L, x, w, b=None, stride=1, pad=1, up=False, up_hw=None, bias2d=No
     oc, k = w.shape[0], w.shape[-1]
     hin, win = (up_hw if up_hw else (2 * h, 2 * wd)) if up else (h, wd)
     oh, ow = (hin + 2 * pad - k) // stride + 1, (win + 2 * pad - k) // stride + 1
-    y = np.zeros((n, oc, oh, ow), np.float32)
+    y = np.empty((n, oc, oh, ow), np.float32)  # every element is written
     L.orc_conv2d_fwd(ptr(x), n, c, h, wd, ptr(w), ptr(f32(b) if b is not None else None), oc, k,
                      stride, pad, int(up), hin, win,
                      ptr(f32(bias2d) if bias2d is not None else None),
@@ -115,10 +130,10 @@ def conv2d_bwd(L, x, w, dy, stride=1, pad=1, up=False, up_hw=None):
     n, c, h, wd = x.shape
     oc, k = w.shape[0], w.shape[-1]
     hin, win = (up_hw if up_hw else (2 * h, 2 * wd)) if up else (h, wd)
-    dx = np.zeros_like(x)
-    dw = np.zeros_like(w)
-    db = np.zeros(oc, np.float32)
-    dbi = np.zeros((n, oc), np.float32)
+    dx = np.empty_like(x)  # dx, dw, db and dbi are overwritten whole
+    dw = np.empty_like(w)
+    db = np.empty(oc, np.float32)
+    dbi = np.empty((n, oc), np.float32)
     L.orc_conv2d_bwd(ptr(x), n, c, h, wd, ptr(w), oc, k, stride, pad, int(up), hin, win, ptr(dy),
                      ptr(dx), ptr(dw), ptr(db), ptr(dbi))
     return dx, dw, db, dbi
@@ -127,9 +142,9 @@ def conv2d_bwd(L, x, w, dy, stride=1, pad=1, up=False, up_hw=None):
 def gn_silu_fwd(L, x, groups, eps, gamma=None, beta=None, silu=True):
     x = f32(x)
     n, c, h, w = x.shape
-    y = np.zeros_like(x)
-    m = np.zeros(n * groups, np.float32)
-    r = np.zeros(n * groups, np.float32)
+    y = np.empty_like(x)  # every element is written
+    m = np.empty(n * groups, np.float32)
+    r = np.empty(n * groups, np.float32)
     L.orc_gn_silu_fwd(ptr(x), n, c, h * w, groups, eps, ptr(f32(gamma) if gamma is not None else None),
                       ptr(f32(beta) if beta is not None else None), int(silu), ptr(y), ptr(m), ptr(r))
     return y, m, r
@@ -138,9 +153,9 @@ def gn_silu_fwd(L, x, groups, eps, gamma=None, beta=None, silu=True):
 def gn_silu_bwd(L, x, dy, groups, eps, gamma=None, beta=None, silu=True, addend=None):
     x, dy = f32(x), f32(dy)
     n, c, h, w = x.shape
-    dx = np.zeros_like(x)
-    dg = np.zeros(c, np.float32)
-    db = np.zeros(c, np.float32)
+    dx = np.empty_like(x)  # every element is written
+    dg = np.empty(c, np.float32)
+    db = np.empty(c, np.float32)
     L.orc_gn_silu_bwd(ptr(x), ptr(dy), n, c, h * w, groups, eps,
                       ptr(f32(gamma) if gamma is not None else None),
                       ptr(f32(beta) if beta is not None else None), int(silu),
