@@ -71,8 +71,19 @@ yl_status yl_session_commit(yl_ctx* ctx);
  * wall time the way boundedGpuMs does (GpuWaitPolicy.swift:75-87). */
 yl_status yl_session_end(yl_ctx* ctx, double timeout_s, double* gpu_ms);
 /* Reads and clears the context's device error word (kernels write it when a
- * bounded wait gives up or a device-side check fails). */
+ * bounded wait gives up or a device-side check fails): YL_ERR_TIMEOUT for a
+ * wait that gave up (the reference's hang guard, GpuTraining.swift:92-97,
+ * exits with 70 instead), YL_ERR_DEVICE_ASSERT for a failed device check. */
 yl_status yl_ctx_check_device_errors(yl_ctx* ctx);
+/* Bound of every device-side wait of this context's kernels, in SM clock
+ * cycles (<= 0: the default 2e9, about 1 s).  The reference's wait policy
+ * (GpuWaitPolicy.swift:54-61) bounds the host wait only; this also bounds
+ * the kernels' pipeline waits.  Tests shorten it to drive the timeout path. */
+yl_status yl_ctx_set_wait_limit(yl_ctx* ctx, long long cycles);
+/* Name of the last conv kernel template this context launched: which = 0
+ * forward / dX, 1 filter gradient ("" before any).  Diagnostics only; no
+ * counterpart in the reference, whose conv is one im2col + matmul path. */
+const char* yl_ctx_last_kernel(yl_ctx* ctx, int which);
 
 /* --------------------------------------------------------------- GPUTensor
  * GPUTensor (GPUTensor.swift:9-143): rows x cols fp32, row-major, owned by
@@ -439,6 +450,15 @@ yl_status yl_profile_groupnorm(yl_ctx* ctx, int n, int c, int h, int w, int reps
 /* Layered 8-channel loss + gradient on n images of `plane` pixels (synthetic
  * planes); *ms = average device time of one yl_layered_loss call. */
 yl_status yl_profile_layered(yl_ctx* ctx, int n, long long plane, int reps, double* ms);
+/* Failure-path probes for the bounded waits (gpuWaitOutcome,
+ * GpuWaitPolicy.swift:54-61, tested by TestGroup1.swift:129): the wait probe
+ * queues one kernel whose single thread waits on an mbarrier nothing arrives
+ * on; the wait gives up after the context's wait limit and the next
+ * yl_ctx_check_device_errors / yl_session_end returns YL_ERR_TIMEOUT.  The
+ * spin queues one kernel that stays busy for `seconds` (<= 10) and ends
+ * normally, so a shorter yl_session_end deadline can run out on the host. */
+yl_status yl_debug_wait_probe(yl_ctx* ctx);
+yl_status yl_debug_spin(yl_ctx* ctx, double seconds);
 
 #ifdef __cplusplus
 }

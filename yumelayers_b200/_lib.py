@@ -151,8 +151,12 @@ SIGNATURES: dict[str, list] = {
     "yl_trainer_kernel_stats": [P, C.POINTER(KernelStats), I],
     "yl_trainer_activation_bytes": [P, C.POINTER(SZ)],
 }
+SIGNATURES["yl_ctx_set_wait_limit"] = [P, C.c_longlong]
+SIGNATURES["yl_ctx_last_kernel"] = [P, I]
+SIGNATURES["yl_debug_wait_probe"] = [P]
+SIGNATURES["yl_debug_spin"] = [P, D]
 _RET = {"yl_last_error_message": C.c_char_p, "yl_version": C.c_char_p,
-        "yl_kernel_launch_count": C.c_ulonglong,
+        "yl_kernel_launch_count": C.c_ulonglong, "yl_ctx_last_kernel": C.c_char_p,
         "yl_ctx_get_stream": P, "yl_tensor_data": P, "yl_tensor_rows": I, "yl_tensor_cols": I}
 NON_STATUS = set(_RET)
 

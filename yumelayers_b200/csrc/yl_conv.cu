@@ -28,6 +28,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <cstdio>
 #include <mutex>
 #include <vector>
 
@@ -70,6 +71,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  const long long lim = wait_limit(err);
 
   if (warp < 4) {
     // ---------------- A-operand gather (implicit im2col) ----------------
@@ -93,7 +95,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool ok = true;
     for (int kb = 0; kb < nk; ++kb) {
       const int s = kb % S;
-      if (kb >= S && !mbar_wait(&empty[s], ((kb / S) - 1) & 1)) {
+      if (kb >= S && !mbar_wait(&empty[s], ((kb / S) - 1) & 1, lim)) {
         ok = false;
         break;
       }
@@ -135,16 +137,21 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 4) {
     // ---------------- B-operand (weights) via TMA ----------------
     if (lane == 0) {
+      uint32_t issued = 0;
       for (int kb = 0; kb < nk; ++kb) {
         const int s = kb % S;
-        if (kb >= S && !mbar_wait(&empty[s], ((kb / S) - 1) & 1)) {
+        if (kb >= S && !mbar_wait(&empty[s], ((kb / S) - 1) & 1, lim)) {
           report_error(err, YL_DEVERR_TIMEOUT);
           break;
         }
         mbar_arrive_expect_tx(&full[s], Cfg::kBTileBytes);
         tma_load_2d(smem_u32(smem + s * Cfg::kStageBytes + kATileBytes), &tmap_w, &full[s],
                     kb * kBK, n0);
+        ++issued;
       }
+      // no copy may still be landing in shared memory when the CTA exits (the
+      // gather threads' cp.async arrivals complete the same phases)
+      drain_ring(full, S, issued);
     }
   } else {
     // ---------------- MMA issue (single thread) ----------------
@@ -152,7 +159,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       constexpr uint32_t idesc = idesc_tf32(kBM, BN, 0, 0);
       for (int kb = 0; kb < nk; ++kb) {
         const int s = kb % S;
-        if (!mbar_wait(&full[s], (kb / S) & 1)) {
+        if (!mbar_wait(&full[s], (kb / S) & 1, lim)) {
           report_error(err, YL_DEVERR_TIMEOUT);
           break;
         }
@@ -169,12 +176,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         umma_commit(&empty[s]);
       }
       umma_commit(accum);
+      // every MMA this thread issued has completed before TMEM is released
+      mbar_wait(accum, 0);
     }
   }
 
   // ---------------- epilogue: TMEM -> registers -> global ----------------
   if (warp < 4) {
-    const bool got = mbar_wait(accum, 0);
+    const bool got = mbar_wait(accum, 0, lim);
     if (!got) report_error(err, YL_DEVERR_TIMEOUT);
     tc_fence_after();
     const int row = warp * 32 + lane;
@@ -289,6 +298,7 @@ __global__ void __launch_bounds__(kThreads, 1) conv_wgrad_kernel(WgradArgs w, in
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  const long long lim = wait_limit(err);
 
   if (warp < 4) {
     const int t = threadIdx.x;
@@ -298,7 +308,7 @@ __global__ void __launch_bounds__(kThreads, 1) conv_wgrad_kernel(WgradArgs w, in
     bool ok = true;
     for (int kb = 0; kb < nk; ++kb) {
       const int s = kb % S;
-      if (kb >= S && !mbar_wait(&empty[s], ((kb / S) - 1) & 1)) {
+      if (kb >= S && !mbar_wait(&empty[s], ((kb / S) - 1) & 1, lim)) {
         ok = false;
         break;
       }
@@ -359,7 +369,7 @@ __global__ void __launch_bounds__(kThreads, 1) conv_wgrad_kernel(WgradArgs w, in
       constexpr uint32_t idesc = idesc_tf32(kBM, BN, 1, 1);
       for (int kb = 0; kb < nk; ++kb) {
         const int s = kb % S;
-        if (!mbar_wait(&full[s], (kb / S) & 1)) {
+        if (!mbar_wait(&full[s], (kb / S) & 1, lim)) {
           report_error(err, YL_DEVERR_TIMEOUT);
           break;
         }
@@ -379,11 +389,13 @@ __global__ void __launch_bounds__(kThreads, 1) conv_wgrad_kernel(WgradArgs w, in
         umma_commit(&empty[s]);
       }
       umma_commit(accum);
+      // every MMA this thread issued has completed before TMEM is released
+      mbar_wait(accum, 0);
     }
   }
 
   if (warp < 4) {
-    const bool got = mbar_wait(accum, 0);
+    const bool got = mbar_wait(accum, 0, lim);
     if (!got) report_error(err, YL_DEVERR_TIMEOUT);
     tc_fence_after();
     const int co = m0 + warp * 32 + lane;
@@ -446,6 +458,7 @@ static yl_status launch_gemm(yl_ctx* ctx, const ConvGather& g, const float* w, i
   YL_CUDA(cudaFuncSetAttribute(conv_gemm_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                Cfg::kSmemBytes));
   dim3 grid((g.m_total + kBM - 1) / kBM, (e.n_total + BN - 1) / BN);
+  snprintf(ctx->last_kernel[0], sizeof(ctx->last_kernel[0]), "conv_gemm_kernel<%d>", BN);
   conv_gemm_kernel<BN><<<grid, kThreads, Cfg::kSmemBytes, ctx->stream>>>(tm, g, e, ctx->dev_err);
   return check_launch("conv_gemm_kernel");
 }
@@ -488,6 +501,7 @@ yl_status conv_wgrad_gather(yl_ctx* ctx, const float* dy, int ldy, int cout,
   YL_CUDA(cudaFuncSetAttribute(conv_wgrad_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                Cfg::kSmemBytes));
   dim3 grid((cout + kBM - 1) / kBM, (n_total + BN - 1) / BN, splits);
+  snprintf(ctx->last_kernel[1], sizeof(ctx->last_kernel[1]), "conv_wgrad_kernel<%d>", BN);
   conv_wgrad_kernel<BN><<<grid, kThreads, Cfg::kSmemBytes, ctx->stream>>>(a, ctx->dev_err);
   YL_TRY(check_launch("conv_wgrad_kernel"));
   long long n = (long long)cout * n_total;

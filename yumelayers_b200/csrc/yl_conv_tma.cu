@@ -14,6 +14,8 @@
 // upsample-conv (output-gradient phase views) filter gradients.
 // Shapes the tap tables do not cover fall back to the cp.async gathers of
 // yl_conv.cu.
+#include <cstdio>
+
 #include "yl_conv_common.cuh"
 #include "yl_norm.h"
 
@@ -60,7 +62,7 @@ struct FpropCfg {
   static constexpr int kStages = kFit > 8 ? 8 : kFit;
   static constexpr int kAccCols = MT * BN < 32 ? 32 : MT * BN;
   static constexpr int kTmemCols = 2 * kAccCols;  // two accumulator buffers
-  static constexpr int kSmemBytes = kStages * kStage + kOut + (2 * kStages + 4) * 8 + 16 + 1024;
+  static constexpr int kSmemBytes = kStages * kStage + kOut + (2 * kStages + 5) * 8 + 16 + 1024;
   static_assert(kTmemCols <= 512, "accumulators exceed TMEM");
   static_assert(kSmemBytes <= 227 * 1024, "stages exceed shared memory");
 };
@@ -78,7 +80,7 @@ struct HaloCfg {
   static constexpr int kAS = 2, kWS = 6;
   static constexpr int kOut = 4 * 2 * 4096;  // epilogue staging, as FpropCfg::kOut
   static constexpr int kRing = kAS * kABox + kWS * kWTile + kOut;
-  static constexpr int kSmemBytes = kRing + (2 * (kAS + kWS) + 4) * 8 + 16 + 1024;
+  static constexpr int kSmemBytes = kRing + (2 * (kAS + kWS) + 5) * 8 + 16 + 1024;
   static_assert(kSmemBytes <= 227 * 1024, "halo rings exceed shared memory");
 };
 
@@ -196,9 +198,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* empty = full + S;
   uint64_t* acc_full = full + kRingBars;  // [2]: MMA -> epilogue
   uint64_t* acc_empty = acc_full + 2;     // [2]: epilogue (128 threads) -> MMA
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  uint64_t* drain = acc_empty + 2;        // MMA thread: all of its MMAs completed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const long long lim = wait_limit(err);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kRingBars; ++s) mbar_init(&full[s], 1);
@@ -206,6 +210,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&acc_full[b], 1);
       mbar_init(&acc_empty[b], 128);
     }
+    mbar_init(drain, 1);
     fence_barrier_init();
   }
   if (warp == 5) {
@@ -230,7 +235,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint64_t* aempty = full + AS;
       uint64_t* wfull = full + 2 * AS;
       uint64_t* wempty = wfull + WS;
-      uint32_t ia = 0, iw = 0;
+      uint32_t ia = 0, iw = 0;  // box / weight fills issued
       bool ok = true;
       for (int tile = blockIdx.x; ok && tile < p.n_tiles; tile += gridDim.x) {
         const FpropTile c = fprop_tile(p, tile);
@@ -238,30 +243,34 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int ox0 = c.tx * 32, oy0 = c.ty * kRows, n0 = c.nb * BN;
         for (int g = 0; ok && g < 3; ++g) {
           const int dy0 = min(ph.dy[g], min(ph.dy[g + 3], ph.dy[g + 6]));
-          for (int ch = 0; ch < p.cpt; ++ch, ++ia) {
+          for (int ch = 0; ok && ch < p.cpt; ++ch) {
             const int sa = ia % AS;
-            if (ia >= AS && !mbar_wait(&aempty[sa], ((ia / AS) - 1) & 1)) {
+            if (ia >= AS && !mbar_wait(&aempty[sa], ((ia / AS) - 1) & 1, lim)) {
               ok = false;
               break;
             }
             mbar_arrive_expect_tx(&afull[sa], HaloCfg::kABox);
             tma_load_4d(smem_u32(smem + sa * HaloCfg::kABox), &ta0, &afull[sa], ch * 32,
                         ox0 + ph.dx[g], oy0 + dy0, c.img);
-            for (int j = 0; j < 3; ++j, ++iw) {
+            ++ia;
+            for (int j = 0; j < 3; ++j) {
               const int sw = iw % WS;
-              if (iw >= WS && !mbar_wait(&wempty[sw], ((iw / WS) - 1) & 1)) {
+              if (iw >= WS && !mbar_wait(&wempty[sw], ((iw / WS) - 1) & 1, lim)) {
                 ok = false;
                 break;
               }
               mbar_arrive_expect_tx(&wfull[sw], HaloCfg::kWTile);
               tma_load_2d(smem_u32(smem + AS * HaloCfg::kABox + sw * HaloCfg::kWTile), &tw,
                           &wfull[sw], ((g + 3 * j) * p.cpt + ch) * kBK, ph.w_row0 + n0);
+              ++iw;
             }
-            if (!ok) break;
           }
         }
       }
       if (!ok) report_error(err, YL_DEVERR_TIMEOUT);
+      // no copy may still be landing in shared memory when the CTA exits
+      drain_ring(afull, AS, ia);
+      drain_ring(wfull, WS, iw);
     }
   } else if (HALO && warp == 5) {
     if (lane == 0) {
@@ -276,7 +285,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       for (int tile = blockIdx.x; ok && tile < p.n_tiles; tile += gridDim.x, ++tc) {
         const int buf = tc & 1, use = tc >> 1;
-        if (tc >= 2 && !mbar_wait(&acc_empty[buf], (use - 1) & 1)) {
+        if (tc >= 2 && !mbar_wait(&acc_empty[buf], (use - 1) & 1, lim)) {
           ok = false;
           break;
         }
@@ -287,14 +296,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int dy0 = min(ph.dy[g], min(ph.dy[g + 3], ph.dy[g + 6]));
           for (int ch = 0; ch < p.cpt; ++ch, ++ia) {
             const int sa = ia % AS;
-            if (!mbar_wait(&afull[sa], (ia / AS) & 1)) {
+            if (!mbar_wait(&afull[sa], (ia / AS) & 1, lim)) {
               ok = false;
               break;
             }
             const uint32_t box = smem_u32(smem + sa * HaloCfg::kABox);
             for (int j = 0; j < 3; ++j, ++iw) {
               const int sw = iw % WS;
-              if (!mbar_wait(&wfull[sw], (iw / WS) & 1)) {
+              if (!mbar_wait(&wfull[sw], (iw / WS) & 1, lim)) {
                 ok = false;
                 break;
               }
@@ -315,6 +324,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (ok) umma_commit(&acc_full[buf]);
       }
       if (!ok) report_error(err, YL_DEVERR_TIMEOUT);
+      // every MMA this thread issued has completed before TMEM is released
+      umma_commit(drain);
+      mbar_wait(drain, 0);
     }
   } else if (warp == 4) {
     if (lane == 0) {
@@ -329,7 +341,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         int t = 0, chunk = 0;
         for (int kb = 0; kb < nk; ++kb, ++it) {
           const int s = it % S;
-          if (it >= S && !mbar_wait(&empty[s], ((it / S) - 1) & 1)) {
+          if (it >= S && !mbar_wait(&empty[s], ((it / S) - 1) & 1, lim)) {
             report_error(err, YL_DEVERR_TIMEOUT);
             ok = false;
             break;
@@ -345,6 +357,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
+      // no copy may still be landing in shared memory when the CTA exits
+      drain_ring(full, S, it);
     }
   } else if (warp == 5) {
     if (lane == 0) {
@@ -354,7 +368,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       for (int tile = blockIdx.x; ok && tile < p.n_tiles; tile += gridDim.x, ++tc) {
         const int buf = tc & 1, use = tc >> 1;
-        if (tc >= 2 && !mbar_wait(&acc_empty[buf], (use - 1) & 1)) {
+        if (tc >= 2 && !mbar_wait(&acc_empty[buf], (use - 1) & 1, lim)) {
           report_error(err, YL_DEVERR_TIMEOUT);
           break;
         }
@@ -364,7 +378,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t dacc = tmem + (uint32_t)(buf * Cfg::kAccCols);
         for (int kb = 0; kb < nk; ++kb, ++it) {
           const int s = it % S;
-          if (!mbar_wait(&full[s], (it / S) & 1)) {
+          if (!mbar_wait(&full[s], (it / S) & 1, lim)) {
             report_error(err, YL_DEVERR_TIMEOUT);
             ok = false;
             break;
@@ -390,6 +404,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (ok) umma_commit(&acc_full[buf]);
       }
+      // every MMA this thread issued has completed before TMEM is released
+      umma_commit(drain);
+      mbar_wait(drain, 0);
     }
   } else {
     // epilogue: warp w owns TMEM lanes 32w..32w+31 = lattice row 4m + w of subtile m
@@ -416,7 +433,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
-      if (!mbar_wait(&acc_full[buf], use & 1)) {
+      if (!mbar_wait(&acc_full[buf], use & 1, lim)) {
         report_error(err, YL_DEVERR_TIMEOUT);
         break;
       }
@@ -729,6 +746,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   // the epilogue warps read every dy stage for the bias gradient and release
   // it together with the MMA warp
   const bool with_db = w.db_ws != nullptr && n0 == 0;
+  const long long lim = wait_limit(err);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
@@ -760,9 +778,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       WgAtom at[Cfg::kBAtoms];
 #pragma unroll
       for (int j = 0; j < Cfg::kBAtoms; ++j) at[j] = wgrad_atom(w, n0 + 32 * j, phase);
+      uint32_t issued = 0;
       for (int kb = 0; kb < nk; ++kb) {
         const int s = kb % S;
-        if (kb >= S && !mbar_wait(&empty[s], ((kb / S) - 1) & 1)) {
+        if (kb >= S && !mbar_wait(&empty[s], ((kb / S) - 1) & 1, lim)) {
           report_error(err, YL_DEVERR_TIMEOUT);
           break;
         }
@@ -784,6 +803,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             tma_load_5d(b_dst + j * Cfg::kAtomBytes, bmaps[at[j].map], &full[s], 0,
                         gx0 + at[j].bx, gy + at[j].by, at[j].ci / 32, im);
         }
+        ++issued;
         if (++xb == w.xblocks) {
           xb = 0;
           if (++gy == w.gh) {
@@ -792,13 +812,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
+      // no copy may still be landing in shared memory when the CTA exits
+      drain_ring(full, S, issued);
     }
   } else if (warp == 5) {
     if (lane == 0) {
       constexpr uint32_t idesc = idesc_tf32(kBM, NW, 1, 1);
       for (int kb = 0; kb < nk; ++kb) {
         const int s = kb % S;
-        if (!mbar_wait(&full[s], (kb / S) & 1)) {
+        if (!mbar_wait(&full[s], (kb / S) & 1, lim)) {
           report_error(err, YL_DEVERR_TIMEOUT);
           break;
         }
@@ -822,6 +844,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         umma_commit(&empty[s]);
       }
       umma_commit(accum);
+      // every MMA this thread issued has completed before TMEM is released
+      mbar_wait(accum, 0);
     }
   }
 
@@ -834,7 +858,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int m = 0; m < MT; ++m) sum[m] = 0.f;
     for (int kb = 0; kb < nk; ++kb) {
       const int s = kb % S;
-      if (!mbar_wait(&full[s], (kb / S) & 1)) {
+      if (!mbar_wait(&full[s], (kb / S) & 1, lim)) {
         report_error(err, YL_DEVERR_TIMEOUT);
         break;
       }
@@ -860,7 +884,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 
   if (warp < 4) {
-    const bool got = mbar_wait(accum, 0);
+    const bool got = mbar_wait(accum, 0, lim);
     if (!got) report_error(err, YL_DEVERR_TIMEOUT);
     tc_fence_after();
 #pragma unroll 1
@@ -1007,12 +1031,14 @@ static View phase_view(const float* p, int c, int w, int h, int n, int ps, int a
               2LL * ps, 2LL * w * ps, (long long)h * w * ps};
 }
 
-static yl_status make_view_tmap(CUtensorMap* tm, const View& v, int box_c, int box_h,
-                                CUtensorMapSwizzle swz, int box_w = 32) {
+// 4-D map {c, w, h, n} of a view with a box of box_c x box_w x box_h x 1.
+// Returns false (and records nothing) when the view cannot be described:
+// unaligned base or pixel stride, an empty extent, or an encode failure.
+static bool encode_view_tmap(CUtensorMap* tm, const View& v, int box_c, int box_h,
+                             CUtensorMapSwizzle swz, int box_w, int* cu_err) {
+  *cu_err = 0;
   auto fn = get_encode_fn();
-  YL_CHECK(fn, YL_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
-  YL_CHECK(((uintptr_t)v.base & 15) == 0 && v.sx % 4 == 0 && v.w >= 1 && v.h >= 1, YL_ERR_INVALID,
-           "view tensor map: alignment / extent");
+  if (!fn || ((uintptr_t)v.base & 15) != 0 || v.sx % 4 != 0 || v.w < 1 || v.h < 1) return false;
   cuuint64_t dims[4] = {(cuuint64_t)v.c, (cuuint64_t)v.w, (cuuint64_t)v.h, (cuuint64_t)v.n};
   cuuint64_t strides[3] = {(cuuint64_t)v.sx * 4, (cuuint64_t)v.sy * 4, (cuuint64_t)v.sn * 4};
   cuuint32_t box[4] = {(cuuint32_t)box_c, (cuuint32_t)box_w, (cuuint32_t)box_h, 1};
@@ -1020,7 +1046,17 @@ static yl_status make_view_tmap(CUtensorMap* tm, const View& v, int box_c, int b
   CUresult r = fn(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, const_cast<float*>(v.base), dims,
                   strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  YL_CHECK(r == CUDA_SUCCESS, YL_ERR_CUDA, "cuTensorMapEncodeTiled (view) failed (%d)", (int)r);
+  *cu_err = (int)r;
+  return r == CUDA_SUCCESS;
+}
+
+static yl_status make_view_tmap(CUtensorMap* tm, const View& v, int box_c, int box_h,
+                                CUtensorMapSwizzle swz, int box_w = 32) {
+  YL_CHECK(get_encode_fn(), YL_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
+  int cu_err = 0;
+  YL_CHECK(encode_view_tmap(tm, v, box_c, box_h, swz, box_w, &cu_err),
+           cu_err ? YL_ERR_CUDA : YL_ERR_INVALID, "view tensor map: %s (%d)",
+           cu_err ? "cuTensorMapEncodeTiled failed" : "alignment / extent", cu_err);
   return YL_OK;
 }
 
@@ -1120,8 +1156,8 @@ static yl_status launch_plan(yl_ctx* ctx, const View* views, int nviews, const f
             std::min(p.gh, (p.out_h - ph.ya + p.ys - 1) / p.ys), p.n_img,
             (long long)p.xs * e.ldo, (long long)p.ys * p.out_w * e.ldo,
             (long long)p.out_h * p.out_w * e.ldo};
-    if (ov.w < 1 || ov.h < 1 ||
-        make_view_tmap(&to[z], ov, 32, 1, CU_TENSOR_MAP_SWIZZLE_128B) != YL_OK)
+    int cu_err = 0;  // a map that cannot be built is not an error: per-thread stores
+    if (!encode_view_tmap(&to[z], ov, 32, 1, CU_TENSOR_MAP_SWIZZLE_128B, 32, &cu_err))
       p.tma_out = 0;
   }
   if (!p.tma_out)
@@ -1149,6 +1185,8 @@ static yl_status launch_plan(yl_ctx* ctx, const View* views, int nviews, const f
   YL_CUDA(cudaFuncSetAttribute(conv_tma_fprop_kernel<BN, MT, TR, HALO>,
                                cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem));
   const int grid = p.n_tiles < ctx->num_sms ? p.n_tiles : ctx->num_sms;
+  snprintf(ctx->last_kernel[0], sizeof(ctx->last_kernel[0]), "conv_tma_fprop_kernel<%d, %d, %d, %d>",
+           BN, MT, (int)TR, (int)HALO);
   conv_tma_fprop_kernel<BN, MT, TR, HALO><<<grid, kThreads, kSmem, ctx->stream>>>(
       ta[0], ta[1], ta[2], ta[3], tw, to[0], to[1], to[2], to[3], p, ek, ctx->dev_err);
   YL_TRY(check_launch("conv_tma_fprop_kernel"));
@@ -1509,6 +1547,8 @@ static yl_status launch_wgrad(yl_ctx* ctx, const View* av, int nav, const View* 
   YL_CUDA(cudaFuncSetAttribute(conv_tma_wgrad_kernel<MT, NSUB, NW, BKP>,
                                cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes));
   dim3 grid((w.cout + MT * kBM - 1) / (MT * kBM), col_blocks, splits);
+  snprintf(ctx->last_kernel[1], sizeof(ctx->last_kernel[1]), "conv_tma_wgrad_kernel<%d, %d, %d, %d>",
+           MT, NSUB, NW, BKP);
   conv_tma_wgrad_kernel<MT, NSUB, NW, BKP><<<grid, kThreads, Cfg::kSmemBytes, ctx->stream>>>(
       ta[0], ta[1], ta[2], ta[3], tb[0], tb[1], tb[2], tb[3], w, ctx->dev_err);
   return check_launch("conv_tma_wgrad_kernel");

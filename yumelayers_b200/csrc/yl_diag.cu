@@ -6,6 +6,7 @@
 #include <vector>
 
 #include "yl_kernels.h"
+#include "yl_ptx.cuh"
 #include "yl_norm.h"
 #include "yume_c.h"
 
@@ -41,9 +42,51 @@ struct DevBufs {
   }
 };
 
+// One thread waits on an mbarrier initialised for one arrival that nothing
+// ever makes: the wait runs out after the context's wait limit and records
+// YL_DEVERR_TIMEOUT, exactly as a conv kernel's pipeline wait would.
+__global__ void wait_probe_kernel(int* err) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x != 0) return;
+  mbar_init(&bar, 1);
+  fence_barrier_init();
+  if (!mbar_wait(&bar, 0, wait_limit(err))) report_error(err, YL_DEVERR_TIMEOUT);
+}
+
+__device__ __forceinline__ unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Busy for `ns` nanoseconds of the global timer; also bounded by `max_cycles`
+// SM clock cycles so it ends even if the timer were to stall.
+__global__ void spin_kernel(unsigned long long ns, long long max_cycles) {
+  const unsigned long long t0 = global_ns();
+  const long long c0 = clock64();
+  while (global_ns() - t0 < ns && clock64() - c0 < max_cycles) {
+  }
+}
+
 }  // namespace
 
 extern "C" {
+
+yl_status yl_debug_wait_probe(yl_ctx* ctx) {
+  YL_CHECK(ctx, YL_ERR_INVALID, "yl_debug_wait_probe: ctx is NULL");
+  wait_probe_kernel<<<1, 32, 0, ctx->stream>>>(ctx->dev_err);
+  return check_launch("wait_probe_kernel");
+}
+
+yl_status yl_debug_spin(yl_ctx* ctx, double seconds) {
+  YL_CHECK(ctx && seconds >= 0.0 && seconds <= 10.0, YL_ERR_INVALID,
+           "yl_debug_spin: seconds must be in [0, 10]");
+  const unsigned long long ns = (unsigned long long)(seconds * 1e9);
+  // 3 GHz is above any SM clock of this part: the cycle bound only backs up
+  // the timer and never cuts a healthy spin short
+  spin_kernel<<<1, 32, 0, ctx->stream>>>(ns, (long long)(seconds * 3e9) + 1000000LL);
+  return check_launch("spin_kernel");
+}
 
 yl_status yl_profile_conv(yl_ctx* ctx, int n, int c, int h, int w, int oc, int k, int stride,
                           int up, int reps, yl_conv_profile* out) {

@@ -57,7 +57,13 @@ struct yl_ctx {
   cudaEvent_t ev_end = nullptr;
   bool session_open = false;
   std::chrono::steady_clock::time_point wall_begin;
-  int* dev_err = nullptr;  // device error word, zeroed at creation
+  // device control block (16 bytes): int error word at [0] (zeroed at
+  // creation), long long bounded-wait limit in SM cycles at byte 8 (0 = the
+  // kernels' default)
+  int* dev_err = nullptr;
+  // names of the last conv kernel templates launched on this context:
+  // [0] forward / dX, [1] filter gradient (diagnostics, yl_ctx_last_kernel)
+  char last_kernel[2][96] = {{0}, {0}};
   // Scratch slots: 0 = temporaries of one internal kernel sequence (split-K
   // partials, reduction partials); 1 = layout conversions of a C-ABI call.
   // slot 0: operator temporaries; 1: NCHW<->NHWC staging of the batched

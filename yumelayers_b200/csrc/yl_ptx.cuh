@@ -8,9 +8,12 @@
 
 namespace yl {
 
-// Every spin-wait in this library gives up after this many SM clock cycles
-// (~1 s at 1.9 GHz) and reports YL_DEVERR_TIMEOUT through the kernel's error
-// word instead of hanging the GPU.
+// Every spin-wait in this library gives up after a bounded number of SM
+// clock cycles and reports YL_DEVERR_TIMEOUT through the kernel's error word
+// instead of hanging the GPU.  The limit is read at kernel start from the
+// context's device control block (yl_ctx_set_wait_limit); this is its
+// default (~1 s at 1.9 GHz).  Waits that only drain a CTA's own copies in
+// flight before it exits always use the default.
 constexpr long long kWaitLimitCycles = 2000000000LL;
 
 enum DevErr : int {
@@ -25,6 +28,14 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
 
 __device__ __forceinline__ void report_error(int* err, int code) {
   if (err) atomicCAS(err, 0, code);
+}
+
+// The context's device control block: int [0] = error code, long long at
+// byte 8 = the bounded-wait limit in SM clock cycles (<= 0: the default).
+__device__ __forceinline__ long long wait_limit(const int* err) {
+  if (!err) return kWaitLimitCycles;
+  const long long v = *reinterpret_cast<const volatile long long*>(err + 2);
+  return v > 0 ? v : kWaitLimitCycles;
 }
 
 // ---------------------------------------------------------------- mbarrier
@@ -54,14 +65,25 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 // Bounded wait: true when the phase with `parity` completed, false when the
-// wait ran past kWaitLimitCycles.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+// wait ran past `limit` SM clock cycles.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
+                                          long long limit = kWaitLimitCycles) {
   if (mbar_try_wait(bar, parity)) return true;
   long long t0 = clock64();
   while (!mbar_try_wait(bar, parity)) {
-    if (clock64() - t0 > kWaitLimitCycles) return false;
+    if (clock64() - t0 > limit) return false;
   }
   return true;
+}
+
+// Before a CTA exits: wait (default limit) until the last min(issued, S)
+// fills of an S-stage ring, each signalled on full[fill % S], have landed.
+// Earlier fills were consumed already (fill i + S was issued only after fill
+// i's stage was released), so no barrier can be past the phase waited on.
+__device__ __forceinline__ void drain_ring(uint64_t* full, int S, uint32_t issued) {
+  const uint32_t first = issued > (uint32_t)S ? issued - (uint32_t)S : 0u;
+  for (uint32_t i = first; i < issued; ++i)
+    mbar_wait(&full[i % (uint32_t)S], (i / (uint32_t)S) & 1u, kWaitLimitCycles);
 }
 
 // ---------------------------------------------------------------- cp.async

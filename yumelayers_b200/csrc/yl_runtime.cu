@@ -84,8 +84,8 @@ yl_status yl_ctx_create(int device, yl_ctx** out) {
   c->stream = c->own_stream;
   YL_CUDA(cudaEventCreate(&c->ev_begin));
   YL_CUDA(cudaEventCreate(&c->ev_end));
-  YL_CUDA(cudaMalloc(&c->dev_err, sizeof(int)));
-  YL_CUDA(cudaMemset(c->dev_err, 0, sizeof(int)));
+  YL_CUDA(cudaMalloc(&c->dev_err, 16));
+  YL_CUDA(cudaMemset(c->dev_err, 0, 16));
   *out = c;
   return YL_OK;
 }
@@ -174,11 +174,29 @@ yl_status yl_ctx_check_device_errors(yl_ctx* ctx) {
   YL_CUDA(cudaStreamSynchronize(ctx->stream));
   if (h != 0) {
     YL_CUDA(cudaMemsetAsync(ctx->dev_err, 0, sizeof(int), ctx->stream));
-    return set_error(YL_ERR_DEVICE_ASSERT,
-                     "a kernel reported device error %d (%s)", h,
-                     h == 1 ? "bounded wait timed out" : "device-side check failed");
+    YL_CUDA(cudaStreamSynchronize(ctx->stream));
+    // a bounded device wait that gave up is the GPU-side hang guard's
+    // timeout (the reference exits with 70 there, GpuTraining.swift:92-97)
+    if (h == 1)
+      return set_error(YL_ERR_TIMEOUT, "a kernel's bounded wait timed out (device error 1)");
+    return set_error(YL_ERR_DEVICE_ASSERT, "a kernel reported device error %d (%s)", h,
+                     "device-side check failed");
   }
   return YL_OK;
+}
+
+yl_status yl_ctx_set_wait_limit(yl_ctx* ctx, long long cycles) {
+  YL_CHECK(ctx, YL_ERR_INVALID, "yl_ctx_set_wait_limit: ctx is NULL");
+  const long long v = cycles > 0 ? cycles : 0;
+  YL_CUDA(cudaMemcpyAsync(reinterpret_cast<char*>(ctx->dev_err) + 8, &v, sizeof(v),
+                          cudaMemcpyHostToDevice, ctx->stream));
+  YL_CUDA(cudaStreamSynchronize(ctx->stream));
+  return YL_OK;
+}
+
+const char* yl_ctx_last_kernel(yl_ctx* ctx, int which) {
+  if (!ctx || which < 0 || which > 1) return "";
+  return ctx->last_kernel[which];
 }
 
 // ------------------------------------------------------------------ tensors

@@ -41,6 +41,19 @@ class Context:
     def set_stream(self, stream_ptr: int | None) -> None:
         call("yl_ctx_set_stream", self.handle, C.c_void_p(stream_ptr or 0))
 
+    def set_wait_limit(self, cycles: int) -> None:
+        """Bound of the kernels' device-side waits in SM cycles (<= 0: default)."""
+        call("yl_ctx_set_wait_limit", self.handle, int(cycles))
+
+    def check_device_errors(self) -> None:
+        """Raise (and clear) what a kernel recorded in the device error word."""
+        call("yl_ctx_check_device_errors", self.handle)
+
+    def last_kernel(self, which: int = 0) -> str:
+        """Template name of the last conv kernel launched: 0 forward / dX, 1 dW."""
+        r = lib().yl_ctx_last_kernel(self.handle, int(which))
+        return r.decode() if r else ""
+
 
 class GPUTensor:
     """rows x cols fp32 device tensor (GPUTensor.swift:9-143)."""
