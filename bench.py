@@ -17,10 +17,14 @@ synchronize on both sides, max over ranks):
 Per-kernel-class times come from CUDA events the library records around
 every conv / GroupNorm launch inside the `value` region.
 
+Roofline denominators: the dense TF32 rate is measured at the start of the
+run on the same GPU (cuBLAS fp32 GEMM with TF32 tensor cores, burst and
+sustained); HBM bandwidth comes from the driver's MEASURED_PEAKS.json.
+
 --impl reference times the reference's arithmetic on the CPU instead: the
 oracle (a C restatement of the reference's own kernels, oracle/) running the
-same joint step, all host threads, on a bounded sample (one frame-pair on a
-16-row crop of the frame, scaled by area to frame-pairs/s).
+same joint step on one full 480x856 frame-pair per step (the metric's unit),
+with the thread count set explicitly to every CPU the process may use.
 """
 from __future__ import annotations
 
@@ -130,15 +134,36 @@ class ClockSampler:
 
 
 # ------------------------------------------------------------------ CPU arm
-def cpu_sample(steps: int, warmup: int, crop_rows: int = 16, width: int = 856):
-    """The oracle's joint step on one frame-pair cropped to `crop_rows` rows."""
+def host_threads() -> int:
+    """CPUs this process may run on (torch.distributed.run sets OMP_NUM_THREADS=1
+    for every rank; the CPU baseline sets its thread count explicitly instead)."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def _oracle():
     sys.path.insert(0, str(ROOT / "oracle"))
+    import oracle_ctypes  # the oracle: a C restatement of the reference's kernels (CPU)
+    L = oracle_ctypes.load_oracle()
+    L.orc_set_num_threads(host_threads())
+    return oracle_ctypes, L
+
+
+def cpu_sample(steps: int, warmup: int, rows: int = 480, width: int = 856):
+    """The oracle's joint step (VAE fwd+bwd on frame k, encoder fwd on frames 0
+    and 16, motion U-Net fwd+bwd, Adam) on one full frame-pair, all host
+    threads.  A 16-row crop step first pages in the code paths untimed."""
+    _, L = _oracle()
     import nets  # the oracle's composition of the reference's kernels (CPU)
     from yumelayers_b200 import synth
-    js = nets.standalone_joint_step(seed=0)
-    clip = synth.make_clip(7, h=crop_rows, w=width - 2, width_padded=width)
+    js = nets.standalone_joint_step(seed=0, ops=nets.Ops(L))
+    clip = synth.make_clip(7, h=rows, w=width - 2, width_padded=width)
     frames = np.ascontiguousarray(np.stack([clip[0][None], clip[16][None], clip[5][None]]))
     t = np.array([5 / 16.0], np.float32)
+    small = np.ascontiguousarray(frames[:, :, :, :16])
+    js.step(small, t)
     for _ in range(warmup):
         js.step(frames, t)
     times = []
@@ -147,23 +172,66 @@ def cpu_sample(steps: int, warmup: int, crop_rows: int = 16, width: int = 856):
         js.step(frames, t)
         times.append(time.perf_counter() - t0)
     per_step = statistics.median(times)
-    frac = crop_rows / 480.0
-    return {"value": frac / per_step, "unit": "frame-pairs/s", "cores": js.o.L.orc_num_threads(),
+    return {"value": 1.0 / per_step, "unit": "frame-pairs/s", "cores": L.orc_num_threads(),
             "kind": "port",
             "sample": (f"oracle joint step (VAE train on frame k, encoder fwd on frames 0/16, "
-                       f"motion U-Net train) on one frame-pair cropped to {crop_rows}x{width}; "
-                       f"median of {steps} steps ({per_step:.2f} s), scaled by area "
-                       f"({crop_rows}/480 of a frame-pair)"),
+                       f"motion U-Net train, Adam) on one full {rows}x{width} frame-pair, "
+                       f"{L.orc_num_threads()} host threads; median of {steps} timed steps "
+                       f"({per_step:.1f} s each) after {warmup} full-size warm-up steps; "
+                       "no scaling"),
             "seconds_per_sample_step": per_step}
+
+
+def cpu_configs(reps_conv: int = 10, reps_block: int = 3):
+    """The two single-op workloads timed in full on the host cores with the
+    oracle: conv3x3 N=2 32->32 64x64 forward + dX + dW + db, and the ResNet
+    block N=8 C=128 128x128 forward + backward (GroupNorm32 eps 1e-6, SiLU)."""
+    oc_, L = _oracle()
+    from yumelayers_b200 import config_bench as cbm
+    rng = np.random.default_rng(0)
+    out = {}
+    d = cbm.CONV1
+    x = oc_.f32(rng.standard_normal((d["n"], d["c"], d["h"], d["w"])))
+    w = oc_.f32(rng.uniform(-0.08, 0.08, (d["oc"], d["c"], 3, 3)))
+    dy = oc_.f32(rng.standard_normal((d["n"], d["oc"], d["h"], d["w"])))
+    ts = []
+    for _ in range(reps_conv + 1):
+        t0 = time.perf_counter()
+        oc_.conv2d_fwd(L, x, w, None)
+        oc_.conv2d_bwd(L, x, w, dy)
+        ts.append(time.perf_counter() - t0)
+    out["conv1"] = statistics.median(ts[1:]) * 1e3
+    b = cbm.BLOCK
+    n, c, h, wd, g, eps = b["n"], b["c"], b["h"], b["w"], b["groups"], b["eps"]
+    x = oc_.f32(rng.standard_normal((n, c, h, wd)))
+    dy = oc_.f32(rng.standard_normal((n, c, h, wd)))
+    ga, be = oc_.f32(1 + 0.02 * rng.standard_normal(c)), oc_.f32(0.02 * rng.standard_normal(c))
+    w1 = oc_.f32(rng.uniform(-0.03, 0.03, (c, c, 3, 3)))
+    w2 = oc_.f32(rng.uniform(-0.03, 0.03, (c, c, 3, 3)))
+    ts = []
+    for _ in range(reps_block + 1):
+        t0 = time.perf_counter()
+        h1, _, _ = oc_.gn_silu_fwd(L, x, g, eps, ga, be)
+        c1 = oc_.conv2d_fwd(L, h1, w1, None)
+        h2, _, _ = oc_.gn_silu_fwd(L, c1, g, eps, ga, be)
+        oc_.conv2d_fwd(L, h2, w2, None, residual=x)
+        dh2, _, _, _ = oc_.conv2d_bwd(L, h2, w2, dy)
+        dc1, _, _ = oc_.gn_silu_bwd(L, c1, dh2, g, eps, ga, be)
+        dh1, _, _, _ = oc_.conv2d_bwd(L, h1, w1, dc1)
+        oc_.gn_silu_bwd(L, x, dh1, g, eps, ga, be, addend=dy)
+        ts.append(time.perf_counter() - t0)
+    out["block"] = statistics.median(ts[1:]) * 1e3
+    out["cores"] = L.orc_num_threads()
+    return out
 
 
 def run_reference(args):
     rank, world, _ = dist_env()
     if rank != 0:
         return
-    # each sample step takes about 2 s on the host cores: at most 5 timed and
-    # 3 warm-up steps keep the run within a minute
-    steps, warmup = max(1, min(args.steps, 5)), max(0, min(args.warmup, 3))
+    # one full frame-pair step takes tens of seconds on the host cores: at most
+    # 2 timed and 1 warm-up steps keep the run within a few minutes
+    steps, warmup = max(1, min(args.steps, 2)), max(0, min(args.warmup, 1))
     cb = cpu_sample(steps, warmup)
     line = {"metric": METRIC, "value": cb["value"], "unit": "frame-pairs/s", "impl": "reference",
             "n_gpus": args.gpus, "steps": steps, "warmup": warmup,
@@ -172,11 +240,57 @@ def run_reference(args):
             "data": "synthetic (seeded 17-frame clips: blobs + gratings + 4 moving sprites)",
             "config": {"workload": WORKLOAD, "frame": "480x856 (854 padded to 856)",
                        "per_gpu_batch": 8, "global_batch": 8,
-                       "parallelism": "host threads on rank 0 (the oracle's CPU path)"},
+                       "parallelism": "host threads on rank 0 (the oracle's CPU path)",
+                       "sample": "one frame-pair per step (the metric's unit), full frame"},
             "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
             "e2e": {"value": cb["value"], "unit": "frame-pairs/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
+
+
+def measure_tf32_peak(device: int) -> dict:
+    """Dense TF32 tensor-core rate of this GPU the way the driver measures bf16:
+    torch.matmul on 8192^3 fp32 operands with TF32 allowed (cuBLAS), best of 10
+    single launches (burst) and back to back for >= 4 s (sustained, under the
+    power cap), with the SM clocks sampled during the sustained loop."""
+    import torch
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = True
+    try:
+        n = 8192
+        dev = f"cuda:{device}"
+        g = torch.Generator(device=dev).manual_seed(0)
+        a = torch.randn(n, n, device=dev, generator=g)
+        b = torch.randn(n, n, device=dev, generator=g)
+        c = torch.empty(n, n, device=dev)
+        flops = 2.0 * n ** 3
+        for _ in range(3):
+            torch.matmul(a, b, out=c)
+        torch.cuda.synchronize(dev)
+        best = float("inf")
+        for _ in range(10):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            torch.matmul(a, b, out=c)
+            e1.record()
+            e1.synchronize()
+            best = min(best, e0.elapsed_time(e1))
+        iters = max(10, int(4000.0 / best) + 1)
+        with ClockSampler(device) as clk:
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(iters):
+                torch.matmul(a, b, out=c)
+            e1.record()
+            e1.synchronize()
+        sustained_ms = e0.elapsed_time(e1) / iters
+        del a, b, c
+        torch.cuda.empty_cache()
+        return {"tf32_tflops": flops / (best * 1e-3) / 1e12,
+                "tf32_tflops_sustained": flops / (sustained_ms * 1e-3) / 1e12,
+                "sustained_seconds": iters * sustained_ms / 1e3, "clocks": clk.summary()}
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
 
 
 # ------------------------------------------------------------------ native arm
@@ -195,6 +309,8 @@ def run_native(args):
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=300),
                                 device_id=torch.device("cuda", local))
+    # this GPU's dense TF32 rate, measured before the trainer holds its memory
+    tf32 = measure_tf32_peak(local)
     ctx = Context(local)
     comm = None
     if world > 1:
@@ -267,13 +383,11 @@ def run_native(args):
     value = world * B * args.steps / (ms / 1000.0)
     e2e_value = world * B * args.steps / (e2e_ms / 1000.0)
     peaks = measured_peaks()
-    # the convs run inside a step of a few hundred ms: the sustained GEMM peak
-    bf16 = peaks.get("bf16_tflops_sustained")
-    hbm = peaks.get("hbm_gbs")
-    peak_src = "measured sustained" if bf16 else "fallback sustained"
-    bf16 = bf16 or 1400.0
-    hbm = hbm or 6650.0
-    tf32_peak = bf16 / 2.0
+    hbm = peaks.get("hbm_gbs") or 6650.0
+    hbm_src = "measured (MEASURED_PEAKS.json)" if peaks.get("hbm_gbs") else "fallback"
+    # the convs run inside a step of a few hundred ms: the sustained TF32 rate
+    tf32_peak = tf32["tf32_tflops_sustained"]
+    templates = tr.template_stats()
     kernels = {}
     for k, v in stats.items():
         if v["ms"] <= 0:
@@ -281,20 +395,33 @@ def run_native(args):
         ent = {"ms_per_step": v["ms"] / args.steps, "launches_per_step": v["launches"] / args.steps,
                "share_of_step": v["ms"] / ms}
         if v["flops"]:
-            ent["tflops"] = v["flops"] / (v["ms"] * 1e-3) / 1e12
-            ent["frac_tf32"] = ent["tflops"] / tf32_peak
+            ent["tflops_algorithmic"] = v["flops"] / (v["ms"] * 1e-3) / 1e12
+            ent["tflops_executed"] = v["exec_flops"] / (v["ms"] * 1e-3) / 1e12
+            ent["frac_tf32_executed"] = ent["tflops_executed"] / tf32_peak
         if v["bytes"]:
             ent["gbs"] = v["bytes"] / (v["ms"] * 1e-3) / 1e9
             ent["frac_hbm"] = ent["gbs"] / hbm
         kernels[k] = ent
+    conv_templates = []
+    for name, v in sorted(templates.items(), key=lambda kv: -kv[1]["ms"]):
+        if v["ms"] <= 0:
+            continue
+        ex = v["exec_flops"] / (v["ms"] * 1e-3) / 1e12
+        conv_templates.append({
+            "kernel": name, "launches_per_step": v["launches"] / args.steps,
+            "ms_per_step": v["ms"] / args.steps, "share_of_step": v["ms"] / ms,
+            "tflops_algorithmic": v["flops"] / (v["ms"] * 1e-3) / 1e12,
+            "tflops_executed": ex, "frac_tf32_executed": ex / tf32_peak})
     classes = ("conv_fprop", "conv_dgrad", "conv_wgrad", "gn_silu_fwd", "gn_silu_bwd")
     top = max(classes, key=lambda k: stats[k]["ms"])
     conv_flops = sum(stats[k]["flops"] for k in ("conv_fprop", "conv_dgrad", "conv_wgrad"))
+    conv_exec = sum(stats[k]["exec_flops"] for k in ("conv_fprop", "conv_dgrad", "conv_wgrad"))
     conv_ms = sum(stats[k]["ms"] for k in ("conv_fprop", "conv_dgrad", "conv_wgrad"))
     dom = stats.get("conv_3x3_128_frame", {"ms": 0.0})
     if dom["ms"] > 0 and dom["launches"] > 0:
         # the dominant launch type: one stride-1 3x3 128->128 pass over the batch
-        # at the frame resolution (forward or dX, the same kernel)
+        # at the frame resolution (forward or dX, the same kernel; algorithmic
+        # and executed FLOPs are equal for it)
         achieved = dom["flops"] / (dom["ms"] * 1e-3) / 1e12
         per_launch_flops = dom["flops"] / dom["launches"]
         per_launch_bytes = 2.0 * B * H * W * 128 * 4 + 128 * 128 * 9 * 4
@@ -302,33 +429,38 @@ def run_native(args):
                   "forward and dX passes)")
         traffic = DOM_TRAFFIC_PER_IMAGE * B if (H, W) == (480, 856) else None
     else:
-        achieved = stats[top]["flops"] / (stats[top]["ms"] * 1e-3) / 1e12
+        achieved = stats[top]["exec_flops"] / (stats[top]["ms"] * 1e-3) / 1e12
         per_launch_flops = per_launch_bytes = None
         kernel, traffic = top, None
     roofline = {"bound": "tensor", "kernel": kernel, "achieved": achieved, "peak": tf32_peak,
                 "unit": "TFLOP/s", "frac": achieved / tf32_peak, "traffic": traffic,
                 "flops_per_launch": per_launch_flops,
                 "algorithmic_bytes_per_launch": per_launch_bytes,
-                "peak_note": (f"tf32 peak = 1/2 of the {peak_src} dense bf16 "
-                              f"{bf16:.1f} TFLOP/s (no tf32 peak is measured)"),
+                "peak_note": ("measured in this run on this GPU: cuBLAS fp32 GEMM with TF32 "
+                              f"tensor cores, 8192^3, back to back for "
+                              f"{tf32['sustained_seconds']:.1f} s (sustained; burst "
+                              f"{tf32['tf32_tflops']:.1f} TFLOP/s), SM clock median "
+                              f"{tf32['clocks'].get('sm_mhz')} MHz, reasons "
+                              f"{tf32['clocks'].get('reasons')}"),
+                "peak_burst": tf32["tf32_tflops"],
                 "flops_note": ("achieved = 2*N*Cout*Cin*9*OH*OW per launch over the summed "
                                "CUDA-event time of those launches in the timed steps"),
                 "traffic_note": ("DRAM read + write bytes per launch from an ncu capture of "
-                                 "the same kernel on 2 images (profiles/"
-                                 "conv_tma_fprop_128ch_2x480x856.md), scaled to the batch; "
-                                 "below the algorithmic bytes because part of the output is "
+                                 "the same kernel on 2 images, scaled to the batch; below "
+                                 "the algorithmic bytes because part of the output is "
                                  "still in L2 when the kernel ends"),
-                "conv_fprop_class": {"achieved": stats["conv_fprop"]["flops"] /
-                                     (stats["conv_fprop"]["ms"] * 1e-3) / 1e12 if
-                                     stats["conv_fprop"]["ms"] > 0 else None},
-                "all_convs": {"achieved": conv_flops / (conv_ms * 1e-3) / 1e12,
-                              "frac": conv_flops / (conv_ms * 1e-3) / 1e12 / tf32_peak}}
+                "all_convs": {"tflops_algorithmic": conv_flops / (conv_ms * 1e-3) / 1e12,
+                              "tflops_executed": conv_exec / (conv_ms * 1e-3) / 1e12,
+                              "frac_executed": conv_exec / (conv_ms * 1e-3) / 1e12 / tf32_peak},
+                "hbm_peak_gbs": hbm, "hbm_peak_source": hbm_src}
     act_gb = tr.activation_bytes() / 1e9
     if rank == 0:
-        cpu = None
+        cpu, configs = None, None
+        if world == 1:
+            configs = config_lines(ctx, args.no_cpu_baseline)
         if world == 1 and not args.no_cpu_baseline:
             try:
-                cb = cpu_sample(steps=2, warmup=1)
+                cb = cpu_sample(steps=1, warmup=0)
                 cpu = {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")}
             except Exception as exc:  # reported, not fatal
                 cpu = {"value": None, "error": str(exc)}
@@ -346,7 +478,8 @@ def run_native(args):
                        "conv_tflop_per_step": conv_flops / 1e12 / args.steps},
             "e2e": {"value": e2e_value, "unit": "frame-pairs/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": 8, "ms_per_step": e2e_ms / args.steps},
-            "roofline": roofline, "kernels": kernels, "cpu_baseline": cpu,
+            "roofline": roofline, "kernels": kernels, "conv_templates": conv_templates,
+            "configs": configs, "cpu_baseline": cpu,
             "clocks": clocks, "gpu_launches": int(launches),
             "losses_last_step": losses,
         }
@@ -357,6 +490,37 @@ def run_native(args):
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def config_lines(ctx, no_cpu: bool) -> dict:
+    """The two single-op workloads: GPU device time through the C ABI (NCHW,
+    L2 evicted before each repetition) and the oracle timed in full on the host
+    cores."""
+    from yumelayers_b200 import config_bench as cbm
+    out = {}
+    try:
+        g1 = cbm.conv1_gpu_ms(ctx)
+        g2 = cbm.block_gpu_ms(ctx)
+        cpu = None if no_cpu else cpu_configs()
+        for key, gms, flops, what in (
+                ("conv3x3_n2_c32_64x64", g1, cbm.CONV1_FLOPS,
+                 "Conv2d 3x3 s1 p1, N=2, 32->32, 64x64: forward + dX + dW + db"),
+                ("resblock_n8_c128_128x128", g2, cbm.BLOCK_FLOPS,
+                 "ResNet block N=8 C=128 128x128 (GN32 eps 1e-6 + SiLU, two 3x3 convs, "
+                 "identity residual): forward + backward")):
+            ent = {"workload": what, "gpu_ms": gms, "gpu_tflops": flops / (gms * 1e-3) / 1e12,
+                   "conv_gflop": flops / 1e9,
+                   "gpu_note": "C-ABI calls on NCHW device buffers incl. layout conversions; "
+                               "median of the repetitions, L2 evicted before each"}
+            if cpu:
+                cms = cpu["conv1" if key.startswith("conv") else "block"]
+                ent.update({"cpu_ms": cms, "cpu_cores": cpu["cores"], "cpu_kind": "port",
+                            "cpu_note": "the oracle (C restatement of the reference's "
+                                        "kernels) timed in full, median of repetitions"})
+            out[key] = ent
+    except Exception as exc:  # reported, not fatal
+        out["error"] = str(exc)
+    return out
 
 
 def main():

@@ -421,12 +421,27 @@ yl_status yl_trainer_prepare_weights(yl_trainer* tr);
 #define YL_KERNEL_CLASSES 6
 typedef struct yl_kernel_stats {
   double ms[YL_KERNEL_CLASSES];
-  double flops[YL_KERNEL_CLASSES];
+  double flops[YL_KERNEL_CLASSES];      /* algorithmic: 2*N*Cout*Cin*k*k*OH*OW */
   double bytes[YL_KERNEL_CLASSES];
   int launches[YL_KERNEL_CLASSES];
+  double exec_flops[YL_KERNEL_CLASSES]; /* 2 x the MACs the conv kernels ran */
 } yl_kernel_stats;
 /* Accumulated CUDA-event times of the profiled steps (cfg.profile = 1). */
 yl_status yl_trainer_kernel_stats(yl_trainer* tr, yl_kernel_stats* out, int reset);
+/* The same profiled conv brackets per kernel template, as of the last
+ * yl_trainer_kernel_stats call: flops = algorithmic 2*N*Cout*Cin*k*k*OH*OW,
+ * exec_flops = 2 x the MACs the kernel ran (zero-padded channels counted;
+ * the merged-tap upsample convs run 16/36 of the algorithmic MACs).  Writes
+ * min(capacity, *count) entries; *count = number of templates.  No
+ * counterpart in the reference (its profileConv, Diagnostics.swift:123-201,
+ * times one im2col + matmul path). */
+typedef struct yl_template_stats {
+  char name[96];
+  double ms, flops, exec_flops;
+  int launches;
+} yl_template_stats;
+yl_status yl_trainer_template_stats(yl_trainer* tr, yl_template_stats* out, int capacity,
+                                    int* count);
 yl_status yl_trainer_activation_bytes(yl_trainer* tr, size_t* bytes);
 
 /* ---------------------------------------------------------------- diagnostics

@@ -55,7 +55,8 @@ class KernelStats(C.Structure):
     """``yl_kernel_stats``: conv fprop, conv dgrad, conv wgrad, GN fwd, GN bwd, and the
     dominant launch type (3x3 128->128 fprop/dX at the frame resolution, also in 0/1)."""
     _fields_ = [("ms", C.c_double * KERNEL_CLASSES), ("flops", C.c_double * KERNEL_CLASSES),
-                ("bytes", C.c_double * KERNEL_CLASSES), ("launches", C.c_int * KERNEL_CLASSES)]
+                ("bytes", C.c_double * KERNEL_CLASSES), ("launches", C.c_int * KERNEL_CLASSES),
+                ("exec_flops", C.c_double * KERNEL_CLASSES)]
 
 
 P = C.c_void_p
@@ -151,6 +152,13 @@ SIGNATURES: dict[str, list] = {
     "yl_trainer_kernel_stats": [P, C.POINTER(KernelStats), I],
     "yl_trainer_activation_bytes": [P, C.POINTER(SZ)],
 }
+class TemplateStats(C.Structure):
+    """``yl_template_stats``."""
+    _fields_ = [("name", C.c_char * 96), ("ms", C.c_double), ("flops", C.c_double),
+                ("exec_flops", C.c_double), ("launches", C.c_int)]
+
+
+SIGNATURES["yl_trainer_template_stats"] = [P, C.POINTER(TemplateStats), I, C.POINTER(I)]
 SIGNATURES["yl_ctx_set_wait_limit"] = [P, C.c_longlong]
 SIGNATURES["yl_ctx_last_kernel"] = [P, I]
 SIGNATURES["yl_debug_wait_probe"] = [P]

@@ -459,6 +459,7 @@ static yl_status launch_gemm(yl_ctx* ctx, const ConvGather& g, const float* w, i
                                Cfg::kSmemBytes));
   dim3 grid((g.m_total + kBM - 1) / kBM, (e.n_total + BN - 1) / BN);
   snprintf(ctx->last_kernel[0], sizeof(ctx->last_kernel[0]), "conv_gemm_kernel<%d>", BN);
+  ctx->last_exec_flops[0] = 2.0 * g.m_total * (double)g.k_total * e.n_total;
   conv_gemm_kernel<BN><<<grid, kThreads, Cfg::kSmemBytes, ctx->stream>>>(tm, g, e, ctx->dev_err);
   return check_launch("conv_gemm_kernel");
 }
@@ -502,6 +503,7 @@ yl_status conv_wgrad_gather(yl_ctx* ctx, const float* dy, int ldy, int cout,
                                Cfg::kSmemBytes));
   dim3 grid((cout + kBM - 1) / kBM, (n_total + BN - 1) / BN, splits);
   snprintf(ctx->last_kernel[1], sizeof(ctx->last_kernel[1]), "conv_wgrad_kernel<%d>", BN);
+  ctx->last_exec_flops[1] = 2.0 * a.g.m_total * (double)a.g.k_total * a.cout;
   conv_wgrad_kernel<BN><<<grid, kThreads, Cfg::kSmemBytes, ctx->stream>>>(a, ctx->dev_err);
   YL_TRY(check_launch("conv_wgrad_kernel"));
   long long n = (long long)cout * n_total;

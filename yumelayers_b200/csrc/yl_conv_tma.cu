@@ -44,8 +44,53 @@ struct ConvPlan {
   int pix_tiles;       // tiles_x * tiles_y * n_img
   int n_tiles;         // pix_tiles * n_nblk * phases
   int tma_out;         // non-transposed epilogue: stage rows in shared memory, TMA store
+  int* sched;          // [0] tiles handed out past the first wave, [1] CTAs done; both
+                       // zero at launch and reset by the last CTA (nullptr: static order)
   TapPhase ph[4];      // indexed by the tile's phase
 };
+
+// Tiles reach the MMA and epilogue warps through a small shared-memory ring
+// written by the producer warp, which takes each CTA's first tile by its block
+// index and every later one from the launch's atomic counter: a CTA that
+// starts late or runs slower (an SM shared with another kernel) simply takes
+// fewer tiles instead of holding up the launch with a fixed share.
+constexpr int kTileRing = 8;
+constexpr int kRingTimeout = -2;
+
+__device__ __forceinline__ int next_tile(const ConvPlan& p, uint32_t k) {
+  if (k == 0) return blockIdx.x;
+  if (p.sched) return (int)gridDim.x + atomicAdd(p.sched, 1);
+  return (int)(blockIdx.x + k * gridDim.x);
+}
+// Producer: publish the CTA's k-th tile (>= n_tiles: no more tiles).
+__device__ __forceinline__ bool ring_put(uint64_t* tfull, uint64_t* tempty, volatile int* ring,
+                                         uint32_t k, int tile, long long lim) {
+  const uint32_t s = k % kTileRing;
+  if (k >= kTileRing && !mbar_wait(&tempty[s], ((k / kTileRing) - 1) & 1, lim)) return false;
+  ring[s] = tile;
+  mbar_arrive(&tfull[s]);  // release: the consumers' wait acquires the store
+  return true;
+}
+// MMA thread: the CTA's k-th tile (kRingTimeout when the wait gave up).
+__device__ __forceinline__ int ring_take(uint64_t* tfull, uint64_t* tempty,
+                                         const volatile int* ring, uint32_t k, long long lim) {
+  const uint32_t s = k % kTileRing;
+  if (!mbar_wait(&tfull[s], (k / kTileRing) & 1, lim)) return kRingTimeout;
+  const int t = ring[s];
+  mbar_arrive(&tempty[s]);
+  return t;
+}
+// Epilogue warp: every lane reads the tile, lane 0 releases the slot.
+__device__ __forceinline__ int ring_take_warp(uint64_t* tfull, uint64_t* tempty,
+                                              const volatile int* ring, uint32_t k,
+                                              long long lim, int lane) {
+  const uint32_t s = k % kTileRing;
+  const bool ok = mbar_wait(&tfull[s], (k / kTileRing) & 1, lim);
+  const int t = ok ? ring[s] : kRingTimeout;
+  __syncwarp();
+  if (ok && lane == 0) mbar_arrive(&tempty[s]);
+  return __shfl_sync(0xffffffffu, t, 0);
+}
 
 // A tile is MT x 128 GEMM rows (MT*4 lattice rows x 32 lattice columns) by BN
 // output channels.  MT = 2 gives two M=128 accumulators that share every B
@@ -62,7 +107,8 @@ struct FpropCfg {
   static constexpr int kStages = kFit > 8 ? 8 : kFit;
   static constexpr int kAccCols = MT * BN < 32 ? 32 : MT * BN;
   static constexpr int kTmemCols = 2 * kAccCols;  // two accumulator buffers
-  static constexpr int kSmemBytes = kStages * kStage + kOut + (2 * kStages + 5) * 8 + 16 + 1024;
+  static constexpr int kSmemBytes =
+      kStages * kStage + kOut + (2 * kStages + 5 + 2 * 8) * 8 + 4 * 8 + 16 + 1024;
   static_assert(kTmemCols <= 512, "accumulators exceed TMEM");
   static_assert(kSmemBytes <= 227 * 1024, "stages exceed shared memory");
 };
@@ -80,7 +126,7 @@ struct HaloCfg {
   static constexpr int kAS = 2, kWS = 6;
   static constexpr int kOut = 4 * 2 * 4096;  // epilogue staging, as FpropCfg::kOut
   static constexpr int kRing = kAS * kABox + kWS * kWTile + kOut;
-  static constexpr int kSmemBytes = kRing + (2 * (kAS + kWS) + 5) * 8 + 16 + 1024;
+  static constexpr int kSmemBytes = kRing + (2 * (kAS + kWS) + 5 + 2 * 8) * 8 + 4 * 8 + 16 + 1024;
   static_assert(kSmemBytes <= 227 * 1024, "halo rings exceed shared memory");
 };
 
@@ -199,7 +245,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* acc_full = full + kRingBars;  // [2]: MMA -> epilogue
   uint64_t* acc_empty = acc_full + 2;     // [2]: epilogue (128 threads) -> MMA
   uint64_t* drain = acc_empty + 2;        // MMA thread: all of its MMAs completed
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* tfull = drain + 1;            // [kTileRing]: producer -> MMA + epilogue
+  uint64_t* tempty = tfull + kTileRing;   // [kTileRing]: MMA + 4 epilogue warps -> producer
+  int* tring = reinterpret_cast<int*>(tempty + kTileRing);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tring + kTileRing);
+  static_assert(kTileRing == 8, "the shared-memory budgets above reserve 8 ring slots");
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const long long lim = wait_limit(err);
@@ -211,6 +261,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&acc_empty[b], 128);
     }
     mbar_init(drain, 1);
+    for (int r = 0; r < kTileRing; ++r) {
+      mbar_init(&tfull[r], 1);
+      mbar_init(&tempty[r], 1 + 4);
+    }
     fence_barrier_init();
   }
   if (warp == 5) {
@@ -237,7 +291,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint64_t* wempty = wfull + WS;
       uint32_t ia = 0, iw = 0;  // box / weight fills issued
       bool ok = true;
-      for (int tile = blockIdx.x; ok && tile < p.n_tiles; tile += gridDim.x) {
+      for (uint32_t k = 0; ok; ++k) {
+        const int tile = next_tile(p, k);
+        if (!ring_put(tfull, tempty, tring, k, tile, lim)) {
+          ok = false;
+          break;
+        }
+        if (tile >= p.n_tiles) break;
         const FpropTile c = fprop_tile(p, tile);
         const TapPhase& ph = p.ph[0];
         const int ox0 = c.tx * 32, oy0 = c.ty * kRows, n0 = c.nb * BN;
@@ -283,7 +343,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t ia = 0, iw = 0;
       int tc = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; ok && tile < p.n_tiles; tile += gridDim.x, ++tc) {
+      for (uint32_t k = 0; ok; ++k, ++tc) {
+        const int tile = ring_take(tfull, tempty, tring, k, lim);
+        if (tile == kRingTimeout) {
+          ok = false;
+          break;
+        }
+        if (tile >= p.n_tiles) break;
         const int buf = tc & 1, use = tc >> 1;
         if (tc >= 2 && !mbar_wait(&acc_empty[buf], (use - 1) & 1, lim)) {
           ok = false;
@@ -333,7 +399,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       const CUtensorMap* maps[4] = {&ta0, &ta1, &ta2, &ta3};
       uint32_t it = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; ok && tile < p.n_tiles; tile += gridDim.x) {
+      for (uint32_t k = 0; ok; ++k) {
+        const int tile = next_tile(p, k);
+        if (!ring_put(tfull, tempty, tring, k, tile, lim)) {
+          report_error(err, YL_DEVERR_TIMEOUT);
+          break;
+        }
+        if (tile >= p.n_tiles) break;
         const FpropTile c = fprop_tile(p, tile);
         const TapPhase& ph = p.ph[c.z];
         const int nk = ph.ntaps * p.cpt;
@@ -366,7 +438,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t it = 0;
       int tc = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; ok && tile < p.n_tiles; tile += gridDim.x, ++tc) {
+      for (uint32_t k = 0; ok; ++k, ++tc) {
+        const int tile = ring_take(tfull, tempty, tring, k, lim);
+        if (tile == kRingTimeout) {
+          report_error(err, YL_DEVERR_TIMEOUT);
+          break;
+        }
+        if (tile >= p.n_tiles) break;
         const int buf = tc & 1, use = tc >> 1;
         if (tc >= 2 && !mbar_wait(&acc_empty[buf], (use - 1) & 1, lim)) {
           report_error(err, YL_DEVERR_TIMEOUT);
@@ -412,7 +490,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     // epilogue: warp w owns TMEM lanes 32w..32w+31 = lattice row 4m + w of subtile m
     int tc = 0;
     uint32_t ost = 0;  // TMA-stored row chunks of this warp (staging buffer = ost & 1)
-    for (int tile = blockIdx.x; tile < p.n_tiles; tile += gridDim.x, ++tc) {
+    for (uint32_t k = 0;; ++k, ++tc) {
+      const int tile = ring_take_warp(tfull, tempty, tring, k, lim, lane);
+      if (tile == kRingTimeout) {
+        report_error(err, YL_DEVERR_TIMEOUT);
+        break;
+      }
+      if (tile >= p.n_tiles) break;
       const int buf = tc & 1, use = tc >> 1;
       const FpropTile c = fprop_tile(p, tile);
       const TapPhase& ph = p.ph[c.z];
@@ -634,6 +718,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     tmem_dealloc(tmem, Cfg::kTmemCols);
   }
+  // the last CTA to finish returns the launch's tile counter to zero (this
+  // CTA's producer took its last tile before the barrier above)
+  if (threadIdx.x == 0 && p.sched) {
+    __threadfence();
+    if (atomicAdd(p.sched + 1, 1) == (int)gridDim.x - 1) {
+      __threadfence();
+      atomicExch(p.sched, 0);
+      atomicExch(p.sched + 1, 0);
+    }
+  }
 }
 
 // ------------------------------------------------------------------ wgrad
@@ -769,11 +863,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0 && nk > 0) {
       const CUtensorMap* amaps[4] = {&ta0, &ta1, &ta2, &ta3};
       const CUtensorMap* bmaps[4] = {&tb0, &tb1, &tb2, &tb3};
+      // k-blocks walk each image in column strips of BKP lattice columns, down
+      // the rows of a strip: the rows a tap row reads again one or two
+      // k-blocks later (and the other column tiles of this pixel range read at
+      // the same time) are still in L2, so every input byte comes from DRAM
+      // about once
       long long r = b_begin;
-      int xb = (int)(r % w.xblocks);
-      r /= w.xblocks;
       int gy = (int)(r % w.gh);
-      int im = (int)(r / w.gh);
+      r /= w.gh;
+      int xb = (int)(r % w.xblocks);
+      int im = (int)(r / w.xblocks);
       const CUtensorMap* amap = amaps[phase];
       WgAtom at[Cfg::kBAtoms];
 #pragma unroll
@@ -804,10 +903,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                         gx0 + at[j].bx, gy + at[j].by, at[j].ci / 32, im);
         }
         ++issued;
-        if (++xb == w.xblocks) {
-          xb = 0;
-          if (++gy == w.gh) {
-            gy = 0;
+        if (++gy == w.gh) {
+          gy = 0;
+          if (++xb == w.xblocks) {
+            xb = 0;
             if (++im == w.n_img) im = 0;
           }
         }
@@ -1185,8 +1284,18 @@ static yl_status launch_plan(yl_ctx* ctx, const View* views, int nviews, const f
   YL_CUDA(cudaFuncSetAttribute(conv_tma_fprop_kernel<BN, MT, TR, HALO>,
                                cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem));
   const int grid = p.n_tiles < ctx->num_sms ? p.n_tiles : ctx->num_sms;
+  p.sched = ctx->sched ? ctx->sched + 2 * (ctx->sched_next++ % kSchedSlots) : nullptr;
   snprintf(ctx->last_kernel[0], sizeof(ctx->last_kernel[0]), "conv_tma_fprop_kernel<%d, %d, %d, %d>",
            BN, MT, (int)TR, (int)HALO);
+  double macs = 0.0;  // as run: every phase's output pixels x its taps x 32-channel chunks
+  for (int z = 0; z < nphase; ++z) {
+    const TapPhase& ph = p.ph[z];
+    const long long rows = std::min(p.gh, (p.out_h - ph.ya + p.ys - 1) / p.ys);
+    const long long cols = std::min(p.gw, (p.out_w - ph.xa + p.xs - 1) / p.xs);
+    if (rows > 0 && cols > 0)
+      macs += (double)p.n_img * rows * cols * ph.ntaps * p.cpt * 32.0 * e.n_total;
+  }
+  ctx->last_exec_flops[0] = 2.0 * macs;
   conv_tma_fprop_kernel<BN, MT, TR, HALO><<<grid, kThreads, kSmem, ctx->stream>>>(
       ta[0], ta[1], ta[2], ta[3], tw, to[0], to[1], to[2], to[3], p, ek, ctx->dev_err);
   YL_TRY(check_launch("conv_tma_fprop_kernel"));
@@ -1549,6 +1658,9 @@ static yl_status launch_wgrad(yl_ctx* ctx, const View* av, int nav, const View* 
   dim3 grid((w.cout + MT * kBM - 1) / (MT * kBM), col_blocks, splits);
   snprintf(ctx->last_kernel[1], sizeof(ctx->last_kernel[1]), "conv_tma_wgrad_kernel<%d, %d, %d, %d>",
            MT, NSUB, NW, BKP);
+  // as run: every lattice pixel against every workspace column (an upsample
+  // conv's four phase GEMMs of 4 merged taps each make 16 taps of columns)
+  ctx->last_exec_flops[1] = 2.0 * w.n_img * w.gh * w.gw * (double)w.cout * w.n_total;
   conv_tma_wgrad_kernel<MT, NSUB, NW, BKP><<<grid, kThreads, Cfg::kSmemBytes, ctx->stream>>>(
       ta[0], ta[1], ta[2], ta[3], tb[0], tb[1], tb[2], tb[3], w, ctx->dev_err);
   return check_launch("conv_tma_wgrad_kernel");

@@ -64,6 +64,13 @@ struct yl_ctx {
   // names of the last conv kernel templates launched on this context:
   // [0] forward / dX, [1] filter gradient (diagnostics, yl_ctx_last_kernel)
   char last_kernel[2][96] = {{0}, {0}};
+  // FLOPs (2 x MACs) those launches executed, padding and merged taps as run
+  double last_exec_flops[2] = {0.0, 0.0};
+  // tile counters of the persistent conv kernels: kSchedSlots pairs (tiles
+  // handed out, CTAs done), zero between launches; consecutive launches take
+  // consecutive pairs so launches in flight together never share one
+  int* sched = nullptr;
+  unsigned sched_next = 0;
   // Scratch slots: 0 = temporaries of one internal kernel sequence (split-K
   // partials, reduction partials); 1 = layout conversions of a C-ABI call.
   // slot 0: operator temporaries; 1: NCHW<->NHWC staging of the batched
@@ -73,6 +80,8 @@ struct yl_ctx {
 };
 
 namespace yl {
+constexpr int kSchedSlots = 64;
+
 // Returns a device buffer of at least `bytes` from scratch slot `slot`,
 // valid for work queued on ctx->stream until the next call on the same slot.
 // Grows with cudaMallocAsync/cudaFreeAsync (stream-ordered, so a buffer

@@ -678,28 +678,42 @@ void Net::prof_end(int cls, double flops, double bytes) {
   cudaEventRecord(pe.b, ctx->stream);
   pe.flops = flops;
   pe.bytes = bytes;
-  (void)cls;
+  if (cls <= 2) {  // a conv class: the template the bracket launched (2: filter gradient)
+    const int which = cls == 2 ? 1 : 0;
+    std::memcpy(pe.kname, ctx->last_kernel[which], sizeof(pe.kname));
+    pe.exec = ctx->last_exec_flops[which];
+  }
   done.push_back(pe);
   pending.pop_back();
 }
 void Net::prof_mark_dominant() {
   if (profiling && !pending.empty()) pending.back().cls2 = kProfDominant;
 }
-yl_status Net::prof_collect(double* ms, double* flops, double* bytes, int* launches) {
+yl_status Net::prof_collect(double* ms, double* flops, double* bytes, int* launches,
+                            double* exec, std::map<std::string, TemplateStat>* templates) {
   if (done.empty()) return YL_OK;
   YL_CUDA(cudaStreamSynchronize(ctx->stream));
   for (auto& pe : done) {
     float t = 0.f;
     YL_CUDA(cudaEventElapsedTime(&t, pe.a, pe.b));
+    if (templates && pe.kname[0]) {
+      TemplateStat& ts = (*templates)[pe.kname];
+      ts.ms += t;
+      ts.flops += pe.flops;
+      ts.exec += pe.exec;
+      ts.launches += 1;
+    }
     ms[pe.cls] += t;
     flops[pe.cls] += pe.flops;
     bytes[pe.cls] += pe.bytes;
     launches[pe.cls] += 1;
+    exec[pe.cls] += pe.exec;
     if (pe.cls2 >= 0) {
       ms[pe.cls2] += t;
       flops[pe.cls2] += pe.flops;
       bytes[pe.cls2] += pe.bytes;
       launches[pe.cls2] += 1;
+      exec[pe.cls2] += pe.exec;
     }
     cudaEventDestroy(pe.a);
     cudaEventDestroy(pe.b);

@@ -3,6 +3,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <map>
 #include <string>
 #include <vector>
 
@@ -56,6 +57,12 @@ struct ParamEntry {
 };
 
 struct Net;
+
+// Profiled time and work of one conv kernel template over the profiled steps.
+struct TemplateStat {
+  double ms = 0.0, flops = 0.0, exec = 0.0;
+  int launches = 0;
+};
 
 struct ConvL {
   std::string name;
@@ -157,6 +164,8 @@ struct Net {
     cudaEvent_t a, b;
     int cls, cls2 = -1;  // cls2: a second class the launch also counts in
     double flops, bytes;
+    double exec = 0.0;      // FLOPs the conv kernel executed (conv classes)
+    char kname[96] = {0};  // the conv kernel template the bracket launched
   };
   std::vector<ProfEvent> pending, done;
   std::vector<PermuteJob> perm_first, perm_second;
@@ -169,7 +178,8 @@ struct Net {
   void prof_end(int cls, double flops, double bytes = 0.0);
   // the open event also counts in class 5 (call between prof_begin and prof_end)
   void prof_mark_dominant();
-  yl_status prof_collect(double* ms, double* flops, double* bytes, int* launches);
+  yl_status prof_collect(double* ms, double* flops, double* bytes, int* launches, double* exec,
+                         std::map<std::string, TemplateStat>* templates = nullptr);
   void grads_ready(size_t lo);
   yl_status prepare_weights();
 };

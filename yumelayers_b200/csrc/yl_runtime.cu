@@ -86,6 +86,8 @@ yl_status yl_ctx_create(int device, yl_ctx** out) {
   YL_CUDA(cudaEventCreate(&c->ev_end));
   YL_CUDA(cudaMalloc(&c->dev_err, 16));
   YL_CUDA(cudaMemset(c->dev_err, 0, 16));
+  YL_CUDA(cudaMalloc(&c->sched, sizeof(int) * 2 * kSchedSlots));
+  YL_CUDA(cudaMemset(c->sched, 0, sizeof(int) * 2 * kSchedSlots));
   *out = c;
   return YL_OK;
 }
@@ -98,6 +100,7 @@ yl_status yl_ctx_destroy(yl_ctx* ctx) {
     if (ctx->scratch[s]) cudaFreeAsync(ctx->scratch[s], ctx->stream);
   cudaStreamSynchronize(ctx->stream);
   cudaFree(ctx->dev_err);
+  cudaFree(ctx->sched);
   cudaEventDestroy(ctx->ev_begin);
   cudaEventDestroy(ctx->ev_end);
   cudaStreamDestroy(ctx->own_stream);

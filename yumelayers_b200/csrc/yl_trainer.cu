@@ -17,7 +17,9 @@
 #include <algorithm>
 #include <cmath>
 #include <cstring>
+#include <map>
 #include <memory>
+#include <string>
 #include <vector>
 
 #include "yl_nets.h"
@@ -108,6 +110,9 @@ struct yl_trainer {
   int64_t step = 0;
   double prof_ms[kProfClasses] = {}, prof_flops[kProfClasses] = {}, prof_bytes[kProfClasses] = {};
   int prof_launches[kProfClasses] = {};
+  double prof_exec[kProfClasses] = {};
+  std::map<std::string, TemplateStat> prof_templates;
+  std::map<std::string, TemplateStat> last_templates;  // as of the last kernel_stats call
 };
 
 extern "C" {
@@ -479,19 +484,45 @@ yl_status yl_trainer_kernel_stats(yl_trainer* tr, yl_kernel_stats* out, int rese
   YL_CHECK(tr && out, YL_ERR_INVALID, "yl_trainer_kernel_stats: NULL argument");
   // events of the profiled steps are read here, after the fact, so profiling
   // adds no synchronisation inside a step
-  YL_TRY(tr->vae->prof_collect(tr->prof_ms, tr->prof_flops, tr->prof_bytes, tr->prof_launches));
-  YL_TRY(tr->unet->prof_collect(tr->prof_ms, tr->prof_flops, tr->prof_bytes, tr->prof_launches));
+  YL_TRY(tr->vae->prof_collect(tr->prof_ms, tr->prof_flops, tr->prof_bytes, tr->prof_launches,
+                               tr->prof_exec, &tr->prof_templates));
+  YL_TRY(tr->unet->prof_collect(tr->prof_ms, tr->prof_flops, tr->prof_bytes, tr->prof_launches,
+                                tr->prof_exec, &tr->prof_templates));
   for (int i = 0; i < kProfClasses && i < YL_KERNEL_CLASSES; ++i) {
     out->ms[i] = tr->prof_ms[i];
     out->flops[i] = tr->prof_flops[i];
     out->bytes[i] = tr->prof_bytes[i];
     out->launches[i] = tr->prof_launches[i];
+    out->exec_flops[i] = tr->prof_exec[i];
   }
   if (reset) {
     std::memset(tr->prof_ms, 0, sizeof(tr->prof_ms));
     std::memset(tr->prof_flops, 0, sizeof(tr->prof_flops));
     std::memset(tr->prof_bytes, 0, sizeof(tr->prof_bytes));
     std::memset(tr->prof_launches, 0, sizeof(tr->prof_launches));
+    std::memset(tr->prof_exec, 0, sizeof(tr->prof_exec));
+    tr->last_templates = std::move(tr->prof_templates);
+    tr->prof_templates.clear();
+  } else {
+    tr->last_templates = tr->prof_templates;
+  }
+  return YL_OK;
+}
+
+yl_status yl_trainer_template_stats(yl_trainer* tr, yl_template_stats* out, int capacity,
+                                    int* count) {
+  YL_CHECK(tr && count, YL_ERR_INVALID, "yl_trainer_template_stats: NULL argument");
+  *count = (int)tr->last_templates.size();
+  int i = 0;
+  for (const auto& kv : tr->last_templates) {
+    if (!out || i >= capacity) break;
+    yl_template_stats& o = out[i++];
+    std::memset(o.name, 0, sizeof(o.name));
+    std::strncpy(o.name, kv.first.c_str(), sizeof(o.name) - 1);
+    o.ms = kv.second.ms;
+    o.flops = kv.second.flops;
+    o.exec_flops = kv.second.exec;
+    o.launches = kv.second.launches;
   }
   return YL_OK;
 }

@@ -12,7 +12,7 @@ from dataclasses import dataclass
 
 import numpy as np
 
-from ._lib import KernelStats, TrainerConfig, YumeError, call, lib
+from ._lib import KernelStats, TemplateStats, TrainerConfig, YumeError, call, lib
 from .session import Context
 
 
@@ -205,7 +205,19 @@ class Trainer:
         st = KernelStats()
         call("yl_trainer_kernel_stats", self.handle, C.byref(st), int(reset))
         return {CLASS_NAMES[i]: {"ms": st.ms[i], "flops": st.flops[i], "bytes": st.bytes[i],
-                                 "launches": st.launches[i]} for i in range(len(CLASS_NAMES))}
+                                 "launches": st.launches[i], "exec_flops": st.exec_flops[i]}
+                for i in range(len(CLASS_NAMES))}
+
+    def template_stats(self) -> dict:
+        """Profiled conv brackets per kernel template, as of the last kernel_stats
+        call: ms, algorithmic flops, executed flops, launches."""
+        n = C.c_int()
+        call("yl_trainer_template_stats", self.handle, None, 0, C.byref(n))
+        arr = (TemplateStats * max(n.value, 1))()
+        call("yl_trainer_template_stats", self.handle, arr, n.value, C.byref(n))
+        return {arr[i].name.decode(): {"ms": arr[i].ms, "flops": arr[i].flops,
+                                       "exec_flops": arr[i].exec_flops,
+                                       "launches": arr[i].launches} for i in range(n.value)}
 
     def activation_bytes(self) -> int:
         b = C.c_size_t()
