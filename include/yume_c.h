@@ -248,9 +248,10 @@ yl_status yl_groupnorm_silu_fwd(yl_ctx* ctx, const float* x, int n, int c, int h
  * (n * chunks * 2 * groups doubles, chunks <= 592/n + 1); larger requests
  * return YL_ERR_SHAPE without launching.  NHWC layout only; mean_out and
  * rstd_out (n*groups) are required.  The first call on each device looks the
- * array up (cudaGetSymbolAddress) and must come before any stream capture.
- * Nothing needs to start at zero.  Calls that overlap on one device share
- * the array and race: serialise them. */
+ * array up (cudaGetSymbolAddress) and must come before any stream capture;
+ * the address is kept for the life of the process, so a cudaDeviceReset of
+ * that device is not supported afterwards.  Nothing needs to start at zero.
+ * Calls that overlap on one device share the array and race: serialise them. */
 yl_status yl_groupnorm_silu_fwd_noalloc(yl_ctx* ctx, const float* x, int n, int c, int h, int w,
                                         int groups, float eps, int mode, const float* gamma,
                                         const float* beta, int apply_silu, float* y,

@@ -1,12 +1,14 @@
 """yl_groupnorm_silu_fwd_noalloc (statistics partials in a fixed array inside
 the library) against yl_groupnorm_silu_fwd on the same NHWC inputs, twice in
-a row, plus its size limit.  Collected last so that it also runs after every
-other GPU test has used the context."""
+a row, and against the oracle's GroupNorm + SiLU, plus its size limit.
+Collected last so that it also runs after every other GPU test has used the
+context."""
 import ctypes as C
 
 import numpy as np
 import pytest
 
+from oracle_lib import gn_silu_fwd
 from yumelayers_b200._lib import LAYOUT_NHWC, call, lib
 from yumelayers_b200.session import GPUTensor
 
@@ -26,7 +28,7 @@ def _rel(a, b):
 
 @pytest.mark.parametrize("n,c,h,w,g", [(2, 128, 24, 20, 32), (8, 256, 30, 54, 32),
                                        (1, 64, 7, 9, 16)])
-def test_noalloc_matches_allocating_entry_point_twice(ctx, n, c, h, w, g):
+def test_noalloc_matches_allocating_entry_point_twice(ctx, oracle, n, c, h, w, g):
     rng = np.random.default_rng(5)
     x = (rng.standard_normal((n, h, w, c)) * 1.3 + 0.2).astype(np.float32)
     ga = (1 + 0.02 * rng.standard_normal(c)).astype(np.float32)
@@ -46,6 +48,9 @@ def test_noalloc_matches_allocating_entry_point_twice(ctx, n, c, h, w, g):
         got = (y.toArray()[: x.size], m.toArray()[: n * g], r.toArray()[: n * g])
         for a, b in zip(got, want):
             assert _rel(a, b) < TOL
+    # and against the oracle's GroupNorm + SiLU (double statistics) directly
+    ref_y, _, _ = gn_silu_fwd(oracle, x.transpose(0, 3, 1, 2), g, 1e-6, ga, be)
+    assert _rel(got[0].reshape(n, h, w, c).transpose(0, 3, 1, 2), ref_y) < 1e-5
 
 
 def test_noalloc_rejects_requests_above_its_fixed_scratch(ctx):

@@ -540,7 +540,9 @@ yl_status gn_silu_backward(yl_ctx* ctx, const float* x, const float* dy, int ldd
 //    the caller provides mean_out / rstd_out (no other temporaries exist);
 //  * the first call on each device looks the array up with
 //    cudaGetSymbolAddress (which may load the library's device code), so make
-//    one call on every device before recording the calls into a graph;
+//    one call on every device before any stream capture; the address is
+//    cached for the life of the process (a cudaDeviceReset of the device
+//    afterwards is not supported: it would leave the cached address stale);
 //  * nothing has to start at zero: each call overwrites every partial it
 //    reads;
 //  * one array per device: calls that overlap on the same device (two
