@@ -65,23 +65,37 @@ def test_joint_step_losses_match_oracle_100_steps():
     tr.close()
 
 
-def test_free_running_trajectories_stay_close():
-    """Without re-syncing, the two trajectories drift apart only slowly (Adam's
-    first steps move every weight by ~lr with the sign of its gradient, so
-    weights whose gradient is ~0 may step either way on either side)."""
+def test_free_running_trajectories_100_steps():
+    """100 joint steps on each side with no re-sync.
+
+    A per-step bound cannot hold here for any arithmetic that is not
+    bit-identical to the oracle's: Adam's first steps move every weight by
+    about lr with the sign of its gradient, so a weight whose gradient is near
+    zero steps either way on either side, and the difference grows by about
+    15% per step.  Two oracle runs whose only difference is the fp32 summation
+    order of the filter gradients (1e-8 apart after one step) are 2e-2 apart
+    in loss by step 100.  What this test holds the free-running GPU trajectory
+    to: the first step within the per-step bound (same weights), finite losses
+    throughout, final weights within 5e-2 relative L2 of the oracle's, and the
+    mean loss over the last 20 steps within 25% (both sides train alike)."""
     tr, js, batches = _setup()
-    worst = 0.0
-    for step in range(6):
+    gpu_l, cpu_l = [], []
+    for step in range(100):
         frames, t = batches[step % len(batches)]
-        gpu = tr.step_host(frames, t)
-        cpu = js.step(frames, t)
-        worst = max(worst, *[abs(g - c) / abs(c) for g, c in zip(gpu, cpu)])
-    assert worst < 5e-3, worst
+        gpu_l.append(tr.step_host(frames, t))
+        cpu_l.append(js.step(frames, t))
+    gpu_l, cpu_l = np.array(gpu_l, np.float64), np.array(cpu_l, np.float64)
+    assert np.isfinite(gpu_l).all() and np.isfinite(cpu_l).all()
+    first = np.abs(gpu_l[0] - cpu_l[0]) / np.abs(cpu_l[0])
+    assert first.max() < LOSS_TOL, first
+    tail_gpu, tail_cpu = gpu_l[-20:].mean(axis=0), cpu_l[-20:].mean(axis=0)
+    tail = np.abs(tail_gpu - tail_cpu) / tail_cpu
+    assert tail.max() < 0.25, (tail_gpu, tail_cpu)
     for which in (0, 1):
         got = tr.download(which)
         ref = js.flat[which]
         diff = np.linalg.norm(got - ref) / np.linalg.norm(ref)
-        assert diff < 1e-2, (which, diff)
+        assert diff < 5e-2, (which, diff)
     tr.close()
 
 
