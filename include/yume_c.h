@@ -343,7 +343,15 @@ yl_status yl_layered_compose(yl_ctx* ctx, const float* recon, int n, long long p
  * closest relative is the per-frame gradient sum, TrainConvVAE.swift:177-217). */
 #define YL_COMM_ID_BYTES 128
 yl_status yl_comm_get_unique_id(uint8_t* out_id /* YL_COMM_ID_BYTES */);
+/* The communicator is non-blocking: set-up and every collective that NCCL
+ * finishes on its own threads are waited for with a deadline (300 s for
+ * yl_comm_init; timeout_s for yl_comm_init_timeout), and a rank that never
+ * joins makes the call return YL_ERR_TIMEOUT instead of blocking for good.
+ * NCCL may use at most 8 CTAs per collective (YL_NCCL_MAX_CTAS in the
+ * environment overrides it; 0 keeps NCCL's default). */
 yl_status yl_comm_init(yl_ctx* ctx, const uint8_t* id, int rank, int world, yl_comm** out);
+yl_status yl_comm_init_timeout(yl_ctx* ctx, const uint8_t* id, int rank, int world,
+                               double timeout_s, yl_comm** out);
 yl_status yl_comm_destroy(yl_comm* comm);
 /* Aborts outstanding collectives (failure handling); destroy afterwards. */
 yl_status yl_comm_abort(yl_comm* comm);

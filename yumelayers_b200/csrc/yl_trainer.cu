@@ -15,8 +15,11 @@
 #include <nccl.h>
 
 #include <algorithm>
+#include <chrono>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
+#include <thread>
 #include <map>
 #include <memory>
 #include <string>
@@ -42,6 +45,51 @@ struct yl_comm {
 };
 
 namespace {
+
+// Communicators are created non-blocking: every NCCL call may return
+// ncclInProgress while NCCL finishes it on its own threads (communicator
+// set-up, the connections of a first collective).  The call's outcome is then
+// polled from ncclCommGetAsyncError with a deadline, so a peer that never
+// joins ends in a status instead of a host thread blocked for good.
+constexpr double kNcclCallTimeoutS = 300.0;
+
+ncclResult_t nccl_settle(ncclComm_t comm, ncclResult_t r, double timeout_s) {
+  if (r != ncclInProgress) return r;
+  const auto t0 = std::chrono::steady_clock::now();
+  for (;;) {
+    ncclResult_t st = ncclSuccess;
+    const ncclResult_t q = ncclCommGetAsyncError(comm, &st);
+    if (q != ncclSuccess) return q;
+    if (st != ncclInProgress) return st;
+    const double el = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+    if (el > timeout_s) return ncclInProgress;
+    std::this_thread::sleep_for(std::chrono::microseconds(100));
+  }
+}
+
+ncclResult_t all_reduce_sum(yl_comm* c, float* buf, size_t n, cudaStream_t stream) {
+  return nccl_settle(c->comm,
+                     ncclAllReduce(buf, buf, n, ncclFloat, ncclSum, c->comm, stream),
+                     kNcclCallTimeoutS);
+}
+
+yl_status nccl_status(ncclResult_t r, const char* what) {
+  if (r == ncclSuccess) return YL_OK;
+  if (r == ncclInProgress)
+    return set_error(YL_ERR_TIMEOUT, "%s: NCCL still in progress after %.0f s", what,
+                     kNcclCallTimeoutS);
+  return set_error(YL_ERR_NCCL, "%s: %s", what, ncclGetErrorString(r));
+}
+
+// CTAs NCCL may use per collective: the gradient all-reduce runs beside the
+// persistent conv kernels (one CTA per SM) and is hidden behind backward, so
+// a few CTAs carry its bytes in time while leaving the SMs to the convs.
+// YL_NCCL_MAX_CTAS overrides it (0: NCCL's default).
+int nccl_max_ctas() {
+  const char* e = std::getenv("YL_NCCL_MAX_CTAS");
+  if (e && *e) return std::max(0, std::atoi(e));
+  return 8;
+}
 
 struct Bucket {
   size_t lo, hi;
@@ -82,10 +130,10 @@ void launch_ready(Overlap* ov, Net* net, size_t lo) {
       ov->status = set_error(YL_ERR_CUDA, "bucket event: %s", cudaGetErrorString(e));
       return;
     }
-    ncclResult_t r = ncclAllReduce(net->params.g + b.lo, net->params.g + b.lo, b.hi - b.lo,
-                                   ncclFloat, ncclSum, ov->comm->comm, ov->comm->stream);
+    const ncclResult_t r =
+        all_reduce_sum(ov->comm, net->params.g + b.lo, b.hi - b.lo, ov->comm->stream);
     if (r != ncclSuccess) {
-      ov->status = set_error(YL_ERR_NCCL, "ncclAllReduce: %s", ncclGetErrorString(r));
+      ov->status = nccl_status(r, "gradient bucket all-reduce");
       return;
     }
     b.launched = true;
@@ -127,7 +175,13 @@ yl_status yl_comm_get_unique_id(uint8_t* out) {
 }
 
 yl_status yl_comm_init(yl_ctx* ctx, const uint8_t* id_bytes, int rank, int world, yl_comm** out) {
-  YL_CHECK(ctx && id_bytes && out, YL_ERR_INVALID, "yl_comm_init: NULL argument");
+  return yl_comm_init_timeout(ctx, id_bytes, rank, world, kNcclCallTimeoutS, out);
+}
+
+yl_status yl_comm_init_timeout(yl_ctx* ctx, const uint8_t* id_bytes, int rank, int world,
+                               double timeout_s, yl_comm** out) {
+  YL_CHECK(ctx && id_bytes && out && timeout_s > 0, YL_ERR_INVALID,
+           "yl_comm_init: NULL argument or non-positive timeout");
   YL_CHECK(world >= 1 && rank >= 0 && rank < world, YL_ERR_INVALID, "yl_comm_init: rank %d of %d",
            rank, world);
   YL_CUDA(cudaSetDevice(ctx->device));
@@ -137,10 +191,23 @@ yl_status yl_comm_init(yl_ctx* ctx, const uint8_t* id_bytes, int rank, int world
   c->device = ctx->device;
   ncclUniqueId id;
   std::memcpy(&id, id_bytes, sizeof(id));
-  ncclResult_t r = ncclCommInitRank(&c->comm, world, id, rank);
+  ncclConfig_t config = NCCL_CONFIG_INITIALIZER;
+  config.blocking = 0;
+  const int max_ctas = nccl_max_ctas();
+  if (max_ctas > 0) {
+    config.minCTAs = 1;
+    config.maxCTAs = max_ctas;
+  }
+  ncclResult_t r = ncclCommInitRankConfig(&c->comm, world, id, rank, &config);
+  if (c->comm) r = nccl_settle(c->comm, r, timeout_s);
   if (r != ncclSuccess) {
+    if (c->comm) ncclCommAbort(c->comm);  // also ends the set-up threads of a timed-out init
     delete c;
-    return set_error(YL_ERR_NCCL, "ncclCommInitRank: %s", ncclGetErrorString(r));
+    if (r == ncclInProgress)
+      return set_error(YL_ERR_TIMEOUT,
+                       "ncclCommInitRankConfig: rank %d of %d: not every rank joined in %.1f s",
+                       rank, world, timeout_s);
+    return set_error(YL_ERR_NCCL, "ncclCommInitRankConfig: %s", ncclGetErrorString(r));
   }
   int lo = 0, hi = 0;
   cudaDeviceGetStreamPriorityRange(&lo, &hi);
@@ -154,7 +221,13 @@ yl_status yl_comm_init(yl_ctx* ctx, const uint8_t* id_bytes, int rank, int world
 yl_status yl_comm_destroy(yl_comm* c) {
   if (!c) return YL_OK;
   if (c->stream) cudaStreamSynchronize(c->stream);
-  if (c->comm) ncclCommDestroy(c->comm);
+  if (c->comm) {
+    // a non-blocking communicator: finalize (bounded), then free; abort if a
+    // peer never finishes its side
+    const ncclResult_t r = nccl_settle(c->comm, ncclCommFinalize(c->comm), kNcclCallTimeoutS);
+    if (r == ncclSuccess) ncclCommDestroy(c->comm);
+    else ncclCommAbort(c->comm);
+  }
   if (c->stream) cudaStreamDestroy(c->stream);
   delete c;
   return YL_OK;
@@ -170,8 +243,8 @@ yl_status yl_comm_abort(yl_comm* c) {
 yl_status yl_allreduce_sum(yl_comm* c, float* buf, size_t n, void* stream) {
   YL_CHECK(c && buf, YL_ERR_INVALID, "yl_allreduce_sum: NULL argument");
   YL_CHECK(c->comm, YL_ERR_NCCL, "yl_allreduce_sum: communicator was aborted");
-  YL_NCCL(ncclAllReduce(buf, buf, n, ncclFloat, ncclSum, c->comm,
-                        stream ? (cudaStream_t)stream : c->stream));
+  YL_TRY(nccl_status(all_reduce_sum(c, buf, n, stream ? (cudaStream_t)stream : c->stream),
+                     "yl_allreduce_sum"));
   return YL_OK;
 }
 
@@ -265,6 +338,17 @@ yl_status yl_trainer_step(yl_trainer* tr, const float* frames, const float* t, f
     YL_TRY(vae.encode());
     YL_TRY(copy_mu(ctx, vae.e, tr->zb, VAE::kLatent));
   }
+  // the motion net's forward + backward; its gradient buckets go to the
+  // communication stream as its backward frontier passes them
+  auto motion_step = [&]() -> yl_status {
+    YL_TRY(unet.set_inputs(tr->za, tr->zb, VAE::kLatent, t));
+    YL_TRY(unet.forward());
+    YL_TRY(mse_head(ctx, unet.pred.p, unet.target.p, unet.pred.pixels(), unet.pred.ld,
+                    UNet::kLat, unet.dpred.p, tr->losses + 1));
+    YL_TRY(unet.backward());
+    launch_ready(&tr->ov_unet, &unet, 0);
+    return tr->ov_unet.status;
+  };
   YL_TRY(frames_to_nhwc4(ctx, frames + 2 * set, B, H, W, vae.x_in.p, 1));
   if (train_vae) {
     // the reconstruction target keeps the frame's fp32 values
@@ -272,30 +356,28 @@ yl_status yl_trainer_step(yl_trainer* tr, const float* frames, const float* t, f
     YL_TRY(vae.forward_train(tr->step));
     YL_TRY(l1_kl_head(ctx, vae.recon.p, vae.x_tgt.p, vae.recon.pixels(), 4, 3, vae.e.p, vae.e.ld,
                       vae.e.pixels(), VAE::kLatent, tr->cfg.beta_kl, vae.drecon.p, tr->losses));
-    if (train_motion) YL_TRY(copy_mu(ctx, vae.e, unet.target.p, VAE::kLatent));
+    if (train_motion) {
+      // the motion step needs only the encoder mean of frame k: it runs before
+      // the VAE backward, so its whole gradient all-reduce hides behind that
+      // backward and only the VAE's last bucket is left after the compute
+      YL_TRY(copy_mu(ctx, vae.e, unet.target.p, VAE::kLatent));
+      YL_TRY(motion_step());
+    }
     YL_TRY(vae.backward(tr->step, tr->cfg.beta_kl));
     launch_ready(&tr->ov_vae, &vae, 0);
     YL_TRY(tr->ov_vae.status);
   } else if (train_motion) {
     YL_TRY(vae.encode());
     YL_TRY(copy_mu(ctx, vae.e, unet.target.p, VAE::kLatent));
-  }
-  if (train_motion) {
-    YL_TRY(unet.set_inputs(tr->za, tr->zb, VAE::kLatent, t));
-    YL_TRY(unet.forward());
-    YL_TRY(mse_head(ctx, unet.pred.p, unet.target.p, unet.pred.pixels(), unet.pred.ld,
-                    UNet::kLat, unet.dpred.p, tr->losses + 1));
-    YL_TRY(unet.backward());
-    launch_ready(&tr->ov_unet, &unet, 0);
-    YL_TRY(tr->ov_unet.status);
+    YL_TRY(motion_step());
   }
   float scale = 1.f;
   if (tr->comm && tr->comm->world > 1) {
     // the step's loss values are averaged across ranks too (after all queued work)
     YL_CUDA(cudaEventRecord(tr->ov_vae.ready_ev, ctx->stream));
     YL_CUDA(cudaStreamWaitEvent(tr->comm->stream, tr->ov_vae.ready_ev, 0));
-    YL_NCCL(ncclAllReduce(tr->losses, tr->losses, 2, ncclFloat, ncclSum, tr->comm->comm,
-                          tr->comm->stream));
+    YL_TRY(nccl_status(all_reduce_sum(tr->comm, tr->losses, 2, tr->comm->stream),
+                       "loss all-reduce"));
     YL_CUDA(cudaEventRecord(tr->comm_done, tr->comm->stream));
     YL_CUDA(cudaStreamWaitEvent(ctx->stream, tr->comm_done, 0));
     scale = 1.f / (float)tr->comm->world;

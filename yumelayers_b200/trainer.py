@@ -43,11 +43,12 @@ class ParamEntry:
 class Comm:
     """The library's NCCL communicator for one rank."""
 
-    def __init__(self, ctx: Context, id_bytes: bytes, rank: int, world: int):
+    def __init__(self, ctx: Context, id_bytes: bytes, rank: int, world: int,
+                 timeout_s: float = 300.0):
         _bind()
         h = C.c_void_p()
         buf = (C.c_uint8 * 128).from_buffer_copy(id_bytes)
-        call("yl_comm_init", ctx.handle, buf, rank, world, C.byref(h))
+        call("yl_comm_init_timeout", ctx.handle, buf, rank, world, float(timeout_s), C.byref(h))
         self.handle, self.rank, self.world = h, rank, world
 
     @staticmethod
