@@ -55,3 +55,17 @@ def test_sobel_nhwc_with_pixel_stride(oracle, ctx):
     np.testing.assert_allclose(ld.toArray()[:n], lref, rtol=1e-5)
     g = gd.toArray()[: n * h * w * 4].reshape(n, h, w, 4)[..., :3].transpose(0, 3, 1, 2)
     assert rel_l2(g, gref) < 1e-5
+
+
+@pytest.mark.parametrize("n,h,w", [(2, 100, 150), (1, 480, 856), (1, 3, 3), (1, 16, 64)])
+def test_sobel_tiles_and_edges_match_oracle(oracle, n, h, w):
+    """Several 64 x 16 tiles with ragged last tiles, the frame size, the
+    smallest image with an interior pixel, and exactly one tile."""
+    from yumelayers_b200 import ops
+    rng = np.random.default_rng(h * 1000 + w)
+    r = f32(rng.uniform(0, 1, (n, 3, h, w)))
+    t = f32(np.clip(r + 0.1 * rng.standard_normal((n, 3, h, w)), 0, 1))
+    loss, grad = ops.sobel_edge_loss(r, t)
+    lref, gref = _oracle(oracle, r, t)
+    np.testing.assert_allclose(loss, lref, rtol=1e-5)
+    assert rel_l2(grad, gref) < 1e-5

@@ -524,80 +524,88 @@ struct ImgView {  // channel c of pixel p of image i: base + i*istride + p*pstri
   }
 };
 
-__constant__ float kSobelX[9] = {-1.f, 0.f, 1.f, -2.f, 0.f, 2.f, -1.f, 0.f, 1.f};
-__constant__ float kSobelY[9] = {-1.f, -2.f, -1.f, 0.f, 0.f, 0.f, 1.f, 2.f, 1.f};
+// One pass per 64 x 16 tile of output pixels: the luma of both images over
+// the tile and a 2-pixel halo goes to shared memory once; each pixel of the
+// tile and a 1-pixel ring gets its two Sobel magnitudes there, its share of
+// the loss, and the coefficients its window hands back to the pixels under
+// it; the tile's gradient then sums the 3x3 neighbours' coefficients.
+// Global traffic: read both images once (halo re-reads hit L1/L2) and write
+// the gradient -- 36 bytes per RGB pixel.
+constexpr int kSobTW = 64, kSobTH = 16;
 
-// maps[img][5][hw]: |grad R|, |grad T|, sx(R), sy(R), 1/|grad R| (0 at the border)
-__global__ void sobel_map_kernel(ImgView r, ImgView t, int h, int w, float* __restrict__ maps) {
-  const long long hw = (long long)h * w;
-  const int img = blockIdx.y;
-  for (long long p = blockIdx.x * (long long)blockDim.x + threadIdx.x; p < hw;
-       p += (long long)gridDim.x * blockDim.x) {
-    float* m = maps + (long long)img * 5 * hw + p;
-    const int y = (int)(p / w), x = (int)(p % w);
-    if (y < 1 || y >= h - 1 || x < 1 || x >= w - 1) {
-      m[0] = m[hw] = m[2 * hw] = m[3 * hw] = m[4 * hw] = 0.f;
-      continue;
-    }
-    float sxr = 0.f, syr = 0.f, sxt = 0.f, syt = 0.f;
-    int k = 0;
-    for (int dy = -1; dy <= 1; ++dy)
-      for (int dx = -1; dx <= 1; ++dx, ++k) {
-        const long long q = (long long)(y + dy) * w + (x + dx);
-        const float lr = 0.2126f * r.at(img, q, 0) + 0.7152f * r.at(img, q, 1) +
-                         0.0722f * r.at(img, q, 2);
-        const float lt = 0.2126f * t.at(img, q, 0) + 0.7152f * t.at(img, q, 1) +
-                         0.0722f * t.at(img, q, 2);
-        sxr += kSobelX[k] * lr;
-        syr += kSobelY[k] * lr;
-        sxt += kSobelX[k] * lt;
-        syt += kSobelY[k] * lt;
-      }
-    const float mr = sqrtf(sxr * sxr + syr * syr), mt = sqrtf(sxt * sxt + syt * syt);
-    m[0] = mr;
-    m[hw] = mt;
-    m[2 * hw] = sxr;
-    m[3 * hw] = syr;
-    m[4 * hw] = mr > 1e-6f ? 1.f / mr : 0.f;
-  }
+__device__ __forceinline__ float luma_at(const ImgView& v, long long img, long long q) {
+  return 0.2126f * v.at(img, q, 0) + 0.7152f * v.at(img, q, 1) + 0.0722f * v.at(img, q, 2);
 }
 
-// Gradient of each pixel from the windows of its 3x3 neighbours, and block
-// partial sums of (|grad R| - |grad T|)^2 (fixed order: part[img][block]).
-__global__ void sobel_grad_kernel(const float* __restrict__ maps, int h, int w, float scale,
-                                  float* grad, long long gi, long long gp, long long gc,
-                                  double* __restrict__ part) {
+__global__ void __launch_bounds__(256)
+    sobel_tile_kernel(ImgView r, ImgView t, int h, int w, int tiles_x, float scale, float* grad,
+                      long long gi, long long gp, long long gc, double* __restrict__ part) {
+  __shared__ float lr[kSobTH + 4][kSobTW + 4], lt[kSobTH + 4][kSobTW + 4];
+  __shared__ float ax[kSobTH + 2][kSobTW + 2], ay[kSobTH + 2][kSobTW + 2];
   __shared__ double red[256];
-  const long long hw = (long long)h * w;
+  // Sobel taps, row by row (dy = -1..1, dx = -1..1)
+  const float KX[9] = {-1.f, 0.f, 1.f, -2.f, 0.f, 2.f, -1.f, 0.f, 1.f};
+  const float KY[9] = {-1.f, -2.f, -1.f, 0.f, 0.f, 0.f, 1.f, 2.f, 1.f};
   const int img = blockIdx.y;
-  const float* eR = maps + (long long)img * 5 * hw;
-  const float *eT = eR + hw, *gx = eR + 2 * hw, *gy = eR + 3 * hw, *inv = eR + 4 * hw;
+  const int x0 = (blockIdx.x % tiles_x) * kSobTW, y0 = (blockIdx.x / tiles_x) * kSobTH;
+  for (int i = threadIdx.x; i < (kSobTH + 4) * (kSobTW + 4); i += blockDim.x) {
+    const int yy = i / (kSobTW + 4), xx = i % (kSobTW + 4);
+    const int y = y0 - 2 + yy, x = x0 - 2 + xx;
+    float a = 0.f, b = 0.f;
+    if (y >= 0 && y < h && x >= 0 && x < w) {
+      const long long q = (long long)y * w + x;
+      a = luma_at(r, img, q);
+      b = luma_at(t, img, q);
+    }
+    lr[yy][xx] = a;
+    lt[yy][xx] = b;
+  }
+  __syncthreads();
   double acc = 0.0;
-  for (long long p = blockIdx.x * (long long)blockDim.x + threadIdx.x; p < hw;
-       p += (long long)gridDim.x * blockDim.x) {
-    const float d0 = eR[p] - eT[p];
-    acc += (double)d0 * d0;
-    if (!grad) continue;
-    const int py = (int)(p / w), px = (int)(p % w);
-    float a0 = 0.f, a1 = 0.f, a2 = 0.f;
-    for (int dy = -1; dy <= 1; ++dy)
-      for (int dx = -1; dx <= 1; ++dx) {
-        const int qy = py + dy, qx = px + dx;
-        if (qy < 1 || qy >= h - 1 || qx < 1 || qx >= w - 1) continue;
-        const long long q = (long long)qy * w + qx;
-        const float diff = eR[q] - eT[q];
-        if (diff == 0.f) continue;
-        const float dX = diff * inv[q] * scale * gx[q], dY = diff * inv[q] * scale * gy[q];
-        const int k = (1 - dy) * 3 + (1 - dx);
-        const float c = dX * kSobelX[k] + dY * kSobelY[k];
-        a0 += c * 0.2126f;
-        a1 += c * 0.7152f;
-        a2 += c * 0.0722f;
+  for (int i = threadIdx.x; i < (kSobTH + 2) * (kSobTW + 2); i += blockDim.x) {
+    const int yy = i / (kSobTW + 2), xx = i % (kSobTW + 2);
+    const int y = y0 - 1 + yy, x = x0 - 1 + xx;
+    float cx = 0.f, cy = 0.f;
+    if (y >= 1 && y < h - 1 && x >= 1 && x < w - 1) {
+      float sxr = 0.f, syr = 0.f, sxt = 0.f, syt = 0.f;
+#pragma unroll
+      for (int k = 0; k < 9; ++k) {
+        const float vr = lr[yy + k / 3][xx + k % 3], vt = lt[yy + k / 3][xx + k % 3];
+        sxr += KX[k] * vr;
+        syr += KY[k] * vr;
+        sxt += KX[k] * vt;
+        syt += KY[k] * vt;
       }
-    float* g = grad + img * gi + p * gp;
-    g[0] = a0;
-    g[gc] = a1;
-    g[2 * gc] = a2;
+      const float mr = sqrtf(sxr * sxr + syr * syr), mt = sqrtf(sxt * sxt + syt * syt);
+      const float d0 = mr - mt;
+      if (yy >= 1 && yy <= kSobTH && xx >= 1 && xx <= kSobTW) acc += (double)d0 * d0;
+      const float inv = mr > 1e-6f ? 1.f / mr : 0.f;
+      cx = d0 * inv * scale * sxr;
+      cy = d0 * inv * scale * syr;
+    }
+    ax[yy][xx] = cx;
+    ay[yy][xx] = cy;
+  }
+  __syncthreads();
+  if (grad) {
+    for (int i = threadIdx.x; i < kSobTH * kSobTW; i += blockDim.x) {
+      const int yy = i / kSobTW, xx = i % kSobTW;
+      const int y = y0 + yy, x = x0 + xx;
+      if (y >= h || x >= w) continue;
+      // pixel p sits at tap (1 - dy, 1 - dx) of the window centred at p + (dy, dx)
+      float c = 0.f;
+#pragma unroll
+      for (int dy = -1; dy <= 1; ++dy)
+#pragma unroll
+        for (int dx = -1; dx <= 1; ++dx) {
+          const int k = (1 - dy) * 3 + (1 - dx);
+          c += ax[yy + 1 + dy][xx + 1 + dx] * KX[k] + ay[yy + 1 + dy][xx + 1 + dx] * KY[k];
+        }
+      float* g = grad + img * gi + ((long long)y * w + x) * gp;
+      g[0] = c * 0.2126f;
+      g[gc] = c * 0.7152f;
+      g[2 * gc] = c * 0.0722f;
+    }
   }
   red[threadIdx.x] = acc;
   __syncthreads();
@@ -632,17 +640,17 @@ extern "C" yl_status yl_sobel_edge_loss(yl_ctx* ctx, const float* recon, const f
   const bool nchw = layout == YL_LAYOUT_NCHW;
   const long long istr = nchw ? 3 * hw : hw * ld, pstr = nchw ? 1 : ld, cstr = nchw ? hw : 1;
   ImgView r{recon, istr, pstr, cstr}, t{target, istr, pstr, cstr};
-  const int blocks = (int)std::max(1LL, std::min((hw + 255) / 256, 256LL));
+  const int tiles_x = (w + kSobTW - 1) / kSobTW, tiles_y = (h + kSobTH - 1) / kSobTH;
+  const long long tiles = (long long)tiles_x * tiles_y;
+  YL_CHECK(tiles < (1LL << 31) && n <= 65535, YL_ERR_SHAPE, "yl_sobel_edge_loss: %d x %d x %d",
+           n, h, w);
+  const int blocks = (int)tiles;
   void* ws = nullptr;
-  const size_t map_bytes = (size_t)n * 5 * hw * sizeof(float);
-  YL_TRY(scratch_get(ctx, map_bytes + (size_t)n * blocks * sizeof(double) + 256, &ws));
-  float* maps = (float*)ws;
-  double* part = (double*)((char*)ws + ((map_bytes + 255) & ~size_t(255)));
-  sobel_map_kernel<<<dim3(blocks, n), 256, 0, ctx->stream>>>(r, t, h, w, maps);
-  YL_TRY(check_launch("sobel_map_kernel"));
-  sobel_grad_kernel<<<dim3(blocks, n), 256, 0, ctx->stream>>>(
-      maps, h, w, (float)(2.0 / (double)hw), grad, istr, pstr, cstr, part);
-  YL_TRY(check_launch("sobel_grad_kernel"));
+  YL_TRY(scratch_get(ctx, (size_t)n * blocks * sizeof(double), &ws));
+  double* part = (double*)ws;
+  sobel_tile_kernel<<<dim3(blocks, n), 256, 0, ctx->stream>>>(
+      r, t, h, w, tiles_x, (float)(2.0 / (double)hw), grad, istr, pstr, cstr, part);
+  YL_TRY(check_launch("sobel_tile_kernel"));
   if (!loss) return YL_OK;
   sobel_loss_final_kernel<<<(n + 127) / 128, 128, 0, ctx->stream>>>(part, blocks, n,
                                                                      1.0 / (double)hw, loss);
