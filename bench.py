@@ -442,7 +442,7 @@ def run_native(args):
                               f"{tf32['tf32_tflops']:.1f} TFLOP/s), SM clock median "
                               f"{tf32['clocks'].get('sm_mhz')} MHz, reasons "
                               f"{tf32['clocks'].get('reasons')}"),
-                "peak_burst": tf32["tf32_tflops"],
+                "peak_burst": tf32["tf32_tflops"], "frac_burst": achieved / tf32["tf32_tflops"],
                 "flops_note": ("achieved = 2*N*Cout*Cin*9*OH*OW per launch over the summed "
                                "CUDA-event time of those launches in the timed steps"),
                 "traffic_note": ("DRAM read + write bytes per launch from an ncu capture of "

@@ -53,9 +53,13 @@ def test_comm_init_times_out_when_a_rank_never_joins():
     assert p.exitcode == 0
 
 
-def _leaving_rank(rank, world, port, out):
+def _leaving_rank(rank, world, port, out, trace_dir):
     os.environ["NCCL_NVLS_ENABLE"] = "0"
+    import faulthandler
     from datetime import timedelta
+    # a child that stalls leaves its stacks behind for the failure message
+    trace = open(os.path.join(trace_dir, f"rank{rank}.txt"), "w")
+    faulthandler.dump_traceback_later(150, exit=False, file=trace)
 
     import numpy as np
     import torch
@@ -76,13 +80,20 @@ def _leaving_rank(rank, world, port, out):
     frames, t = synth.sample_batch(clips, 1, seed=rank)
     loss = tr.step_host(frames, t)  # one data-parallel step; returns with nothing in flight
     if rank == 1:
-        store.set("left", "1")  # leaves between steps
+        # leaves between steps: stops stepping, says so, and ends its side once
+        # the other rank has aborted
+        store.set("left", "1")
+        store.wait(["aborted"], timedelta(seconds=60))
+        comm.abort()
+        comm.close()
+        tr.close()
         out.put((rank, "left", float(loss[0])))
         return
     # rank 0 learns of it from the store before its next launch, aborts the
     # communicator and keeps working on its own
     store.wait(["left"], timedelta(seconds=60))
     comm.abort()
+    store.set("aborted", "1")
     comm.close()
     tr.close()
     solo = Trainer(cfg, ctx=ctx)
@@ -95,19 +106,29 @@ def test_rank_leaving_between_steps_is_seen_and_the_comm_aborted():
     import torch
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
+    import tempfile
     world, port = 2, _free_port()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_leaving_rank, args=(r, world, port, q)) for r in range(world)]
+    trace_dir = tempfile.mkdtemp(prefix="yl_comm_")
+    procs = [ctx.Process(target=_leaving_rank, args=(r, world, port, q, trace_dir))
+             for r in range(world)]
     for p in procs:
         p.start()
+    res = []
     try:
-        res = sorted(q.get(timeout=300) for _ in range(world))
+        for _ in range(world):
+            res.append(q.get(timeout=240))
+    except Exception:
+        stacks = "".join(open(os.path.join(trace_dir, f)).read()
+                         for f in sorted(os.listdir(trace_dir)))
+        pytest.fail(f"ranks reported {res}; stacks of stalled ranks:\n{stacks}")
     finally:
         for p in procs:
             p.join(timeout=120)
             if p.is_alive():
                 p.kill()
+    res.sort()
     assert res[0][:2] == (0, "aborted") and res[0][2] is True
     assert res[1][:2] == (1, "left")
     assert all(p.exitcode == 0 for p in procs)

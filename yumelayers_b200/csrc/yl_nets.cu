@@ -333,6 +333,8 @@ yl_status ConvL::forward(Net& net, const Act& x, const Act& y, const float* resi
     // 4 input channels: a 1x1 GEMM over the 64-channel 3x3 patches of x
     float* xp = nullptr;
     YL_TRY(net.pool.get((size_t)x.n * x.h * x.w * 64, &xp));
+    // the bracket times the patch pass with the GEMM it feeds
+    net.prof_begin(0);
     YL_TRY(rgb_patches(net.ctx, x.p, x.ld, x.n, x.h, x.w, 1, 1, xp));
     ConvEpilogue e;
     e.out = y.p;
@@ -350,7 +352,6 @@ yl_status ConvL::forward(Net& net, const Act& x, const Act& y, const float* resi
       e.gn_rstd = gn_next->rstd;
       e.gn_groups = gn_next->G;
     }
-    net.prof_begin(0);
     yl_status st =
         conv_fprop(net.ctx, pointwise(xp, x.n, x.h, x.w, 64, 64), Wx, cout_p, e);
     net.prof_end(0, 2.0 * x.pixels() * cout * cin * k * k);
@@ -397,8 +398,8 @@ yl_status ConvL::backward(Net& net, const Act& x, const Act& dy, const Act* dx,
     float *xp = nullptr, *dw = nullptr;
     YL_TRY(net.pool.get((size_t)x.n * x.h * x.w * 64, &xp));
     YL_TRY(net.pool.get((size_t)cout_p * 64, &dw));
-    YL_TRY(rgb_patches(ctx, x.p, x.ld, x.n, x.h, x.w, 1, 1, xp));
     net.prof_begin(2);
+    YL_TRY(rgb_patches(ctx, x.p, x.ld, x.n, x.h, x.w, 1, 1, xp));
     YL_TRY(conv_wgrad(ctx, dy.p, dy.ld, cout_p, pointwise(xp, x.n, x.h, x.w, 64, 64), dw, 0, gb));
     net.prof_end(2, 2.0 * x.pixels() * cout * cin * k * k);
     YL_TRY(weight_permute(ctx, dw, gW, cout_p, 1, 36, 36, 64, 0, 1, 0));
@@ -414,8 +415,8 @@ yl_status ConvL::backward(Net& net, const Act& x, const Act& dy, const Act* dx,
     YL_TRY(net.pool.get((size_t)x.n * x.h * x.w * 64, &d));
     YL_TRY(net.pool.get((size_t)64 * cin_p, &dw));
     YL_TRY(net.pool.get(64, &db));
-    YL_TRY(rgb_patches(ctx, dy.p, dy.ld, x.n, x.h, x.w, -1, 1, d));
     net.prof_begin(2);
+    YL_TRY(rgb_patches(ctx, dy.p, dy.ld, x.n, x.h, x.w, -1, 1, d));
     YL_TRY(conv_wgrad(ctx, d, 64, 64, pointwise(x.p, x.n, x.h, x.w, x.ld, cin_p), dw, 0, db));
     net.prof_end(2, 2.0 * x.pixels() * cout * cin * k * k);
     YL_TRY(weight_permute(ctx, dw, gW, 4, 9, cin_p, cin_p, cin_p, 4LL * cin_p, 1, 0));

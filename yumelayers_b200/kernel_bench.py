@@ -49,6 +49,29 @@ SMALL_SHAPES = [
 ]
 
 
+def _sobel(ctx, reps: int) -> None:
+    """Device time of yl_sobel_edge_loss on 8 NCHW RGB frames of 480x856
+    (reads recon + target, writes the gradient: 36 B per pixel)."""
+    import numpy as np
+    from .session import GPUTensor
+    n, h, w = 8, 480, 856
+    rng = np.random.default_rng(0)
+    r = GPUTensor(ctx, 1, n * 3 * h * w, rng.uniform(0, 1, n * 3 * h * w).astype(np.float32))
+    t = GPUTensor(ctx, 1, n * 3 * h * w, rng.uniform(0, 1, n * 3 * h * w).astype(np.float32))
+    g, loss = GPUTensor(ctx, 1, n * 3 * h * w), GPUTensor(ctx, 1, n)
+    ms = C.c_double()
+    args = (ctx.handle, C.c_void_p(r.ptr), C.c_void_p(t.ptr), n, h, w, 0, 0, C.c_void_p(g.ptr),
+            C.c_void_p(loss.ptr))
+    call("yl_sobel_edge_loss", *args)  # warm-up
+    call("yl_session_begin", ctx.handle)
+    for _ in range(reps):
+        call("yl_sobel_edge_loss", *args)
+    call("yl_session_end", ctx.handle, 60.0, C.byref(ms))
+    per = ms.value / reps
+    print(json.dumps({"sobel": [n, 3, h, w], "ms": per,
+                      "gbs": 36.0 * n * h * w / (per * 1e-3) / 1e9}), flush=True)
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--shapes", default="vae", choices=["vae", "unet", "epilogue", "small"])
@@ -57,6 +80,8 @@ def main(argv=None):
     ap.add_argument("--groupnorm", action="store_true")
     ap.add_argument("--layered", action="store_true",
                     help="layered 8-channel loss + gradient (108 B per pixel)")
+    ap.add_argument("--sobel", action="store_true",
+                    help="Sobel edge loss + gradient on 8 RGB frames of 480x856 (NCHW)")
     ap.add_argument("--adam", action="store_true",
                     help="one multi-tensor Adam step over the joint step's 28.5 M parameters")
     a = ap.parse_args(argv)
@@ -91,6 +116,8 @@ def main(argv=None):
         call("yl_profile_adam", ctx.handle, n, tensors, a.reps, C.byref(ms))
         print(json.dumps({"adam_params": n, "ms": ms.value,
                           "gbs": 28.0 * n / (ms.value * 1e-3) / 1e9}), flush=True)
+    if a.sobel:
+        _sobel(ctx, a.reps)
     if a.layered:
         n, plane = (8, 480 * 856) if a.shapes == "vae" else (4, 480 * 856)
         ms = C.c_double()
