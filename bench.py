@@ -51,8 +51,8 @@ ENC_FWD_PER_FRAME = 1.1100e12
 MOTION_TRAIN_PER_SAMPLE = 0.1433e12
 # DRAM bytes (read + write) of one conv_tma_fprop_kernel<128, 2, 1, 1> launch
 # per image of 480x856 (3x3, 128 -> 128): ncu capture of a 2-image launch,
-# 421.7 MB read + 376.1 MB written.
-DOM_TRAFFIC_PER_IMAGE = (421.7e6 + 376.1e6) / 2
+# 421.5 MB read + 374.6 MB written.
+DOM_TRAFFIC_PER_IMAGE = (421.5e6 + 374.6e6) / 2
 WORKLOAD = ("joint VAE + motion-net train step at 854x480: VAE fwd+bwd on frame k, encoder fwd "
             "on frames 0/16, U-Net fwd+bwd, all-reduce, Adam")
 
@@ -363,6 +363,9 @@ def run_native(args):
     ms = max_over_ranks(ev0.elapsed_time(ev1), f"cuda:{local}")
     clocks = clk.summary()
     stats = tr.kernel_stats(reset=True)
+    comm_ms, comm_steps = tr.comm_stats(reset=True)
+    # every rank profiled the same steps: at N > 1 all ranks take part in the max
+    exposed = (max_over_ranks(comm_ms / comm_steps, f"cuda:{local}") if comm_steps else None)
     tr.set_config(profile=0)
     losses = losses_dev.cpu().numpy().tolist()
 
@@ -480,6 +483,7 @@ def run_native(args):
                     "d2h_bytes_per_step": 8, "ms_per_step": e2e_ms / args.steps},
             "roofline": roofline, "kernels": kernels, "conv_templates": conv_templates,
             "configs": configs, "cpu_baseline": cpu,
+            "exposed_comm_ms_per_step": exposed,
             "clocks": clocks, "gpu_launches": int(launches),
             "losses_last_step": losses,
         }

@@ -444,6 +444,11 @@ yl_status yl_trainer_kernel_stats(yl_trainer* tr, yl_kernel_stats* out, int rese
  * min(capacity, *count) entries; *count = number of templates.  No
  * counterpart in the reference (its profileConv, Diagnostics.swift:123-201,
  * times one im2col + matmul path). */
+/* Profiled data-parallel steps: device time the compute stream waited, after
+ * the last backward kernel, for the gradient and loss reductions (the
+ * communication backward did not hide), summed over *steps steps.  No
+ * counterpart in the reference (single device). */
+yl_status yl_trainer_comm_stats(yl_trainer* tr, double* exposed_ms, int* steps, int reset);
 typedef struct yl_template_stats {
   char name[96];
   double ms, flops, exec_flops;

@@ -159,6 +159,7 @@ class TemplateStats(C.Structure):
 
 
 SIGNATURES["yl_trainer_template_stats"] = [P, C.POINTER(TemplateStats), I, C.POINTER(I)]
+SIGNATURES["yl_trainer_comm_stats"] = [P, C.POINTER(D), C.POINTER(I), I]
 SIGNATURES["yl_comm_init_timeout"] = [P, P, I, I, D, C.POINTER(P)]
 SIGNATURES["yl_ctx_set_wait_limit"] = [P, C.c_longlong]
 SIGNATURES["yl_ctx_last_kernel"] = [P, I]

@@ -161,6 +161,12 @@ struct yl_trainer {
   double prof_exec[kProfClasses] = {};
   std::map<std::string, TemplateStat> prof_templates;
   std::map<std::string, TemplateStat> last_templates;  // as of the last kernel_stats call
+  // profiled steps of a data-parallel run: the compute stream's wait for the
+  // gradient and loss reductions after the last backward kernel (exposed
+  // communication), one event pair per step, read in yl_trainer_comm_stats
+  std::vector<std::pair<cudaEvent_t, cudaEvent_t>> comm_wait_ev;
+  double comm_exposed_ms = 0.0;
+  int comm_steps = 0;
 };
 
 extern "C" {
@@ -373,6 +379,12 @@ yl_status yl_trainer_step(yl_trainer* tr, const float* frames, const float* t, f
   }
   float scale = 1.f;
   if (tr->comm && tr->comm->world > 1) {
+    cudaEvent_t w0 = nullptr, w1 = nullptr;
+    if (tr->cfg.profile) {
+      YL_CUDA(cudaEventCreate(&w0));
+      YL_CUDA(cudaEventCreate(&w1));
+      YL_CUDA(cudaEventRecord(w0, ctx->stream));
+    }
     // the step's loss values are averaged across ranks too (after all queued work)
     YL_CUDA(cudaEventRecord(tr->ov_vae.ready_ev, ctx->stream));
     YL_CUDA(cudaStreamWaitEvent(tr->comm->stream, tr->ov_vae.ready_ev, 0));
@@ -380,6 +392,10 @@ yl_status yl_trainer_step(yl_trainer* tr, const float* frames, const float* t, f
                        "loss all-reduce"));
     YL_CUDA(cudaEventRecord(tr->comm_done, tr->comm->stream));
     YL_CUDA(cudaStreamWaitEvent(ctx->stream, tr->comm_done, 0));
+    if (w0) {
+      YL_CUDA(cudaEventRecord(w1, ctx->stream));
+      tr->comm_wait_ev.push_back({w0, w1});
+    }
     scale = 1.f / (float)tr->comm->world;
   }
   if (train_vae) YL_TRY(adam_step(tr, vae, tr->cfg.lr_vae, scale));
@@ -587,6 +603,27 @@ yl_status yl_trainer_kernel_stats(yl_trainer* tr, yl_kernel_stats* out, int rese
     tr->prof_templates.clear();
   } else {
     tr->last_templates = tr->prof_templates;
+  }
+  return YL_OK;
+}
+
+yl_status yl_trainer_comm_stats(yl_trainer* tr, double* exposed_ms, int* steps, int reset) {
+  YL_CHECK(tr && exposed_ms && steps, YL_ERR_INVALID, "yl_trainer_comm_stats: NULL argument");
+  if (!tr->comm_wait_ev.empty()) YL_CUDA(cudaStreamSynchronize(tr->ctx->stream));
+  for (auto& e : tr->comm_wait_ev) {
+    float t = 0.f;
+    YL_CUDA(cudaEventElapsedTime(&t, e.first, e.second));
+    tr->comm_exposed_ms += t;
+    tr->comm_steps += 1;
+    cudaEventDestroy(e.first);
+    cudaEventDestroy(e.second);
+  }
+  tr->comm_wait_ev.clear();
+  *exposed_ms = tr->comm_exposed_ms;
+  *steps = tr->comm_steps;
+  if (reset) {
+    tr->comm_exposed_ms = 0.0;
+    tr->comm_steps = 0;
   }
   return YL_OK;
 }

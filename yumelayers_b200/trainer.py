@@ -209,6 +209,12 @@ class Trainer:
                                  "launches": st.launches[i], "exec_flops": st.exec_flops[i]}
                 for i in range(len(CLASS_NAMES))}
 
+    def comm_stats(self, reset: bool = False) -> tuple[float, int]:
+        """(exposed communication ms summed over profiled steps, steps)."""
+        ms, n = C.c_double(), C.c_int()
+        call("yl_trainer_comm_stats", self.handle, C.byref(ms), C.byref(n), int(reset))
+        return ms.value, n.value
+
     def template_stats(self) -> dict:
         """Profiled conv brackets per kernel template, as of the last kernel_stats
         call: ms, algorithmic flops, executed flops, launches."""
