@@ -14,8 +14,9 @@ synchronize on both sides, max over ranks):
   e2e   -- K steps through yl_trainer_step_host: host->device copy of the
            step's frames from pinned memory, the step, device->host read of
            the two losses, every step.
-Per-kernel-class times come from CUDA events the library records around
-every conv / GroupNorm launch inside the `value` region.
+Per-kernel-class and per-template times come from CUDA events the library
+records around every conv / GroupNorm launch, in K further steps run after
+the `value` region (so the value itself carries no per-launch events).
 
 Roofline denominators: the dense TF32 rate is measured at the start of the
 run on the same GPU (cuBLAS fp32 GEMM with TF32 tensor cores, burst and
@@ -346,9 +347,8 @@ def run_native(args):
         tr.step_device(dev[i % nb].data_ptr(), tdev[i % nb].data_ptr(), losses_dev.data_ptr())
     barrier()
 
-    # ---- value: device-resident inputs
-    tr.set_config(profile=1)
-    tr.kernel_stats(reset=True)
+    # ---- value: device-resident inputs, no per-launch events in the step
+    tr.set_config(profile=0)
     launches0 = lib().yl_kernel_launch_count()
     barrier()
     with ClockSampler(local) as clk:
@@ -362,12 +362,27 @@ def run_native(args):
     launches = lib().yl_kernel_launch_count() - launches0
     ms = max_over_ranks(ev0.elapsed_time(ev1), f"cuda:{local}")
     clocks = clk.summary()
+    losses = losses_dev.cpu().numpy().tolist()
+
+    # ---- the same steps again with CUDA events around every conv / GroupNorm
+    # launch: per-class and per-template times, exposed communication
+    tr.set_config(profile=1)
+    tr.kernel_stats(reset=True)
+    tr.comm_stats(reset=True)
+    barrier()
+    p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    p0.record(stream)
+    for i in range(args.steps):
+        tr.step_device(dev[i % nb].data_ptr(), tdev[i % nb].data_ptr(), losses_dev.data_ptr())
+    p1.record(stream)
+    p1.synchronize()
+    barrier()
+    prof_ms = max_over_ranks(p0.elapsed_time(p1), f"cuda:{local}")
     stats = tr.kernel_stats(reset=True)
     comm_ms, comm_steps = tr.comm_stats(reset=True)
     # every rank profiled the same steps: at N > 1 all ranks take part in the max
     exposed = (max_over_ranks(comm_ms / comm_steps, f"cuda:{local}") if comm_steps else None)
     tr.set_config(profile=0)
-    losses = losses_dev.cpu().numpy().tolist()
 
     # ---- e2e: host buffers through the public step call
     out = np.zeros(2, np.float32)
@@ -396,7 +411,7 @@ def run_native(args):
         if v["ms"] <= 0:
             continue
         ent = {"ms_per_step": v["ms"] / args.steps, "launches_per_step": v["launches"] / args.steps,
-               "share_of_step": v["ms"] / ms}
+               "share_of_step": v["ms"] / prof_ms}
         if v["flops"]:
             ent["tflops_algorithmic"] = v["flops"] / (v["ms"] * 1e-3) / 1e12
             ent["tflops_executed"] = v["exec_flops"] / (v["ms"] * 1e-3) / 1e12
@@ -412,7 +427,7 @@ def run_native(args):
         ex = v["exec_flops"] / (v["ms"] * 1e-3) / 1e12
         conv_templates.append({
             "kernel": name, "launches_per_step": v["launches"] / args.steps,
-            "ms_per_step": v["ms"] / args.steps, "share_of_step": v["ms"] / ms,
+            "ms_per_step": v["ms"] / args.steps, "share_of_step": v["ms"] / prof_ms,
             "tflops_algorithmic": v["flops"] / (v["ms"] * 1e-3) / 1e12,
             "tflops_executed": ex, "frac_tf32_executed": ex / tf32_peak})
     classes = ("conv_fprop", "conv_dgrad", "conv_wgrad", "gn_silu_fwd", "gn_silu_bwd")
@@ -484,6 +499,7 @@ def run_native(args):
             "roofline": roofline, "kernels": kernels, "conv_templates": conv_templates,
             "configs": configs, "cpu_baseline": cpu,
             "exposed_comm_ms_per_step": exposed,
+            "profiled_ms_per_step": prof_ms / args.steps,
             "clocks": clocks, "gpu_launches": int(launches),
             "losses_last_step": losses,
         }
