@@ -473,9 +473,11 @@ yl_status yl_profile_conv(yl_ctx* ctx, int n, int c, int h, int w, int oc, int k
 /* One multi-tensor Adam step over n parameters split into `tensors` (<= 48)
  * tensors; *ms = average device time of one step.  Diagnostic only. */
 yl_status yl_profile_adam(yl_ctx* ctx, long long n, int tensors, int reps, double* ms);
-/* GroupNorm(32)+SiLU forward and backward on an n x h x w x c NHWC tensor. */
+/* GroupNorm(32)+SiLU forward (statistics + apply) and backward on an
+ * n x h x w x c NHWC tensor; apply_ms (may be NULL) gets the apply pass alone,
+ * the training step's forward when a conv supplied the statistics. */
 yl_status yl_profile_groupnorm(yl_ctx* ctx, int n, int c, int h, int w, int reps, double* fwd_ms,
-                               double* bwd_ms);
+                               double* bwd_ms, double* apply_ms);
 /* Layered 8-channel loss + gradient on n images of `plane` pixels (synthetic
  * planes); *ms = average device time of one yl_layered_loss call. */
 yl_status yl_profile_layered(yl_ctx* ctx, int n, long long plane, int reps, double* ms);

@@ -215,7 +215,7 @@ class ConvProfile(C.Structure):
 
 
 SIGNATURES["yl_profile_conv"] = [P, I, I, I, I, I, I, I, I, I, C.POINTER(ConvProfile)]
-SIGNATURES["yl_profile_groupnorm"] = [P, I, I, I, I, I, C.POINTER(D), C.POINTER(D)]
+SIGNATURES["yl_profile_groupnorm"] = [P, I, I, I, I, I, C.POINTER(D), C.POINTER(D), C.POINTER(D)]
 SIGNATURES["yl_trainer_interpolate"] = [P, P, P, P, I, I, P]
 SIGNATURES["yl_interpolation_plan"] = [D, I, I, P, C.POINTER(I)]
 SIGNATURES["yl_trainer_get_step"] = [P, C.POINTER(C.c_int64)]

@@ -225,7 +225,7 @@ yl_status yl_profile_adam(yl_ctx* ctx, long long n, int tensors, int reps, doubl
 }
 
 yl_status yl_profile_groupnorm(yl_ctx* ctx, int n, int c, int h, int w, int reps, double* fwd_ms,
-                               double* bwd_ms) {
+                               double* bwd_ms, double* apply_ms) {
   YL_CHECK(ctx && fwd_ms && bwd_ms && reps >= 1, YL_ERR_INVALID, "yl_profile_groupnorm");
   const long long e = (long long)n * h * w * c;
   DevBufs b;
@@ -248,13 +248,15 @@ yl_status yl_profile_groupnorm(yl_ctx* ctx, int n, int c, int h, int w, int reps
   cudaEvent_t e0, e1;
   YL_CUDA(cudaEventCreate(&e0));
   YL_CUDA(cudaEventCreate(&e1));
-  double ms[2];
-  for (int mode = 0; mode < 2; ++mode) {
+  double ms[3];
+  for (int mode = 0; mode < 3; ++mode) {
     for (int rr = -1; rr < reps; ++rr) {
       if (rr == 0) YL_CUDA(cudaEventRecord(e0, ctx->stream));
       if (mode == 0)
         YL_TRY(gn_silu_forward(ctx, x, n, c, 32, (long long)h * w, c, 1e-6f, 0, g, bt, 1, y, c, 1,
                                m, r));
+      else if (mode == 2)  // the apply pass alone, statistics from mode 0
+        YL_TRY(gn_silu_apply(ctx, x, n, c, 32, (long long)h * w, c, m, r, g, bt, 1, y, c, 1));
       else
         YL_TRY(gn_silu_backward(ctx, x, dy, c, n, c, 32, (long long)h * w, c, m, r, g, bt, 1, y, c,
                                 dx, c, 1, dg, db, 0));
@@ -269,6 +271,7 @@ yl_status yl_profile_groupnorm(yl_ctx* ctx, int n, int c, int h, int w, int reps
   cudaEventDestroy(e1);
   *fwd_ms = ms[0];
   *bwd_ms = ms[1];
+  if (apply_ms) *apply_ms = ms[2];
   return yl_ctx_check_device_errors(ctx);
 }
 

@@ -104,10 +104,12 @@ def main(argv=None):
         gn_shapes = ([(8, 128, 480, 856), (8, 256, 240, 428)] if a.shapes == "vae"
                      else [(8, 128, 192, 192)])
         for (n, c, h, w) in gn_shapes:
-            f, b = C.c_double(), C.c_double()
-            call("yl_profile_groupnorm", ctx.handle, n, c, h, w, a.reps, C.byref(f), C.byref(b))
+            f, b, ap = C.c_double(), C.c_double(), C.c_double()
+            call("yl_profile_groupnorm", ctx.handle, n, c, h, w, a.reps, C.byref(f), C.byref(b),
+                 C.byref(ap))
             e = n * c * h * w * 4
             print(json.dumps({"groupnorm": [n, c, h, w], "fwd_ms": f.value, "bwd_ms": b.value,
+                              "apply_ms": ap.value, "apply_gbs": 2 * e / (ap.value * 1e-3) / 1e9,
                               "fwd_gbs": 3 * e / (f.value * 1e-3) / 1e9,
                               "bwd_gbs": 5 * e / (b.value * 1e-3) / 1e9}), flush=True)
     if a.adam:
