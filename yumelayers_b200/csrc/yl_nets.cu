@@ -199,7 +199,6 @@ yl_status ConvL::bind(Net& net) {
   gb = net.params.g + off_b;
   YL_TRY(net.arena.alloc((size_t)cout_p * k * k * cin_p, &Wr));
   YL_TRY(net.arena.alloc((size_t)cin_p * k * k * cout_p, &Wd));
-  if (rgb == 1) YL_TRY(net.arena.alloc((size_t)cout_p * 64, &Wx));
   if (rgb == 2) {
     YL_TRY(net.arena.alloc((size_t)36 * cin_p, &Wx));
     YL_TRY(net.arena.alloc((size_t)cin_p * 64, &Wx2));
@@ -220,8 +219,6 @@ void ConvL::prepare_jobs(std::vector<PermuteJob>& first, std::vector<PermuteJob>
   const int kk = k * k;
   first.push_back({W, Wr, cout_p, kk, cin_p, cin_p, (long long)kk * cin_p, cin_p, 1, 1});
   first.push_back({W, Wd, cin_p, kk, cout_p, cout_p, 1, cin_p, (long long)kk * cin_p, 1});
-  if (rgb == 1)  // [cout][t*4 + ci], zero-padded to 64 columns
-    second.push_back({Wr, Wx, cout_p, 1, 64, 36, 36, 0, 1, 0});
   if (rgb == 2) {
     // [t*4 + co][ci] = W[co][t][ci] and [ci][t*4 + co] (from the dgrad copy), padded
     second.push_back({Wr, Wx, 9, 4, cin_p, cin_p, cin_p, 9LL * cin_p, 1, 0});
@@ -329,36 +326,9 @@ yl_status ConvL::forward(Net& net, const Act& x, const Act& y, const float* resi
     net.pool.put(z);
     return YL_OK;
   }
-  if (rgb == 1 && !up) {
-    // 4 input channels: a 1x1 GEMM over the 64-channel 3x3 patches of x
-    float* xp = nullptr;
-    YL_TRY(net.pool.get((size_t)x.n * x.h * x.w * 64, &xp));
-    // the bracket times the patch pass with the GEMM it feeds
-    net.prof_begin(0);
-    YL_TRY(rgb_patches(net.ctx, x.p, x.ld, x.n, x.h, x.w, 1, 1, xp));
-    ConvEpilogue e;
-    e.out = y.p;
-    e.ldo = y.ld;
-    e.n_total = cout_p;
-    e.bias = b;
-    e.bias2d = bias2d;
-    e.residual = residual;
-    e.ldr = ldr;
-    e.round_tf32 = 1;
-    const bool fuse_gn =
-        gn_next && gn_next->c == cout_p && conv_gn_stats_supported(cout_p, gn_next->G);
-    if (fuse_gn) {
-      e.gn_mean = gn_next->mean;
-      e.gn_rstd = gn_next->rstd;
-      e.gn_groups = gn_next->G;
-    }
-    yl_status st =
-        conv_fprop(net.ctx, pointwise(xp, x.n, x.h, x.w, 64, 64), Wx, cout_p, e);
-    net.prof_end(0, 2.0 * x.pixels() * cout * cin * k * k);
-    net.pool.put(xp);
-    if (st == YL_OK && fuse_gn) gn_next->stats_ready = true;
-    return st;
-  }
+  // 4 input channels (the RGB frame) take the general path: the narrow TMA
+  // plan loads one zero-filled 32-channel box per tap straight from the
+  // 16-byte pixels (no patch tensor), through the halo-box kernel
   // a cropped upsample runs as a plain conv over the upsampled input: the
   // merged phase taps need the whole x2 grid
   Act xu = x;

@@ -71,8 +71,9 @@ struct ConvL {
   float *W = nullptr, *b = nullptr, *gW = nullptr, *gb = nullptr;
   float *Wr = nullptr, *Wd = nullptr;  // tf32 copies: fprop [cout][tap][cin], dgrad [cin][tap][cout]
   // 3x3 convs with a 4-channel (RGB) side run as 1x1 GEMMs over 3x3 patches:
-  // rgb 1 = 4-channel input (Wx: [cout][64] patch weights); rgb 2 = 4-channel
-  // output (Wx: [9*4][cin] tap weights, Wx2: [cin][64] dX patch weights)
+  // rgb 1 = 4-channel input (its filter gradient runs over 64-channel 3x3
+  // patches); rgb 2 = 4-channel output (Wx: [9*4][cin] tap weights,
+  // Wx2: [cin][64] dX patch weights)
   int rgb = 0;
   float *Wx = nullptr, *Wx2 = nullptr;
   void setup(Net& net, const char* name, int cin, int cout, int k, int stride, int pad);
