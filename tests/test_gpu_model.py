@@ -15,7 +15,7 @@ pytestmark = pytest.mark.gpu
 LOSS_TOL = 1e-3
 
 
-def _setup(batch=2, h=32, w=48, seed=3):
+def _setup(batch=2, h=32, w=48, seed=3, n_batches=4):
     from yumelayers_b200 import synth
     from yumelayers_b200.trainer import Trainer, default_config
     import nets
@@ -25,7 +25,7 @@ def _setup(batch=2, h=32, w=48, seed=3):
     js = nets.JointStep(vp, up, tr.param_count(0), tr.param_count(1))
     rng = np.random.default_rng(seed)
     batches = []
-    for s in range(4):
+    for s in range(n_batches):
         frames = np.stack([np.stack([synth.make_frame(100 * s + 10 * b + f, h, w, w)
                                      for b in range(batch)]) for f in range(3)])
         t = (rng.integers(1, 16, batch) / 16.0).astype(np.float32)
@@ -46,12 +46,17 @@ def _resync(js, tr):
 def test_joint_step_losses_match_oracle_100_steps():
     """Per-step loss within 1e-3 over 100 training steps: before every step the
     oracle takes the GPU's weights; both then run the same step on the same
-    frames (the GPU's Adam keeps training the weights between steps)."""
-    tr, js, batches = _setup()
+    frames (the GPU's Adam keeps training the weights between steps).
+
+    Every step sees new frames, as training does.  (Cycling a handful of
+    batches lets the VAE memorise them: its L1 loss falls toward the absolute
+    tf32 noise of the reconstruction, ~2e-4 on these 9216-pixel batches, and
+    the relative bound then measures that floor rather than the step.)"""
+    tr, js, batches = _setup(n_batches=100)
     worst = 0.0
     rows = []
     for step in range(100):
-        frames, t = batches[step % len(batches)]
+        frames, t = batches[step]
         _resync(js, tr)
         js.step_no = step
         gpu = tr.step_host(frames, t)
