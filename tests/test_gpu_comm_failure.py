@@ -57,9 +57,14 @@ def _leaving_rank(rank, world, port, out, trace_dir):
     os.environ["NCCL_NVLS_ENABLE"] = "0"
     import faulthandler
     from datetime import timedelta
-    # a child that stalls leaves its stacks behind for the failure message
-    trace = open(os.path.join(trace_dir, f"rank{rank}.txt"), "w")
+    # a child that stalls or dies leaves its last stage and its stacks behind
+    # for the failure message
+    trace = open(os.path.join(trace_dir, f"rank{rank}.txt"), "w", buffering=1)
+    faulthandler.enable(file=trace, all_threads=True)
     faulthandler.dump_traceback_later(150, exit=False, file=trace)
+
+    def stage(what):
+        trace.write(f"rank {rank}: {what}\n")
 
     import numpy as np
     import torch
@@ -69,21 +74,26 @@ def _leaving_rank(rank, world, port, out, trace_dir):
     from yumelayers_b200.session import Context
     from yumelayers_b200.trainer import Comm, Trainer, default_config
     torch.cuda.set_device(rank)
+    stage("store")
     store = dist.TCPStore("127.0.0.1", port, world, rank == 0, timeout=timedelta(seconds=60))
     ctx = Context(rank)
     if rank == 0:
         store.set("uid", Comm.unique_id())
+    stage("communicator")
     comm = Comm(ctx, store.get("uid"), rank, world, timeout_s=60.0)
     cfg = default_config(batch=1, height=32, width=48, seed=2)
     tr = Trainer(cfg, ctx=ctx, comm=comm)
     clips = [synth.make_clip(60 + rank, h=32, w=48, width_padded=48)]
     frames, t = synth.sample_batch(clips, 1, seed=rank)
+    stage("step")
     loss = tr.step_host(frames, t)  # one data-parallel step; returns with nothing in flight
     if rank == 1:
         # leaves between steps: stops stepping, says so, and ends its side once
         # the other rank has aborted
         store.set("left", "1")
+        stage("left; waiting for the other rank's abort")
         store.wait(["aborted"], timedelta(seconds=60))
+        stage("abort")
         comm.abort()
         comm.close()
         tr.close()
@@ -92,7 +102,9 @@ def _leaving_rank(rank, world, port, out, trace_dir):
     # rank 0 learns of it from the store before its next launch, aborts the
     # communicator and keeps working on its own
     store.wait(["left"], timedelta(seconds=60))
+    stage("abort")
     comm.abort()
+    stage("aborted")
     store.set("aborted", "1")
     comm.close()
     tr.close()
@@ -122,7 +134,10 @@ def test_rank_leaving_between_steps_is_seen_and_the_comm_aborted():
     except Exception:
         stacks = "".join(open(os.path.join(trace_dir, f)).read()
                          for f in sorted(os.listdir(trace_dir)))
-        pytest.fail(f"ranks reported {res}; stacks of stalled ranks:\n{stacks}")
+        for p in procs:
+            p.join(timeout=30)
+        codes = [p.exitcode for p in procs]
+        pytest.fail(f"ranks reported {res}; exit codes {codes}; stages and stacks:\n{stacks}")
     finally:
         for p in procs:
             p.join(timeout=120)
