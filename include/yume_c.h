@@ -379,6 +379,8 @@ typedef struct yl_trainer_config {
 } yl_trainer_config;
 yl_status yl_trainer_create(yl_ctx* ctx, const yl_trainer_config* cfg, yl_comm* comm_or_null,
                             yl_trainer** out);
+/* A trainer borrows its communicator: destroy the trainer before the
+ * communicator (yl_comm_abort may come first; yl_comm_destroy may not). */
 yl_status yl_trainer_destroy(yl_trainer* tr);
 /* frames: device, [3][batch][3][height][width] fp32 in [-1, 1] = frame 0,
  * frame 16 and frame k of every sample (NCHW); t: device [batch] (k/16);

@@ -95,8 +95,8 @@ def _leaving_rank(rank, world, port, out, trace_dir):
         store.wait(["aborted"], timedelta(seconds=60))
         stage("abort")
         comm.abort()
+        tr.close()  # the trainer borrows the communicator: release it first
         comm.close()
-        tr.close()
         out.put((rank, "left", float(loss[0])))
         return
     # rank 0 learns of it from the store before its next launch, aborts the
@@ -106,8 +106,8 @@ def _leaving_rank(rank, world, port, out, trace_dir):
     comm.abort()
     stage("aborted")
     store.set("aborted", "1")
+    tr.close()  # the trainer borrows the communicator: release it first
     comm.close()
-    tr.close()
     solo = Trainer(cfg, ctx=ctx)
     solo_loss = solo.step_host(frames, t)
     solo.close()

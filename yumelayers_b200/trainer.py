@@ -8,6 +8,7 @@ library's own NCCL communicator carries the gradients), and moves buffers.
 from __future__ import annotations
 
 import ctypes as C
+import weakref
 from dataclasses import dataclass
 
 import numpy as np
@@ -49,6 +50,7 @@ class Comm:
         h = C.c_void_p()
         buf = (C.c_uint8 * 128).from_buffer_copy(id_bytes)
         call("yl_comm_init_timeout", ctx.handle, buf, rank, world, float(timeout_s), C.byref(h))
+        self._users = []  # trainers borrowing this communicator (weak references)
         self.handle, self.rank, self.world = h, rank, world
 
     @staticmethod
@@ -62,6 +64,12 @@ class Comm:
         call("yl_comm_abort", self.handle)
 
     def close(self) -> None:
+        """Destroys the communicator; trainers still using it are closed first
+        (a trainer must not outlive the communicator it borrows)."""
+        for ref in getattr(self, "_users", []):
+            t = ref()
+            if t is not None:
+                t.close()
         if self.handle:
             call("yl_comm_destroy", self.handle)
             self.handle = None
@@ -107,6 +115,8 @@ class Trainer:
         call("yl_trainer_create", self.ctx.handle, C.byref(cfg), comm.handle if comm else None,
              C.byref(h))
         self.handle = h
+        if comm is not None:
+            comm._users.append(weakref.ref(self))
 
     def close(self) -> None:
         if getattr(self, "handle", None):
