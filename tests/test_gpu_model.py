@@ -149,3 +149,55 @@ def test_vae_gradients_match_oracle():
     assert rel < 1e-2, detail
     assert per[0][0] < 2e-2, detail
     tr.close()
+
+
+def test_unet_gradients_match_oracle():
+    """One motion-net step's full gradient vector (before Adam) against the
+    oracle's, from the same weights and frames: the U-Net's inputs are the
+    encoder means of frames 0 and 16 and its target the mean of frame k, each
+    computed by its own side (MSE loss: no sign ties).  This covers the
+    GroupNorm backward sums the residual blocks' dX convs write for the
+    GroupNorm that follows them."""
+    from yumelayers_b200 import synth
+    from yumelayers_b200.trainer import Trainer, default_config
+    import nets
+    h, w = 32, 48
+    tr = Trainer(default_config(batch=2, height=h, width=w, seed=6, train_vae=0, lr_motion=0.0))
+    vp = nets.Params(tr.param_table(0), tr.download(0))
+    up = nets.Params(tr.param_table(1), tr.download(1))
+    # a non-zero output conv, so that every gradient of the net is exercised
+    rng = np.random.default_rng(2)
+    flat = tr.download(1)
+    for e in up.table:
+        if e.name == "conv_out.weight":
+            n = int(np.prod([d for d in e.shape if d > 0]))
+            flat[e.offset:e.offset + n] = rng.uniform(-0.02, 0.02, n).astype(np.float32)
+    tr.upload(1, flat)
+    up = nets.Params(up.table, flat)
+    ops = nets.Ops()
+    vae, unet = nets.VAE(ops, vp), nets.UNet(ops, up)
+    frames = np.stack([np.stack([synth.make_frame(700 + 10 * b + f, h, w, w) for b in range(2)])
+                       for f in range(3)]).astype(np.float32)
+    t = np.array([0.25, 0.75], np.float32)
+    gpu_loss = tr.step_host(frames, t)
+    g_gpu = tr.download(1, kind=1)
+    c = 32
+    za, zb, zk = (vae.encode(frames[i])[0][:, :c] for i in range(3))
+    loss, g = unet.train_forward_backward(np.ascontiguousarray(za), np.ascontiguousarray(zb), t,
+                                          np.ascontiguousarray(zk))
+    g_ref = up.to_flat(g, g_gpu.size)
+    assert abs(gpu_loss[1] - loss) / loss < LOSS_TOL
+    rel = np.linalg.norm(g_gpu - g_ref) / np.linalg.norm(g_ref)
+    per = []
+    for e in up.table:
+        n = int(np.prod([d for d in e.shape if d > 0]))
+        if n < 4096:
+            continue
+        a = np.asarray(up._get(e, g_gpu))
+        b = np.asarray(up._get(e, g_ref))
+        per.append((float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30)), e.name))
+    per.sort(reverse=True)
+    detail = f"global {rel:.3e}; worst tensors " + ", ".join(f"{n} {r:.2e}" for r, n in per[:6])
+    assert rel < 1e-2, detail
+    assert per[0][0] < 2e-2, detail
+    tr.close()
