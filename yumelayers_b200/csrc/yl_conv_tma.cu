@@ -507,14 +507,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         // lattice row
         const int t = warp * 32 + lane, q = t >> 2, ch = n0 + (t & 3) * 32;
         const int gx = c.tx * 32 + q, X = gx * p.xs + ph.xa;
-        if ((e.residual || e.gnb_part) && ch < e.n_total && gx < p.gw && X < p.out_w) {
+        if (e.residual && ch < e.n_total && gx < p.gw && X < p.out_w) {
 #pragma unroll 1
           for (int j = 0; j < kRows; ++j) {
             const int gy = c.ty * kRows + j, Y = gy * p.ys + ph.ya;
             if (gy >= p.gh || Y >= p.out_h) break;
             const long long pix = ((long long)c.img * p.out_h + Y) * p.out_w + X;
-            if (e.residual) prefetch_l2(e.residual + pix * e.ldr + ch);
-            if (e.gnb_part) prefetch_l2(e.gnb_x + pix * e.gnb_ldx + ch);
+            prefetch_l2(e.residual + pix * e.ldr + ch);
           }
         }
       }
@@ -533,17 +532,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t tbase =
             tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)(buf * Cfg::kAccCols);
         float gs = 0.f, gss = 0.f;  // GroupNorm partials of this channel
-        // the output is the gradient of a GroupNorm + SiLU: that backward's
-        // sums of this channel over the tile's pixels
-        const bool gnb = e.gnb_part != nullptr;
-        float gm = 0.f, gr = 0.f, gga = 1.f, gbe = 0.f, gdg = 0.f, gdb = 0.f;
-        if (gnb && cval) {
-          const int gi = c.img * e.gnb_groups + co / (e.n_total / e.gnb_groups);
-          gm = __ldg(e.gnb_mean + gi);
-          gr = __ldg(e.gnb_rstd + gi);
-          if (e.gnb_gamma) gga = __ldg(e.gnb_gamma + co);
-          if (e.gnb_beta) gbe = __ldg(e.gnb_beta + co);
-        }
 #pragma unroll 1
         for (int j = 0; j < kRows; ++j) {
           uint32_t r[32];
@@ -580,24 +568,6 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (cval && q < qn) {
               gs += v[q];
               gss += v[q] * v[q];
-            }
-          }
-          if (gnb) {
-            const float* xrow = e.gnb_x + (rowp + X0) * e.gnb_ldx + (cval ? co : 0);
-            const int sx = p.xs * e.gnb_ldx;
-            float xv[32];
-#pragma unroll
-            for (int q = 0; q < 32; ++q) xv[q] = cval && q < qn ? xrow[q * sx] : 0.f;
-#pragma unroll
-            for (int q = 0; q < 32; ++q) {
-              if (cval && q < qn) {
-                const float xh = (xv[q] - gm) * gr;
-                const float a = fmaf(xh, gga, gbe);
-                const float sg = __fdividef(1.f, 1.f + __expf(-a));
-                const float d = v[q] * (sg * fmaf(a, 1.f - sg, 1.f));
-                gdg = fmaf(d, xh, gdg);
-                gdb += d;
-              }
             }
           }
           if (p.tma_out) {
@@ -640,7 +610,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           if ((lane & (e.gn_cg - 1)) == 0)
             e.gn_part[(long long)tile * gpb + (warp * 32 + lane) / e.gn_cg] = make_float2(gs, gss);
         }
-        if (gnb && cval) e.gnb_part[(long long)tile * BN + warp * 32 + lane] = make_float2(gdg, gdb);
         tc_fence_before();
         mbar_arrive(&acc_empty[buf]);
         continue;
@@ -1312,20 +1281,6 @@ static yl_status launch_plan(yl_ctx* ctx, const View* views, int nviews, const f
     YL_TRY(scratch_get(ctx, (size_t)p.n_tiles * slots * gpb * sizeof(float2), &part, 2));
     ek.gn_part = (float2*)part;
   }
-  ek.gnb_part = nullptr;
-  if (e.gnb_x && e.gnb_out && TR && nphase == 1 && e.gnb_groups > 0 &&
-      e.n_total % e.gnb_groups == 0) {
-    // the GroupNorm backward sums of the output, one float2 per (tile,
-    // channel); they stay in scratch slot 3 for the GroupNorm backward
-    void* gp = nullptr;
-    YL_TRY(scratch_get(ctx, (size_t)p.n_tiles * BN * sizeof(float2), &gp, 3));
-    ek.gnb_part = (float2*)gp;
-    e.gnb_out->part = ek.gnb_part;
-    e.gnb_out->n_img = p.n_img;
-    e.gnb_out->tiles_per_img = p.tiles_x * p.tiles_y;
-    e.gnb_out->n_nblk = p.n_nblk;
-    e.gnb_out->bn = BN;
-  }
   YL_CUDA(cudaFuncSetAttribute(conv_tma_fprop_kernel<BN, MT, TR, HALO>,
                                cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem));
   const int grid = p.n_tiles < ctx->num_sms ? p.n_tiles : ctx->num_sms;
@@ -1427,7 +1382,6 @@ static yl_status gather_fprop(yl_ctx* ctx, const ConvGather& g, const float* w, 
 
 yl_status conv_fprop(yl_ctx* ctx, const ConvGather& g, const float* w, int n_rows,
                      const ConvEpilogue& e) {
-  if (e.gnb_out) *e.gnb_out = GnBwdTiles{};  // filled only by a plan that writes the sums
   int sw = 0, sh = 0;
   // fewer than 32 channels (RGB frames, the RGB head's dy): each tap reads one
   // 32-channel box of which the channels past cin read as zero, against

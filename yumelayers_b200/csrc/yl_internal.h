@@ -75,10 +75,8 @@ struct yl_ctx {
   // partials, reduction partials); 1 = layout conversions of a C-ABI call.
   // slot 0: operator temporaries; 1: NCHW<->NHWC staging of the batched
   // C-ABI entry points; 2: GroupNorm statistics partials written by a conv
-  // 3: GroupNorm backward partials written by a dX conv for the GroupNorm
-  // backward that follows it
-  void* scratch[4] = {nullptr, nullptr, nullptr, nullptr};
-  size_t scratch_bytes[4] = {0, 0, 0, 0};
+  void* scratch[3] = {nullptr, nullptr, nullptr};
+  size_t scratch_bytes[3] = {0, 0, 0};
 };
 
 namespace yl {

@@ -52,30 +52,6 @@ struct ConvEpilogue {
   // set by conv_fprop: per-tile partial sums (float2) and channels per group
   float2* gn_part = nullptr;
   int gn_cg = 0;
-  // GroupNorm backward partials: when gnb_x is set, the output is the
-  // gradient of a GroupNorm(groups = gnb_groups) + SiLU whose input is gnb_x
-  // (pixel stride gnb_ldx, the output's pixel grid), and conv_fprop may also
-  // write that GroupNorm's backward sums per (tile, channel): (sum da*xh,
-  // sum da) over the tile's pixels, xh = (x - mean) * rstd, a = xh * gamma +
-  // beta, da = dout * silu'(a).  It does so for plans whose tiles hold all
-  // pixels of one output phase with the transposed accumulator, and then
-  // fills *gnb_out (which it leaves cleared otherwise).
-  const float* gnb_x = nullptr;
-  int gnb_ldx = 0;
-  const float *gnb_mean = nullptr, *gnb_rstd = nullptr;
-  const float *gnb_gamma = nullptr, *gnb_beta = nullptr;
-  int gnb_groups = 0;
-  struct GnBwdTiles* gnb_out = nullptr;
-  float2* gnb_part = nullptr;  // set by conv_fprop
-};
-
-// Where a conv left the GroupNorm backward sums of its output (see
-// ConvEpilogue::gnb_x): part[(pix_tile * n_nblk + nb) * bn + c_local] for the
-// pix_tiles pixel tiles of each of n_img images (image-major), channel
-// nb * bn + c_local.  part == nullptr: the conv did not write them.
-struct GnBwdTiles {
-  float2* part = nullptr;
-  int n_img = 0, tiles_per_img = 0, n_nblk = 0, bn = 0;
 };
 
 // True when conv_fprop can produce GroupNorm statistics for this epilogue.

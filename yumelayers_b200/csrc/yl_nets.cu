@@ -361,7 +361,7 @@ yl_status ConvL::forward(Net& net, const Act& x, const Act& y, const float* resi
 
 yl_status ConvL::backward(Net& net, const Act& x, const Act& dy, const Act* dx,
                           const float* dx_addend, int ld_addend, float* dbias2d, int up, int hv,
-                          int wv, GNL* gn_prev, const Act* gn_in) {
+                          int wv) {
   yl_ctx* ctx = net.ctx;
   if (rgb == 1 && !up && !dbias2d) {
     // dW[co][t*4 + ci] = sum_p dy[p][co] * patches(x)[p][t*4 + ci]; db fused
@@ -467,17 +467,6 @@ yl_status ConvL::backward(Net& net, const Act& x, const Act& dy, const Act* dx,
   e.residual = up ? nullptr : dx_addend;
   e.ldr = ld_addend;
   e.round_tf32 = 1;
-  if (gn_prev && gn_in && !up && gn_prev->c == cin_p && gn_in->ld % 4 == 0) {
-    // dX is the gradient of gn_prev's output: its backward sums come along
-    e.gnb_x = gn_in->p;
-    e.gnb_ldx = gn_in->ld;
-    e.gnb_mean = gn_prev->mean;
-    e.gnb_rstd = gn_prev->rstd;
-    e.gnb_gamma = gn_prev->gamma;
-    e.gnb_beta = gn_prev->beta;
-    e.gnb_groups = gn_prev->G;
-    e.gnb_out = &gn_prev->tiles;
-  }
   net.prof_begin(1);
   if (dominant(net, x.h, x.w, up)) net.prof_mark_dominant();
   YL_TRY(conv_fprop(ctx, gd, Wd, cin_p, e));
@@ -533,13 +522,11 @@ yl_status GNL::forward(Net& net, const Act& x, const Act& y) {
 yl_status GNL::backward(Net& net, const Act& x, const Act& dy, const Act& dx, const float* addend,
                         int ldadd) {
   net.prof_begin(4);
-  const bool from_tiles = tiles.part != nullptr;  // no separate pass over x and dy
   yl_status st = gn_silu_backward(net.ctx, x.p, dy.p, dy.ld, x.n, c, G, (long long)x.h * x.w, x.ld,
                                   mean, rstd, gamma, beta, 1, addend, ldadd, dx.p, dx.ld, 1, ggamma,
-                                  gbeta, 0, tiles.part ? &tiles : nullptr);
-  tiles = GnBwdTiles{};  // they belonged to this dy
+                                  gbeta, 0);
   const double e = (double)x.n * x.h * x.w * c;
-  net.prof_end(4, 0.0, 4.0 * ((from_tiles ? 2 : 4) * e + (addend ? e : 0) + e));
+  net.prof_end(4, 0.0, 4.0 * (4 * e + (addend ? e : 0) + e));
   return st;
 }
 
@@ -620,10 +607,9 @@ yl_status RB::backward(Net& net, const Act& x, const Act& dy, const Act& dx) {
   dh2.ld = h2.c;
   dc1.ld = c1o.c;
   dh1.ld = h1.c;
-  YL_TRY(c2.backward(net, h2, dy, &dh2, nullptr, 0, nullptr, 0, 0, 0, &gn2, &c1o));
+  YL_TRY(c2.backward(net, h2, dy, &dh2));
   YL_TRY(gn2.backward(net, c1o, dh2, dc1));
-  YL_TRY(c1.backward(net, h1, dc1, &dh1, nullptr, 0, has_temb ? dproj : nullptr, 0, 0, 0, &gn1,
-                     &x));
+  YL_TRY(c1.backward(net, h1, dc1, &dh1, nullptr, 0, has_temb ? dproj : nullptr));
   if (has_skip) {
     Act dxs = x;
     YL_TRY(net.pool.get(x.elems(), &dxs.p));

@@ -89,13 +89,9 @@ struct ConvL {
   yl_status forward(Net& net, const Act& x, const Act& y, const float* residual = nullptr,
                     int ldr = 0, const float* bias2d = nullptr, int up = 0, int hv = 0,
                     int wv = 0, struct GNL* gn_next = nullptr);
-  // gn_prev / gn_in: the GroupNorm(+SiLU) whose output dx is the gradient of,
-  // and that GroupNorm's input: the dX conv may then also write the
-  // GroupNorm backward's sums (gn_prev->tiles)
   yl_status backward(Net& net, const Act& x, const Act& dy, const Act* dx,
                      const float* dx_addend = nullptr, int ld_addend = 0,
-                     float* dbias2d = nullptr, int up = 0, int hv = 0, int wv = 0,
-                     struct GNL* gn_prev = nullptr, const Act* gn_in = nullptr);
+                     float* dbias2d = nullptr, int up = 0, int hv = 0, int wv = 0);
   bool dominant(const struct Net& net, int h, int w, int up) const;
   bool crop_up(const Act& x, int up, int hv, int wv) const;
   yl_status upsampled(struct Net& net, const Act& x, int hv, int wv, Act* out) const;
@@ -108,7 +104,6 @@ struct GNL {
   float *gamma = nullptr, *beta = nullptr, *ggamma = nullptr, *gbeta = nullptr;
   float *mean = nullptr, *rstd = nullptr;
   bool stats_ready = false;  // mean/rstd already written by the producing conv
-  GnBwdTiles tiles;          // backward sums written by the conv that produced dy
   void setup(Net& net, const char* name, int c);
   yl_status bind(Net& net, int n);
   yl_status init(yl_ctx* ctx, uint64_t seed);

@@ -417,79 +417,6 @@ __global__ void __launch_bounds__(256, 4)
   }
 }
 
-// The backward sums from a dX conv's per-(tile, channel) partials (see
-// ConvEpilogue::gnb_x) instead of a pass over x and dy.  Stage 1: per (image,
-// chunk of its pixel tiles, channel), the chunk's tiles in order, in double.
-constexpr int kGnTileChunks = 32;
-
-__global__ void __launch_bounds__(128)
-    gn_bwd_tile_chunk_kernel(const float2* __restrict__ part, int tiles_per_img, int n_nblk,
-                             int bn, int c, double2* __restrict__ out) {
-  const int chunk = blockIdx.x, img = blockIdx.y;
-  const int per = (tiles_per_img + kGnTileChunks - 1) / kGnTileChunks;
-  const int t0 = chunk * per, t1 = min(tiles_per_img, t0 + per);
-  for (int nb = 0; nb < n_nblk; ++nb) {
-    for (int cl = threadIdx.x; cl < bn; cl += blockDim.x) {
-      const int ch = nb * bn + cl;
-      if (ch >= c) break;
-      double a = 0.0, b = 0.0;
-      for (int t = t0; t < t1; ++t) {
-        const float2 v = part[(((long long)img * tiles_per_img + t) * n_nblk + nb) * bn + cl];
-        a += v.x;
-        b += v.y;
-      }
-      out[((long long)img * kGnTileChunks + chunk) * c + ch] = make_double2(a, b);
-    }
-  }
-}
-
-// Stage 2: one warp per (image, group) -> coef = (mean(dxh), mean(dxh*xh))
-// with dxh = da * gamma (from the channel sums), and one warp per channel ->
-// dgamma, dbeta over the images; fixed-order sums.
-__global__ void gn_bwd_tile_final_kernel(const double2* __restrict__ chunks, int n, int c, int g,
-                                         long long hw, const float* __restrict__ gamma,
-                                         float* __restrict__ coef, float* dgamma, float* dbeta,
-                                         int accumulate) {
-  const int wid = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
-  const int lane = threadIdx.x & 31;
-  const int cg = c / g;
-  double a = 0.0, b = 0.0;  // (sum da*xh, sum da), gamma-weighted for a group
-  if (wid < n * g) {
-    const int img = wid / g, grp = wid % g;
-    for (int i = lane; i < cg * kGnTileChunks; i += 32) {
-      const int ch = grp * cg + i / kGnTileChunks, k = i % kGnTileChunks;
-      const double ga = gamma ? (double)gamma[ch] : 1.0;
-      const double2 v = chunks[((long long)img * kGnTileChunks + k) * c + ch];
-      a += ga * v.x;
-      b += ga * v.y;
-    }
-  } else if (wid < n * g + c) {
-    const int ch = wid - n * g;
-    for (int i = lane; i < n * kGnTileChunks; i += 32) {
-      const double2 v = chunks[(long long)i * c + ch];
-      a += v.x;
-      b += v.y;
-    }
-  } else {
-    return;
-  }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    a += __shfl_xor_sync(0xffffffffu, a, o);
-    b += __shfl_xor_sync(0xffffffffu, b, o);
-  }
-  if (lane) return;
-  if (wid < n * g) {
-    const double cnt = (double)hw * cg;
-    coef[2 * wid] = (float)(b / cnt);
-    coef[2 * wid + 1] = (float)(a / cnt);
-  } else {
-    const int ch = wid - n * g;
-    if (dgamma) dgamma[ch] = accumulate ? dgamma[ch] + (float)a : (float)a;
-    if (dbeta) dbeta[ch] = accumulate ? dbeta[ch] + (float)b : (float)b;
-  }
-}
-
 static yl_status gn_check(int n, int c, int g, long long hw, int ps) {
   YL_CHECK(n > 0 && hw > 0 && g > 0 && c % g == 0, YL_ERR_SHAPE,
            "groupnorm: channels %d not divisible by groups %d", c, g);
@@ -565,31 +492,11 @@ yl_status gn_silu_backward(yl_ctx* ctx, const float* x, const float* dy, int ldd
                            int g, long long hw, int ps, const float* mean, const float* rstd,
                            const float* gamma, const float* beta, int silu, const float* addend,
                            int ldadd, float* dx, int lddx, int round, float* dgamma, float* dbeta,
-                           int accumulate_params, const GnBwdTiles* tiles) {
+                           int accumulate_params) {
   YL_TRY(gn_check(n, c, g, hw, ps));
   YL_CHECK(lddy % 4 == 0 && lddx % 4 == 0 && (!addend || ldadd % 4 == 0), YL_ERR_SHAPE,
            "groupnorm backward: strides must be multiples of 4");
   GnGeom q = gn_geom(n, c, g, hw, ps);
-  if (tiles && tiles->part && silu && tiles->n_img == n && tiles->n_nblk * tiles->bn >= c) {
-    const size_t chunk_bytes = (size_t)n * kGnTileChunks * c * sizeof(double2);
-    const size_t coef_off = (chunk_bytes + 255) & ~size_t(255);
-    void* ws = nullptr;
-    YL_TRY(scratch_get(ctx, coef_off + (size_t)n * g * 2 * sizeof(float), &ws));
-    double2* chunks = (double2*)ws;
-    float* coef = (float*)((char*)ws + coef_off);
-    gn_bwd_tile_chunk_kernel<<<dim3(kGnTileChunks, n), 128, 0, ctx->stream>>>(
-        tiles->part, tiles->tiles_per_img, tiles->n_nblk, tiles->bn, c, chunks);
-    YL_TRY(check_launch("gn_bwd_tile_chunk_kernel"));
-    const int warps = n * g + c;
-    gn_bwd_tile_final_kernel<<<(warps + 7) / 8, 256, 0, ctx->stream>>>(
-        chunks, n, c, g, hw, gamma, coef, dgamma, dbeta, accumulate_params);
-    YL_TRY(check_launch("gn_bwd_tile_final_kernel"));
-    const int agrid =
-        resident_grid(ctx, gn_bwd_apply_kernel, q.quads * q.rows, (long long)n * q.achunks);
-    gn_bwd_apply_kernel<<<agrid, q.quads * q.rows, 0, ctx->stream>>>(
-        x, dy, lddy, q, mean, rstd, gamma, beta, silu, coef, addend, ldadd, dx, lddx, round);
-    return check_launch("gn_bwd_apply_kernel");
-  }
   const int nsh = 2 * g + 2 * c;
   size_t part_bytes = (size_t)n * q.chunks * nsh * sizeof(double);
   size_t coef_off = (part_bytes + 255) & ~size_t(255);

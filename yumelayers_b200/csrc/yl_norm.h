@@ -20,16 +20,13 @@ yl_status gn_silu_forward(yl_ctx* ctx, const float* x, int n, int c, int g, long
 yl_status gn_silu_apply(yl_ctx* ctx, const float* x, int n, int c, int g, long long hw, int ps,
                         const float* mean, const float* rstd, const float* gamma,
                         const float* beta, int silu, float* y, int ldy, int round);
-struct GnBwdTiles;
 // dx = d/dx of the forward given dy (+ addend); dgamma/dbeta overwritten or
-// accumulated.  With `tiles` holding the per-(tile, channel) sums the conv
-// that produced dy wrote (silu = 1 only), those replace the first read of
-// x and dy.
+// accumulated.
 yl_status gn_silu_backward(yl_ctx* ctx, const float* x, const float* dy, int lddy, int n, int c,
                            int g, long long hw, int ps, const float* mean, const float* rstd,
                            const float* gamma, const float* beta, int silu, const float* addend,
                            int ldadd, float* dx, int lddx, int round, float* dgamma, float* dbeta,
-                           int accumulate_params, const GnBwdTiles* tiles = nullptr);
+                           int accumulate_params);
 
 struct AdamTensor {
   float* param;

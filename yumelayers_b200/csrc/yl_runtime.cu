@@ -96,7 +96,7 @@ yl_status yl_ctx_destroy(yl_ctx* ctx) {
   if (!ctx) return YL_OK;
   cudaSetDevice(ctx->device);
   cudaStreamSynchronize(ctx->stream);
-  for (int s = 0; s < 4; ++s)
+  for (int s = 0; s < 3; ++s)
     if (ctx->scratch[s]) cudaFreeAsync(ctx->scratch[s], ctx->stream);
   cudaStreamSynchronize(ctx->stream);
   cudaFree(ctx->dev_err);
