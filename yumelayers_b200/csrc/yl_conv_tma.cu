@@ -217,14 +217,8 @@ __device__ __forceinline__ void gn_chunk_partials_any(int cg, const float (&v)[3
 // TMEM then holds [channel][pixel]: epilogue thread = one output channel,
 // and each store instruction of a warp writes 32 consecutive channels of one
 // pixel.
-// Threads of the forward kernel: 4 epilogue warps, the TMA warp, the MMA
-// warp; transposed tiles get a second epilogue warpgroup (warps 6-9) that
-// drains the second half of each tile's lattice rows.
-template <bool TR>
-constexpr int fprop_threads() { return TR ? kThreads + 128 : kThreads; }
-
 template <int BN, int MT, bool TR = false, bool HALO = false>
-__global__ void __launch_bounds__(fprop_threads<TR>(), 1)
+__global__ void __launch_bounds__(kThreads, 1)
     conv_tma_fprop_kernel(const __grid_constant__ CUtensorMap ta0,
                           const __grid_constant__ CUtensorMap ta1,
                           const __grid_constant__ CUtensorMap ta2,
@@ -237,7 +231,6 @@ __global__ void __launch_bounds__(fprop_threads<TR>(), 1)
                           int* err) {
   static_assert(!HALO || (TR && BN == 128 && MT == 2), "halo boxes feed the transposed tile");
   using Cfg = FpropCfg<BN, MT>;
-  constexpr int kEpiWarps = TR ? 8 : 4;
   constexpr int S = Cfg::kStages;
   constexpr int kRows = 4 * MT;  // lattice rows per tile
   constexpr int kRing = HALO ? HaloCfg::kRing : S * Cfg::kStage + Cfg::kOut;
@@ -250,10 +243,10 @@ __global__ void __launch_bounds__(fprop_threads<TR>(), 1)
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + kRing);
   uint64_t* empty = full + S;
   uint64_t* acc_full = full + kRingBars;  // [2]: MMA -> epilogue
-  uint64_t* acc_empty = acc_full + 2;     // [2]: epilogue threads -> MMA
+  uint64_t* acc_empty = acc_full + 2;     // [2]: epilogue (128 threads) -> MMA
   uint64_t* drain = acc_empty + 2;        // MMA thread: all of its MMAs completed
   uint64_t* tfull = drain + 1;            // [kTileRing]: producer -> MMA + epilogue
-  uint64_t* tempty = tfull + kTileRing;   // [kTileRing]: MMA + epilogue warps -> producer
+  uint64_t* tempty = tfull + kTileRing;   // [kTileRing]: MMA + 4 epilogue warps -> producer
   int* tring = reinterpret_cast<int*>(tempty + kTileRing);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tring + kTileRing);
   static_assert(kTileRing == 8, "the shared-memory budgets above reserve 8 ring slots");
@@ -265,12 +258,12 @@ __global__ void __launch_bounds__(fprop_threads<TR>(), 1)
     for (int s = 0; s < kRingBars; ++s) mbar_init(&full[s], 1);
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], kEpiWarps * 32);
+      mbar_init(&acc_empty[b], 128);
     }
     mbar_init(drain, 1);
     for (int r = 0; r < kTileRing; ++r) {
       mbar_init(&tfull[r], 1);
-      mbar_init(&tempty[r], 1 + kEpiWarps);
+      mbar_init(&tempty[r], 1 + 4);
     }
     fence_barrier_init();
   }
@@ -494,15 +487,9 @@ __global__ void __launch_bounds__(fprop_threads<TR>(), 1)
       mbar_wait(drain, 0);
     }
   } else {
-    // epilogue: warp w owns TMEM lanes 32(w % 4) .. +31 (a warp may only
-    // touch its quarter of the lanes).  Plain tiles: lattice row 4m + w of
-    // subtile m.  Transposed tiles: output channels, and the two warpgroups
-    // (warps 0-3, 6-9) take the first and second half of the lattice rows.
-    const int quarter = warp & 3;
-    const int ew = warp < 4 ? warp : warp - 2;  // epilogue warp 0 .. kEpiWarps-1
-    const int half = TR ? (ew >> 2) : 0;
+    // epilogue: warp w owns TMEM lanes 32w..32w+31 = lattice row 4m + w of subtile m
     int tc = 0;
-    uint32_t ost = 0;  // TMA-stored row chunks of this warp
+    uint32_t ost = 0;  // TMA-stored row chunks of this warp (staging buffer = ost & 1)
     for (uint32_t k = 0;; ++k, ++tc) {
       const int tile = ring_take_warp(tfull, tempty, tring, k, lim, lane);
       if (tile == kRingTimeout) {
@@ -518,11 +505,11 @@ __global__ void __launch_bounds__(fprop_threads<TR>(), 1)
         // while the accumulator is still being computed: pull this tile's
         // residual into L2, one 128-byte line of 32 channels per thread and
         // lattice row
-        const int t = quarter * 32 + lane, q = t >> 2, ch = n0 + (t & 3) * 32;
+        const int t = warp * 32 + lane, q = t >> 2, ch = n0 + (t & 3) * 32;
         const int gx = c.tx * 32 + q, X = gx * p.xs + ph.xa;
         if (e.residual && ch < e.n_total && gx < p.gw && X < p.out_w) {
 #pragma unroll 1
-          for (int j = half * (kRows / 2); j < (half + 1) * (kRows / 2); ++j) {
+          for (int j = 0; j < kRows; ++j) {
             const int gy = c.ty * kRows + j, Y = gy * p.ys + ph.ya;
             if (gy >= p.gh || Y >= p.out_h) break;
             const long long pix = ((long long)c.img * p.out_h + Y) * p.out_w + X;
@@ -537,16 +524,16 @@ __global__ void __launch_bounds__(fprop_threads<TR>(), 1)
       tc_fence_after();
       if constexpr (TR) {
         // lane row = output channel, column = pixel (lattice row j of the tile, column q)
-        const int co = n0 + quarter * 32 + lane;
+        const int co = n0 + warp * 32 + lane;
         const bool cval = co < e.n_total;
         float badd = 0.f;
         if (cval && e.bias) badd += __ldg(e.bias + co);
         if (cval && e.bias2d) badd += __ldg(e.bias2d + (long long)c.img * e.n_total + co);
         const uint32_t tbase =
-            tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(buf * Cfg::kAccCols);
+            tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)(buf * Cfg::kAccCols);
         float gs = 0.f, gss = 0.f;  // GroupNorm partials of this channel
 #pragma unroll 1
-        for (int j = half * (kRows / 2); j < (half + 1) * (kRows / 2); ++j) {
+        for (int j = 0; j < kRows; ++j) {
           uint32_t r[32];
           tmem_ld_32x32b_x32(tbase + (uint32_t)(j * 32), r);
           tmem_ld_wait();
@@ -587,11 +574,9 @@ __global__ void __launch_bounds__(fprop_threads<TR>(), 1)
             // staging row q = pixel q, this lane's channel at 4-byte column
             // `lane` of the 128-byte row (16-byte chunks swizzled by q), then
             // one TMA store of the warp's 32 pixels x 32 channels
-            // one 4 KB staging buffer per epilogue warp: wait until the
-            // previous store of this warp has read it
-            uint8_t* ob = smem + kOutOff + ew * 4096;
-            if (ost >= 1) {
-              if (lane == 0) bulk_wait_group_read<0>();
+            uint8_t* ob = smem + kOutOff + (warp * 2 + (ost & 1)) * 4096;
+            if (ost >= 2) {
+              if (lane == 0) bulk_wait_group_read<1>();
               __syncwarp();
             }
             const uint32_t col = (uint32_t)(lane & 3) << 2;
@@ -603,7 +588,7 @@ __global__ void __launch_bounds__(fprop_threads<TR>(), 1)
             __syncwarp();
             if (lane == 0) {
               const CUtensorMap* om = c.z == 0 ? &to0 : c.z == 1 ? &to1 : c.z == 2 ? &to2 : &to3;
-              tma_store_4d(om, smem_u32(ob), n0 + quarter * 32, c.tx * 32, gy, c.img);
+              tma_store_4d(om, smem_u32(ob), n0 + warp * 32, c.tx * 32, gy, c.img);
               bulk_commit_group();
             }
             ++ost;
@@ -621,10 +606,9 @@ __global__ void __launch_bounds__(fprop_threads<TR>(), 1)
             gs += __shfl_xor_sync(0xffffffffu, gs, o);
             gss += __shfl_xor_sync(0xffffffffu, gss, o);
           }
-          const int gpb = BN / e.gn_cg;  // two slots per tile: the two row halves
+          const int gpb = BN / e.gn_cg;
           if ((lane & (e.gn_cg - 1)) == 0)
-            e.gn_part[((long long)tile * 2 + half) * gpb + (quarter * 32 + lane) / e.gn_cg] =
-                make_float2(gs, gss);
+            e.gn_part[(long long)tile * gpb + (warp * 32 + lane) / e.gn_cg] = make_float2(gs, gss);
         }
         tc_fence_before();
         mbar_arrive(&acc_empty[buf]);
@@ -1285,7 +1269,7 @@ static yl_status launch_plan(yl_ctx* ctx, const View* views, int nviews, const f
   YL_CHECK(tiles > 0 && tiles < (1LL << 31), YL_ERR_SHAPE, "conv: %lld tiles", tiles);
   p.n_tiles = (int)tiles;
   ConvEpilogue ek = e;
-  const int slots = TR ? 2 : MT * 4;
+  const int slots = TR ? 1 : MT * 4;
   int gpb = 0;
   if (e.gn_mean) {
     YL_CHECK(conv_gn_stats_supported(e.n_total, e.gn_groups) && BN % (e.n_total / e.gn_groups) == 0,
@@ -1312,7 +1296,7 @@ static yl_status launch_plan(yl_ctx* ctx, const View* views, int nviews, const f
       macs += (double)p.n_img * rows * cols * ph.ntaps * p.cpt * 32.0 * e.n_total;
   }
   ctx->last_exec_flops[0] = 2.0 * macs;
-  conv_tma_fprop_kernel<BN, MT, TR, HALO><<<grid, fprop_threads<TR>(), kSmem, ctx->stream>>>(
+  conv_tma_fprop_kernel<BN, MT, TR, HALO><<<grid, kThreads, kSmem, ctx->stream>>>(
       ta[0], ta[1], ta[2], ta[3], tw, to[0], to[1], to[2], to[3], p, ek, ctx->dev_err);
   YL_TRY(check_launch("conv_tma_fprop_kernel"));
   if (!e.gn_mean) return YL_OK;
