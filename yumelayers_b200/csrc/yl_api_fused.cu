@@ -189,12 +189,13 @@ yl_status yl_conv2d_bwd_data(yl_ctx* ctx, const yl_conv_desc* d, const float* dy
   e.ldo = s.cp;
   e.n_total = d->c;
   e.round_tf32 = 0;
-  if (d->up && s.ih == 2 * d->h && s.iw == 2 * d->w) {
-    // upsample conv: dX at the source resolution through the merged phase taps
+  if (d->up && d->k == 3 && d->pad == 1 && d->stride == 1) {
+    // upsample conv (the x2 grid, or one cut by a row / column): dX at the
+    // source resolution through the merged phase taps
     ConvEpilogue eu = e;
     eu.out = dxh;
-    const yl_status st =
-        conv_dgrad_upsampled(ctx, dyh, s.ocp, s.ocp, d->n, d->h, d->w, wd, d->c, eu);
+    const yl_status st = conv_dgrad_upsampled(ctx, dyh, s.ocp, s.ocp, d->n, d->h, d->w, s.ih,
+                                              s.iw, wd, d->c, eu);
     if (st == YL_OK) return from_internal(ctx, dxh, s.cp, d->layout, d->n, d->c, hw_in, dx);
     if (st != YL_ERR_UNSUPPORTED) return st;
   }

@@ -816,39 +816,6 @@ __global__ void downsample_sum_nhwc_kernel(const float* __restrict__ src, int uh
   }
 }
 
-// Nearest x2 upsample cut to uh x uw (upsample2x_kernel,
-// MetalKernelSourcesA.swift:425, with the decoder's crop): dst[y][x] =
-// src[y / 2][x / 2], four channels per thread.
-__global__ void upsample_nearest_nhwc_kernel(const float* __restrict__ src, int n, int h, int w,
-                                             int c4, int ps_src, float* __restrict__ dst, int uh,
-                                             int uw, int ps_dst) {
-  const long long total = (long long)n * uh * uw * c4;
-  for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < total;
-       idx += (long long)gridDim.x * blockDim.x) {
-    const int cq = (int)(idx % c4);
-    long long r = idx / c4;
-    const int x = (int)(r % uw);
-    r /= uw;
-    const int y = (int)(r % uh);
-    const int img = (int)(r / uh);
-    const float4 v = __ldg(reinterpret_cast<const float4*>(
-        src + (((long long)img * h + y / 2) * w + x / 2) * ps_src + 4 * cq));
-    *reinterpret_cast<float4*>(dst + (((long long)img * uh + y) * uw + x) * ps_dst + 4 * cq) = v;
-  }
-}
-
-yl_status upsample_nearest_nhwc(yl_ctx* ctx, const float* src, int n, int h, int w, int c,
-                                int ps_src, float* dst, int uh, int uw, int ps_dst) {
-  YL_CHECK(c % 4 == 0 && ps_src % 4 == 0 && ps_dst % 4 == 0, YL_ERR_SHAPE,
-           "upsample_nearest_nhwc: channels must be multiples of 4");
-  YL_CHECK(uh <= 2 * h && uw <= 2 * w, YL_ERR_SHAPE, "upsample_nearest_nhwc: %dx%d from %dx%d",
-           uh, uw, h, w);
-  long long total = (long long)n * uh * uw * (c / 4);
-  upsample_nearest_nhwc_kernel<<<grid_1d(total, 256), 256, 0, ctx->stream>>>(
-      src, n, h, w, c / 4, ps_src, dst, uh, uw, ps_dst);
-  return check_launch("upsample_nearest_nhwc_kernel");
-}
-
 yl_status downsample_sum_nhwc(yl_ctx* ctx, const float* src, int uh, int uw, float* dst, int n,
                               int h, int w, int c, int ps_src, int ps_dst) {
   YL_CHECK(c % 4 == 0 && ps_src % 4 == 0 && ps_dst % 4 == 0, YL_ERR_SHAPE,

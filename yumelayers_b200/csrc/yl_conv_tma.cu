@@ -1114,6 +1114,160 @@ __global__ void s2_phase_weights_kernel(const float* __restrict__ wd, float* __r
   }
 }
 
+// ------------------------------------------------------------------ cropped x2 grids
+// A nearest-x2 upsample cut to hv x wv (hv in {2sh - 1, 2sh}, wv in {2sw - 1,
+// 2sw}) runs through the merged phase taps of the whole 2sh x 2sw grid U,
+// whose phase outputs the tensor maps clip to the cut grid u.  The merged
+// taps then still read U's pixels outside u -- the last upsampled column
+// (X' = wv when wv < 2sw) and row (Y' = hv when hv < 2sh), which u's zero
+// padding replaces -- and only the outputs next to the cut see them.  These
+// kernels subtract exactly those terms: a few border pixels' worth of work.
+
+// One border pixel of a cut grid of ext_h x ext_w: the last column (when
+// col) for rows [0, ext_h), then the last row (when row) for the columns the
+// column did not already cover.
+__device__ __forceinline__ void crop_border_pixel(int b, bool col, bool row, int ext_h, int ext_w,
+                                                  int* y, int* x) {
+  const int ncol = col ? ext_h : 0;
+  if (b < ncol) {
+    *y = b;
+    *x = ext_w - 1;
+  } else {
+    *y = ext_h - 1;
+    *x = b - ncol;
+  }
+  (void)row;
+}
+static int crop_border_count(bool col, bool row, int ext_h, int ext_w) {
+  return (col ? ext_h : 0) + (row ? ext_w - (col ? 1 : 0) : 0);
+}
+
+// Forward: out[img][Y][X][co] -= sum over taps (ky, kx) whose source pixel
+// (Y', X') = (Y + ky - 1, X + kx - 1) lies in U but not in u of
+// w[co][ky*3+kx][:] . x[img][Y'/2][X'/2][:], for the output pixels on the
+// cut row / column.  One warp per (image, border pixel, output channel),
+// lanes over input channels; rounded to tf32 again when the epilogue was.
+__global__ void up_crop_fix_fprop_kernel(const float* __restrict__ x, int ps, int sh, int sw,
+                                         int cin, const float* __restrict__ w, int cout, int n_img,
+                                         int hv, int wv, float* __restrict__ out, int ldo,
+                                         int round) {
+  const bool col = wv < 2 * sw, row = hv < 2 * sh;
+  const int nb = (col ? hv : 0) + (row ? wv - (col ? 1 : 0) : 0);
+  const long long items = (long long)n_img * nb * cout;
+  const int lane = threadIdx.x & 31;
+  const long long warps = (long long)gridDim.x * (blockDim.x >> 5);
+  for (long long it = blockIdx.x * (long long)(blockDim.x >> 5) + (threadIdx.x >> 5); it < items;
+       it += warps) {
+    const int co = (int)(it % cout);
+    const long long r = it / cout;
+    const int b = (int)(r % nb), img = (int)(r / nb);
+    int Y, X;
+    crop_border_pixel(b, col, row, hv, wv, &Y, &X);
+    float s = 0.f;
+    for (int ky = 0; ky < 3; ++ky) {
+      const int yy = Y + ky - 1;
+      if (yy < 0 || yy >= 2 * sh) continue;
+      for (int kx = 0; kx < 3; ++kx) {
+        const int xx = X + kx - 1;
+        if (xx < 0 || xx >= 2 * sw || (yy < hv && xx < wv)) continue;
+        const float* xp = x + (((long long)img * sh + (yy >> 1)) * sw + (xx >> 1)) * ps;
+        const float* wp = w + ((long long)co * 9 + ky * 3 + kx) * cin;
+        for (int ci = lane; ci < cin; ci += 32) s += wp[ci] * xp[ci];
+      }
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    if (lane == 0) {
+      float* op = out + (((long long)img * hv + Y) * wv + X) * ldo + co;
+      const float v = *op - s;
+      *op = round ? round_tf32(v) : v;
+    }
+  }
+}
+
+// dX at the source resolution: dx[img][i][j][ci] -= the part of the merged
+// sum that comes from the upsampled pixels of U outside u, du[Y'][X'] =
+// sum_taps wd[ci][ky*3+kx][:] . dy[img][Y' - ky + 1][X' - kx + 1][:] (dy is
+// hv x wv), over (Y', X') in {2i, 2i+1} x {2j, 2j+1} with Y' >= hv or X' >= wv.
+// One warp per (image, border source pixel, input channel), lanes over the
+// output-gradient channels.
+__global__ void up_crop_fix_dgrad_kernel(const float* __restrict__ dy, int ldy, int cout, int sh,
+                                         int sw, int hv, int wv, const float* __restrict__ wd,
+                                         int cin, int n_img, float* __restrict__ dx, int ldo,
+                                         int round) {
+  const bool col = wv < 2 * sw, row = hv < 2 * sh;
+  const int nb = (col ? sh : 0) + (row ? sw - (col ? 1 : 0) : 0);
+  const long long items = (long long)n_img * nb * cin;
+  const int lane = threadIdx.x & 31;
+  const long long warps = (long long)gridDim.x * (blockDim.x >> 5);
+  for (long long it = blockIdx.x * (long long)(blockDim.x >> 5) + (threadIdx.x >> 5); it < items;
+       it += warps) {
+    const int ci = (int)(it % cin);
+    const long long r = it / cin;
+    const int b = (int)(r % nb), img = (int)(r / nb);
+    int i, j;
+    crop_border_pixel(b, col, row, sh, sw, &i, &j);
+    float s = 0.f;
+    for (int vy = 2 * i; vy < 2 * i + 2; ++vy) {
+      for (int vx = 2 * j; vx < 2 * j + 2; ++vx) {
+        if (vy < hv && vx < wv) continue;  // a pixel of u: no excess
+        for (int ky = 0; ky < 3; ++ky) {
+          const int yy = vy - ky + 1;
+          if (yy < 0 || yy >= hv) continue;
+          for (int kx = 0; kx < 3; ++kx) {
+            const int xx = vx - kx + 1;
+            if (xx < 0 || xx >= wv) continue;
+            const float* dp = dy + (((long long)img * hv + yy) * wv + xx) * ldy;
+            const float* wp = wd + ((long long)ci * 9 + ky * 3 + kx) * cout;
+            for (int co = lane; co < cout; co += 32) s += wp[co] * dp[co];
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    if (lane == 0) {
+      float* op = dx + (((long long)img * sh + i) * sw + j) * ldo + ci;
+      const float v = *op - s;
+      *op = round ? round_tf32(v) : v;
+    }
+  }
+}
+
+// Filter gradient: dw[co][ky*3+kx][ci] -= sum over images and the output
+// pixels (Y, X) on the cut row / column whose tap source (Y', X') lies in U
+// but not in u of dy[img][Y][X][co] * x[img][Y'/2][X'/2][ci].  Only taps with
+// ky = 2 or kx = 2 reach outside u.  One thread per (co, tap, ci), fixed
+// summation order.
+__global__ void up_crop_fix_wgrad_kernel(const float* __restrict__ dy, int ldy, int cout,
+                                         const float* __restrict__ x, int ps, int cin, int sh,
+                                         int sw, int hv, int wv, int n_img,
+                                         float* __restrict__ dw) {
+  const bool col = wv < 2 * sw, row = hv < 2 * sh;
+  const int nb = (col ? hv : 0) + (row ? wv - (col ? 1 : 0) : 0);
+  const long long n = (long long)cout * 9 * cin;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int ci = (int)(i % cin);
+    const long long r = i / cin;
+    const int tap = (int)(r % 9), co = (int)(r / 9);
+    const int ky = tap / 3, kx = tap % 3;
+    if (ky != 2 && kx != 2) continue;
+    float s = 0.f;
+    for (int img = 0; img < n_img; ++img) {
+      for (int b = 0; b < nb; ++b) {
+        int Y, X;
+        crop_border_pixel(b, col, row, hv, wv, &Y, &X);
+        const int yy = Y + ky - 1, xx = X + kx - 1;
+        if (yy < 0 || yy >= 2 * sh || xx < 0 || xx >= 2 * sw || (yy < hv && xx < wv)) continue;
+        s += dy[(((long long)img * hv + Y) * wv + X) * ldy + co] *
+             x[(((long long)img * sh + (yy >> 1)) * sw + (xx >> 1)) * ps + ci];
+      }
+    }
+    dw[i] -= s;
+  }
+}
+
 // ------------------------------------------------------------------ host side
 struct View {
   const float* base;
@@ -1451,8 +1605,13 @@ yl_status conv_fprop(yl_ctx* ctx, const ConvGather& g, const float* w, int n_row
     }
     return run_plan(ctx, v, 4, w, n_rows, g.k_total, p, 1, e);
   }
-  if (g.mode == MODE_FPROP && g.up && g.stride == 1 && k3p1 && g.hv == 2 * sh && g.wv == 2 * sw) {
-    // nearest-x2 upsample + conv: four output phases, each a 2x2 conv on the source
+  if (g.mode == MODE_FPROP && g.up && g.stride == 1 && k3p1 && (g.hv + 1) / 2 == sh &&
+      (g.wv + 1) / 2 == sw && g.hv <= 2 * sh && g.wv <= 2 * sw && g.oh == g.hv &&
+      g.ow == g.wv) {
+    // nearest-x2 upsample + conv: four output phases, each a 2x2 conv on the
+    // source; a cut grid (hv or wv odd) clips the phase outputs, and the
+    // terms of the cut pixels are subtracted afterwards
+    const bool cut = g.hv != 2 * sh || g.wv != 2 * sw;
     void* wsb = nullptr;
     YL_TRY(scratch_get(ctx, (size_t)4 * n_rows * 4 * g.cin * sizeof(float), &wsb));
     float* wm = (float*)wsb;
@@ -1474,7 +1633,19 @@ yl_status conv_fprop(yl_ctx* ctx, const ConvGather& g, const float* w, int n_row
         tp.dx[t] = (int8_t)((t & 1) + b - 1);
       }
     }
-    return run_plan(ctx, &v, 1, wm, 4 * n_rows, 4 * g.cin, p, 4, e);
+    if (!cut) return run_plan(ctx, &v, 1, wm, 4 * n_rows, 4 * g.cin, p, 4, e);
+    // GroupNorm statistics must see the corrected border: a separate pass
+    ConvEpilogue ec = e;
+    ec.gn_mean = ec.gn_rstd = nullptr;
+    YL_TRY(run_plan(ctx, &v, 1, wm, 4 * n_rows, 4 * g.cin, p, 4, ec));
+    const long long items =
+        (long long)n_img * crop_border_count(g.wv < 2 * sw, g.hv < 2 * sh, g.hv, g.wv) * e.n_total;
+    up_crop_fix_fprop_kernel<<<grid_1d(items * 32, 256), 256, 0, ctx->stream>>>(
+        g.src, g.ps, sh, sw, g.cin, w, e.n_total, n_img, g.hv, g.wv, e.out, e.ldo, e.round_tf32);
+    YL_TRY(check_launch("up_crop_fix_fprop_kernel"));
+    if (!e.gn_mean) return YL_OK;
+    return gn_stats(ctx, e.out, n_img, e.n_total, e.gn_groups, (long long)g.oh * g.ow, e.ldo,
+                    e.gn_eps, 0, e.gn_mean, e.gn_rstd);
   }
   if (g.mode == MODE_DGRAD && g.stride == 2 && k3p1 && sw == g.wv && sh == g.hv) {
     // stride-2 dX: output phase (a, b) gathers the dy taps whose parity matches
@@ -1510,12 +1681,16 @@ yl_status conv_fprop(yl_ctx* ctx, const ConvGather& g, const float* w, int n_row
 // dX of a nearest-x2 upsample + 3x3 conv (pad 1) at the source resolution
 // sh x sw: dX[u][v] = sum over the four output phases (a, b) and their 2x2
 // merged taps of Wm[ph][t]^T dy_ph[u + 1 - a - ty][v + 1 - b - tx], with
-// dy_ph the phase views of dy (2sh x 2sw).  16 taps at the source
-// resolution instead of 9 at the output resolution plus a 2x2 sum.
+// dy_ph the phase views of dy (hv x wv, the x2 grid, possibly cut by one row
+// and / or column; the views read zero past the cut).  16 taps at the source
+// resolution instead of 9 at the output resolution plus a 2x2 sum; a cut
+// grid then has the terms of its cut pixels subtracted on the border.
 yl_status conv_dgrad_upsampled(yl_ctx* ctx, const float* dy, int ldy, int cout, int n, int sh,
-                               int sw, const float* wd, int rows, const ConvEpilogue& e) {
+                               int sw, int hv, int wv, const float* wd, int rows,
+                               const ConvEpilogue& e) {
   if (cout % 32 != 0 || ldy % 4 != 0 || ((uintptr_t)dy & 15) != 0 || sh < 1 || sw < 1 ||
-      e.n_total <= 0 || e.ldo < e.n_total)
+      e.n_total <= 0 || e.ldo < e.n_total || (hv + 1) / 2 != sh || (wv + 1) / 2 != sw ||
+      hv > 2 * sh || wv > 2 * sw || (e.gn_mean && (hv != 2 * sh || wv != 2 * sw)))
     return YL_ERR_UNSUPPORTED;
   void* wsb = nullptr;
   YL_TRY(scratch_get(ctx, (size_t)rows * 16 * cout * sizeof(float), &wsb));
@@ -1524,8 +1699,10 @@ yl_status conv_dgrad_upsampled(yl_ctx* ctx, const float* dy, int ldy, int cout, 
       wd, wm, rows, cout);
   YL_TRY(check_launch("up_merge_dgrad_weights_kernel"));
   View v[4];
+  for (int ph = 0; ph < 4; ++ph) v[ph] = phase_view(dy, cout, wv, hv, n, ldy, ph >> 1, ph & 1);
+  // a one-pixel dy has empty phase views: the plain path covers it
   for (int ph = 0; ph < 4; ++ph)
-    v[ph] = phase_view(dy, cout, 2 * sw, 2 * sh, n, ldy, ph >> 1, ph & 1);
+    if (v[ph].w < 1 || v[ph].h < 1) return YL_ERR_UNSUPPORTED;
   ConvPlan p{};
   p.cpt = cout / 32;
   p.n_img = n;
@@ -1538,7 +1715,13 @@ yl_status conv_dgrad_upsampled(yl_ctx* ctx, const float* dy, int ldy, int cout, 
     tp.dy[pt] = (int8_t)(1 - (ph >> 1) - (t >> 1));
     tp.dx[pt] = (int8_t)(1 - (ph & 1) - (t & 1));
   }
-  return run_plan(ctx, v, 4, wm, rows, 16 * cout, p, 1, e);
+  YL_TRY(run_plan(ctx, v, 4, wm, rows, 16 * cout, p, 1, e));
+  if (hv == 2 * sh && wv == 2 * sw) return YL_OK;
+  const long long items =
+      (long long)n * crop_border_count(wv < 2 * sw, hv < 2 * sh, sh, sw) * e.n_total;
+  up_crop_fix_dgrad_kernel<<<grid_1d(items * 32, 256), 256, 0, ctx->stream>>>(
+      dy, ldy, cout, sh, sw, hv, wv, wd, e.n_total, n, e.out, e.ldo, e.round_tf32);
+  return check_launch("up_crop_fix_dgrad_kernel");
 }
 
 // Tile shape of the TMA wgrad for a cout x n_total filter gradient
@@ -1586,9 +1769,10 @@ static WgShape wgrad_shape(const ConvGather& g, int cout, const float* dy, int l
   else if (g.stride == 2 && !g.up && k3p1 && r.sw == g.wv && r.sh == g.hv && r.sw >= 2 &&
            r.sh >= 2)
     mode = WG_STRIDE2;
-  else if (g.stride == 1 && g.up && k3p1 && g.hv == 2 * r.sh && g.wv == 2 * r.sw &&
-           g.oh == g.hv && g.ow == g.wv)
-    mode = WG_UP;
+  else if (g.stride == 1 && g.up && k3p1 && (g.hv + 1) / 2 == r.sh && (g.wv + 1) / 2 == r.sw &&
+           g.hv <= 2 * r.sh && g.wv <= 2 * r.sw && g.hv >= 2 && g.wv >= 2 && g.oh == g.hv &&
+           g.ow == g.wv)
+    mode = WG_UP;  // the x2 grid, or one cut by a row and / or column (every phase non-empty)
   if (mode < 0 || (narrow && (mode != WG_PLAIN || g.ksize != 3))) return r;
   r.narrow = narrow;
   r.gemm_n = narrow ? 9 * 32 : mode == WG_UP ? 4LL * g.cin : g.k_total;
@@ -1787,7 +1971,11 @@ yl_status conv_wgrad_ws(yl_ctx* ctx, const float* dy, int ldy, int cout, const C
     const long long n = (long long)cout * 9 * g.cin;
     wgrad_unmerge_kernel<<<grid_1d(n, 256), 256, 0, ctx->stream>>>(ws, splits, w.ws_split_stride,
                                                                    cout, g.cin, dw, accumulate);
-    return check_launch("wgrad_unmerge_kernel");
+    YL_TRY(check_launch("wgrad_unmerge_kernel"));
+    if (g.hv == 2 * sh && g.wv == 2 * sw) return YL_OK;
+    up_crop_fix_wgrad_kernel<<<grid_1d(n, 256), 256, 0, ctx->stream>>>(
+        dy, ldy, cout, g.src, g.ps, g.cin, sh, sw, g.hv, g.wv, n_img, dw);
+    return check_launch("up_crop_fix_wgrad_kernel");
   }
   const long long n = (long long)cout * g.k_total;
   splitk_reduce_kernel<<<grid_1d(n / 4 + 1, 256), 256, 0, ctx->stream>>>(ws, splits, n, dw, n,

@@ -163,7 +163,7 @@ yl_status yl_profile_conv(yl_ctx* ctx, int n, int c, int h, int w, int oc, int k
       if (mode == 0) YL_TRY(conv_fprop(ctx, g, wt, oc, e));
       if (mode == 1) {
         // an upsample conv's dX at the source resolution, as the executor runs it
-        yl_status st = up ? conv_dgrad_upsampled(ctx, dy, oc, oc, n, h, w, wd, c, ed)
+        yl_status st = up ? conv_dgrad_upsampled(ctx, dy, oc, oc, n, h, w, 2 * h, 2 * w, wd, c, ed)
                           : YL_ERR_UNSUPPORTED;
         if (st == YL_ERR_UNSUPPORTED) st = conv_fprop(ctx, gd, wd, c, ed);
         YL_TRY(st);

@@ -63,11 +63,13 @@ yl_status conv_fprop(yl_ctx* ctx, const ConvGather& g, const float* w, int n_row
                      const ConvEpilogue& e);
 
 // dX (n x sh x sw, into e) of a nearest-x2 upsample + 3x3 pad-1 conv from its
-// output gradient dy (n x 2sh x 2sw x cout, pixel stride ldy) and the dgrad
+// output gradient dy (n x hv x wv x cout, pixel stride ldy; hv in {2sh - 1,
+// 2sh}, wv in {2sw - 1, 2sw}: the x2 grid, possibly cut) and the dgrad
 // weights wd [rows][9][cout].  YL_ERR_UNSUPPORTED (nothing launched) when the
 // shapes do not fit the merged-tap path.
 yl_status conv_dgrad_upsampled(yl_ctx* ctx, const float* dy, int ldy, int cout, int n, int sh,
-                               int sw, const float* wd, int rows, const ConvEpilogue& e);
+                               int sw, int hv, int wv, const float* wd, int rows,
+                               const ConvEpilogue& e);
 
 // dW[co][k] (+)= sum_p dy[p][co] * gather(p, k), p over all m_total pixels,
 // and, when db != nullptr, db[co] (+)= sum_p dy[p][co] from the same reads.
@@ -132,8 +134,5 @@ yl_status rgb_tap_sum(yl_ctx* ctx, const float* z, int n, int h, int w, const fl
 // uh x uw, cropped) -- the adjoint of nearest upsampling into (h, w).
 yl_status downsample_sum_nhwc(yl_ctx* ctx, const float* src, int uh, int uw, float* dst, int n,
                               int h, int w, int c, int ps_src, int ps_dst);
-// dst (uh x uw, uh <= 2h, uw <= 2w) = the nearest x2 upsample of src (h x w).
-yl_status upsample_nearest_nhwc(yl_ctx* ctx, const float* src, int n, int h, int w, int c,
-                                int ps_src, float* dst, int uh, int uw, int ps_dst);
 
 }  // namespace yl

@@ -278,29 +278,6 @@ ConvGather ConvL::gather(const Act& x, int oh, int ow, int up, int hv, int wv) c
   return g;
 }
 
-// An upsample + conv whose x2 grid is cut (hv x wv smaller than 2h x 2w).
-bool ConvL::crop_up(const Act& x, int up, int hv, int wv) const {
-  return up && (hv != 2 * x.h || wv != 2 * x.w) && cin_p % 4 == 0 && x.ld % 4 == 0;
-}
-
-// x upsampled (nearest x2, cut to hv x wv) into a pool buffer.
-yl_status ConvL::upsampled(Net& net, const Act& x, int hv, int wv, Act* out) const {
-  Act u = x;
-  u.h = hv;
-  u.w = wv;
-  u.c = cin_p;
-  u.ld = cin_p;
-  YL_TRY(net.pool.get(u.elems(), &u.p));
-  const yl_status st = upsample_nearest_nhwc(net.ctx, x.p, x.n, x.h, x.w, cin_p, x.ld, u.p, hv,
-                                             wv, cin_p);
-  if (st != YL_OK) {
-    net.pool.put(u.p);
-    return st;
-  }
-  *out = u;
-  return YL_OK;
-}
-
 // The step's dominant launch type for the kernel-class timing: a stride-1 3x3
 // 128 -> 128 conv pass at the frame resolution.
 bool ConvL::dominant(const Net& net, int h, int w, int up) const {
@@ -328,12 +305,9 @@ yl_status ConvL::forward(Net& net, const Act& x, const Act& y, const float* resi
   }
   // 4 input channels (the RGB frame) take the general path: the narrow TMA
   // plan loads one zero-filled 32-channel box per tap straight from the
-  // 16-byte pixels (no patch tensor), through the halo-box kernel
-  // a cropped upsample runs as a plain conv over the upsampled input: the
-  // merged phase taps need the whole x2 grid
-  Act xu = x;
-  if (crop_up(x, up, hv, wv)) YL_TRY(upsampled(net, x, hv, wv, &xu));
-  ConvGather g = xu.p != x.p ? gather(xu, y.h, y.w, 0, 0, 0) : gather(x, y.h, y.w, up, hv, wv);
+  // 16-byte pixels (no patch tensor), through the halo-box kernel.  An
+  // upsample conv (a cut x2 grid included) runs as merged phase taps.
+  ConvGather g = gather(x, y.h, y.w, up, hv, wv);
   ConvEpilogue e;
   e.out = y.p;
   e.ldo = y.ld;
@@ -354,7 +328,6 @@ yl_status ConvL::forward(Net& net, const Act& x, const Act& y, const float* resi
   if (dominant(net, y.h, y.w, up)) net.prof_mark_dominant();
   yl_status st = conv_fprop(net.ctx, g, Wr, cout_p, e);
   net.prof_end(0, 2.0 * g.m_total * cout * cin * k * k);
-  if (xu.p != x.p) net.pool.put(xu.p);
   if (st == YL_OK && fuse_gn) gn_next->stats_ready = true;
   return st;
 }
@@ -409,20 +382,17 @@ yl_status ConvL::backward(Net& net, const Act& x, const Act& dy, const Act* dx,
     return YL_OK;
   }
   // dW (split-K tcgen05, MN-major operands) and db (fixed-order column sums)
-  Act xu = x;
-  if (crop_up(x, up, hv, wv)) YL_TRY(upsampled(net, x, hv, wv, &xu));
-  ConvGather g = xu.p != x.p ? gather(xu, dy.h, dy.w, 0, 0, 0) : gather(x, dy.h, dy.w, up, hv, wv);
+  ConvGather g = gather(x, dy.h, dy.w, up, hv, wv);
   net.prof_begin(2);
   // db comes out of the filter-gradient pass unless per-image sums are needed
-  const yl_status sw = conv_wgrad(ctx, dy.p, dy.ld, cout_p, g, gW, 0, dbias2d ? nullptr : gb);
+  YL_TRY(conv_wgrad(ctx, dy.p, dy.ld, cout_p, g, gW, 0, dbias2d ? nullptr : gb));
   net.prof_end(2, 2.0 * g.m_total * cout * cin * k * k);
-  if (xu.p != x.p) net.pool.put(xu.p);
-  YL_TRY(sw);
   if (dbias2d)
     YL_TRY(channel_sums(ctx, dy.p, dy.n, (long long)dy.h * dy.w, dy.ld, cout_p, gb, dbias2d, 0));
   if (!dx) return YL_OK;
-  if (up && !dx_addend && hv == 2 * x.h && wv == 2 * x.w && k == 3 && pad == 1 && stride == 1) {
-    // dX at the source resolution through the 16 merged phase taps
+  if (up && !dx_addend && k == 3 && pad == 1 && stride == 1) {
+    // dX at the source resolution through the 16 merged phase taps (a cut x2
+    // grid included)
     ConvEpilogue e;
     e.out = dx->p;
     e.ldo = dx->ld;
@@ -430,7 +400,7 @@ yl_status ConvL::backward(Net& net, const Act& x, const Act& dy, const Act* dx,
     e.round_tf32 = 1;
     net.prof_begin(1);
     const yl_status st =
-        conv_dgrad_upsampled(ctx, dy.p, dy.ld, cout_p, x.n, x.h, x.w, Wd, cin_p, e);
+        conv_dgrad_upsampled(ctx, dy.p, dy.ld, cout_p, x.n, x.h, x.w, hv, wv, Wd, cin_p, e);
     net.prof_end(1, 2.0 * (double)x.n * hv * wv * cout * cin * k * k);
     if (st == YL_OK) return YL_OK;
     if (st != YL_ERR_UNSUPPORTED) return st;

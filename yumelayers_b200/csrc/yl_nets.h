@@ -93,8 +93,6 @@ struct ConvL {
                      const float* dx_addend = nullptr, int ld_addend = 0,
                      float* dbias2d = nullptr, int up = 0, int hv = 0, int wv = 0);
   bool dominant(const struct Net& net, int h, int w, int up) const;
-  bool crop_up(const Act& x, int up, int hv, int wv) const;
-  yl_status upsampled(struct Net& net, const Act& x, int hv, int wv, Act* out) const;
 };
 
 struct GNL {
