@@ -52,7 +52,7 @@ CASES = [
     # the motion U-Net's cut up level (30x54 -> 60x107, 256 -> 128): merged
     # phase taps over the x2 grid, then the border terms of the cut column
     ("up_crop_unet_256_128", 2, 256, 128, 30, 54, 3, 1, 1, True, (60, 107)),
-    ("up_crop_rows_c64", 1, 64, 96, 7, 6, 3, 1, 1, True, (13, 12)),
+    ("up_crop_rows_c64", 1, 64, 128, 7, 6, 3, 1, 1, True, (13, 12)),
     # a 1x1 conv of an upsampled input: no merged 3x3 taps for its dX
     ("up_k1", 1, 32, 32, 6, 7, 1, 1, 0, True, None),
 ]
