@@ -1123,11 +1123,11 @@ __global__ void s2_phase_weights_kernel(const float* __restrict__ wd, float* __r
 // padding replaces -- and only the outputs next to the cut see them.  These
 // kernels subtract exactly those terms: a few border pixels' worth of work.
 
-// One border pixel of a cut grid of ext_h x ext_w: the last column (when
-// col) for rows [0, ext_h), then the last row (when row) for the columns the
-// column did not already cover.
-__device__ __forceinline__ void crop_border_pixel(int b, bool col, bool row, int ext_h, int ext_w,
-                                                  int* y, int* x) {
+// Border pixel b of a cut grid of ext_h x ext_w: the last column (when col)
+// for rows [0, ext_h), then the last row for the columns the column did not
+// already cover (crop_border_count counts both).
+__device__ __forceinline__ void crop_border_pixel(int b, bool col, int ext_h, int ext_w, int* y,
+                                                  int* x) {
   const int ncol = col ? ext_h : 0;
   if (b < ncol) {
     *y = b;
@@ -1136,9 +1136,9 @@ __device__ __forceinline__ void crop_border_pixel(int b, bool col, bool row, int
     *y = ext_h - 1;
     *x = b - ncol;
   }
-  (void)row;
 }
-static int crop_border_count(bool col, bool row, int ext_h, int ext_w) {
+__host__ __device__ __forceinline__ int crop_border_count(bool col, bool row, int ext_h,
+                                                           int ext_w) {
   return (col ? ext_h : 0) + (row ? ext_w - (col ? 1 : 0) : 0);
 }
 
@@ -1152,7 +1152,7 @@ __global__ void up_crop_fix_fprop_kernel(const float* __restrict__ x, int ps, in
                                          int hv, int wv, float* __restrict__ out, int ldo,
                                          int round) {
   const bool col = wv < 2 * sw, row = hv < 2 * sh;
-  const int nb = (col ? hv : 0) + (row ? wv - (col ? 1 : 0) : 0);
+  const int nb = crop_border_count(col, row, hv, wv);
   const long long items = (long long)n_img * nb * cout;
   const int lane = threadIdx.x & 31;
   const long long warps = (long long)gridDim.x * (blockDim.x >> 5);
@@ -1162,7 +1162,7 @@ __global__ void up_crop_fix_fprop_kernel(const float* __restrict__ x, int ps, in
     const long long r = it / cout;
     const int b = (int)(r % nb), img = (int)(r / nb);
     int Y, X;
-    crop_border_pixel(b, col, row, hv, wv, &Y, &X);
+    crop_border_pixel(b, col, hv, wv, &Y, &X);
     float s = 0.f;
     for (int ky = 0; ky < 3; ++ky) {
       const int yy = Y + ky - 1;
@@ -1196,7 +1196,7 @@ __global__ void up_crop_fix_dgrad_kernel(const float* __restrict__ dy, int ldy, 
                                          int cin, int n_img, float* __restrict__ dx, int ldo,
                                          int round) {
   const bool col = wv < 2 * sw, row = hv < 2 * sh;
-  const int nb = (col ? sh : 0) + (row ? sw - (col ? 1 : 0) : 0);
+  const int nb = crop_border_count(col, row, sh, sw);
   const long long items = (long long)n_img * nb * cin;
   const int lane = threadIdx.x & 31;
   const long long warps = (long long)gridDim.x * (blockDim.x >> 5);
@@ -1206,7 +1206,7 @@ __global__ void up_crop_fix_dgrad_kernel(const float* __restrict__ dy, int ldy, 
     const long long r = it / cin;
     const int b = (int)(r % nb), img = (int)(r / nb);
     int i, j;
-    crop_border_pixel(b, col, row, sh, sw, &i, &j);
+    crop_border_pixel(b, col, sh, sw, &i, &j);
     float s = 0.f;
     for (int vy = 2 * i; vy < 2 * i + 2; ++vy) {
       for (int vx = 2 * j; vx < 2 * j + 2; ++vx) {
@@ -1244,7 +1244,7 @@ __global__ void up_crop_fix_wgrad_kernel(const float* __restrict__ dy, int ldy, 
                                          int sw, int hv, int wv, int n_img,
                                          float* __restrict__ dw) {
   const bool col = wv < 2 * sw, row = hv < 2 * sh;
-  const int nb = (col ? hv : 0) + (row ? wv - (col ? 1 : 0) : 0);
+  const int nb = crop_border_count(col, row, hv, wv);
   const long long n = (long long)cout * 9 * cin;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
        i += (long long)gridDim.x * blockDim.x) {
@@ -1257,7 +1257,7 @@ __global__ void up_crop_fix_wgrad_kernel(const float* __restrict__ dy, int ldy, 
     for (int img = 0; img < n_img; ++img) {
       for (int b = 0; b < nb; ++b) {
         int Y, X;
-        crop_border_pixel(b, col, row, hv, wv, &Y, &X);
+        crop_border_pixel(b, col, hv, wv, &Y, &X);
         const int yy = Y + ky - 1, xx = X + kx - 1;
         if (yy < 0 || yy >= 2 * sh || xx < 0 || xx >= 2 * sw || (yy < hv && xx < wv)) continue;
         s += dy[(((long long)img * hv + Y) * wv + X) * ldy + co] *
