@@ -1142,131 +1142,174 @@ __host__ __device__ __forceinline__ int crop_border_count(bool col, bool row, in
   return (col ? ext_h : 0) + (row ? ext_w - (col ? 1 : 0) : 0);
 }
 
+// Taps that can reach outside u: kernel column 2 (a cut column) or row 2 (a
+// cut row) -- taps 2, 5, 8 and 6, 7 of the 3x3 kernel.
+__device__ __forceinline__ int cut_tap(int t5) { return t5 < 2 ? 2 + 3 * t5 : t5 + 4; }
+
+// The three fixes are small gathered GEMMs, C[m][n] -= sum_k A[m][k] B[k][n],
+// with k in groups of gk (a tap, or a tap and an upsampled pixel) whose
+// entries are zero where the term does not exist.  One 256-thread block per
+// 32 x 32 tile of C (and per tap for dW): k streams through shared memory in
+// 128-deep stages, each thread holding 4 outputs; a group that no row of the
+// tile uses is skipped.  Fixed summation order: the results are deterministic.
+constexpr int kCutKS = 128;
+
+template <class Op>
+__global__ void __launch_bounds__(256) cut_fix_gemm_kernel(Op op) {
+  __shared__ float As[kCutKS][33], Bs[kCutKS][33];
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  const int n0 = blockIdx.x * 32, m0 = blockIdx.y * 32, z = blockIdx.z;
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int g = 0; g < op.groups; ++g) {
+    if (!__syncthreads_or(threadIdx.x < 32 && op.live(z, m0 + (int)threadIdx.x, g))) continue;
+    for (int c0 = 0; c0 < op.gk; c0 += kCutKS) {
+#pragma unroll 4
+      for (int i = 0; i < kCutKS * 32 / 256; ++i) {
+        const int e = threadIdx.x + 256 * i;
+        int kk = Op::kAKFast ? e % kCutKS : e / 32, r = Op::kAKFast ? e / kCutKS : e % 32;
+        As[kk][r] = c0 + kk < op.gk ? op.a(z, m0 + r, g, c0 + kk) : 0.f;
+        kk = Op::kBKFast ? e % kCutKS : e / 32;
+        r = Op::kBKFast ? e / kCutKS : e % 32;
+        Bs[kk][r] = c0 + kk < op.gk ? op.b(z, g, c0 + kk, n0 + r) : 0.f;
+      }
+      __syncthreads();
+#pragma unroll 8
+      for (int kk = 0; kk < kCutKS; ++kk) {
+        const float bv = Bs[kk][tx];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[j] = fmaf(As[kk][ty + 8 * j], bv, acc[j]);
+      }
+      __syncthreads();
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < 4; ++j) op.store(z, m0 + ty + 8 * j, n0 + tx, acc[j]);
+}
+
 // Forward: out[img][Y][X][co] -= sum over taps (ky, kx) whose source pixel
 // (Y', X') = (Y + ky - 1, X + kx - 1) lies in U but not in u of
 // w[co][ky*3+kx][:] . x[img][Y'/2][X'/2][:], for the output pixels on the
-// cut row / column.  One warp per (image, border pixel, output channel),
-// lanes over input channels; rounded to tf32 again when the epilogue was.
-__global__ void up_crop_fix_fprop_kernel(const float* __restrict__ x, int ps, int sh, int sw,
-                                         int cin, const float* __restrict__ w, int cout, int n_img,
-                                         int hv, int wv, float* __restrict__ out, int ldo,
-                                         int round) {
-  const bool col = wv < 2 * sw, row = hv < 2 * sh;
-  const int nb = crop_border_count(col, row, hv, wv);
-  const long long items = (long long)n_img * nb * cout;
-  const int lane = threadIdx.x & 31;
-  const long long warps = (long long)gridDim.x * (blockDim.x >> 5);
-  for (long long it = blockIdx.x * (long long)(blockDim.x >> 5) + (threadIdx.x >> 5); it < items;
-       it += warps) {
-    const int co = (int)(it % cout);
-    const long long r = it / cout;
-    const int b = (int)(r % nb), img = (int)(r / nb);
-    int Y, X;
-    crop_border_pixel(b, col, hv, wv, &Y, &X);
-    float s = 0.f;
-    for (int ky = 0; ky < 3; ++ky) {
-      const int yy = Y + ky - 1;
-      if (yy < 0 || yy >= 2 * sh) continue;
-      for (int kx = 0; kx < 3; ++kx) {
-        const int xx = X + kx - 1;
-        if (xx < 0 || xx >= 2 * sw || (yy < hv && xx < wv)) continue;
-        const float* xp = x + (((long long)img * sh + (yy >> 1)) * sw + (xx >> 1)) * ps;
-        const float* wp = w + ((long long)co * 9 + ky * 3 + kx) * cin;
-        for (int ci = lane; ci < cin; ci += 32) s += wp[ci] * xp[ci];
-      }
-    }
-#pragma unroll
-    for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-    if (lane == 0) {
-      float* op = out + (((long long)img * hv + Y) * wv + X) * ldo + co;
-      const float v = *op - s;
-      *op = round ? round_tf32(v) : v;
-    }
+// cut row / column.  m = (image, border pixel), n = co, k = (tap, ci).
+struct CutFixFprop {
+  static constexpr bool kAKFast = true, kBKFast = true;
+  const float* x;
+  const float* w;
+  float* out;
+  int ps, sh, sw, cin, cout, hv, wv, ldo, round, nb, M;
+  bool col;
+  int groups, gk;
+  __device__ const float* src(int m, int g, int* Y, int* X) const {
+    if (m >= M) return nullptr;
+    const int img = m / nb;
+    crop_border_pixel(m - img * nb, col, hv, wv, Y, X);
+    const int tap = cut_tap(g), yy = *Y + tap / 3 - 1, xx = *X + tap % 3 - 1;
+    if (yy < 0 || yy >= 2 * sh || xx < 0 || xx >= 2 * sw || (yy < hv && xx < wv)) return nullptr;
+    return x + (((long long)img * sh + (yy >> 1)) * sw + (xx >> 1)) * ps;
   }
-}
+  __device__ bool live(int, int m, int g) const {
+    int Y, X;
+    return src(m, g, &Y, &X) != nullptr;
+  }
+  __device__ float a(int, int m, int g, int c) const {
+    int Y, X;
+    const float* p = src(m, g, &Y, &X);
+    return p ? p[c] : 0.f;
+  }
+  __device__ float b(int, int g, int c, int n) const {
+    return n < cout ? w[((long long)n * 9 + cut_tap(g)) * cin + c] : 0.f;
+  }
+  __device__ void store(int, int m, int n, float v) const {
+    if (m >= M || n >= cout) return;
+    const int img = m / nb;
+    int Y, X;
+    crop_border_pixel(m - img * nb, col, hv, wv, &Y, &X);
+    float* op = out + (((long long)img * hv + Y) * wv + X) * ldo + n;
+    const float r = *op - v;
+    *op = round ? round_tf32(r) : r;
+  }
+};
 
 // dX at the source resolution: dx[img][i][j][ci] -= the part of the merged
 // sum that comes from the upsampled pixels of U outside u, du[Y'][X'] =
 // sum_taps wd[ci][ky*3+kx][:] . dy[img][Y' - ky + 1][X' - kx + 1][:] (dy is
 // hv x wv), over (Y', X') in {2i, 2i+1} x {2j, 2j+1} with Y' >= hv or X' >= wv.
-// One warp per (image, border source pixel, input channel), lanes over the
-// output-gradient channels.
-__global__ void up_crop_fix_dgrad_kernel(const float* __restrict__ dy, int ldy, int cout, int sh,
-                                         int sw, int hv, int wv, const float* __restrict__ wd,
-                                         int cin, int n_img, float* __restrict__ dx, int ldo,
-                                         int round) {
-  const bool col = wv < 2 * sw, row = hv < 2 * sh;
-  const int nb = crop_border_count(col, row, sh, sw);
-  const long long items = (long long)n_img * nb * cin;
-  const int lane = threadIdx.x & 31;
-  const long long warps = (long long)gridDim.x * (blockDim.x >> 5);
-  for (long long it = blockIdx.x * (long long)(blockDim.x >> 5) + (threadIdx.x >> 5); it < items;
-       it += warps) {
-    const int ci = (int)(it % cin);
-    const long long r = it / cin;
-    const int b = (int)(r % nb), img = (int)(r / nb);
+// m = (image, border source pixel), n = ci, k = (pixel of the 2x2 block, tap, co).
+struct CutFixDgrad {
+  static constexpr bool kAKFast = true, kBKFast = true;
+  const float* dy;
+  const float* wd;
+  float* dx;
+  int ldy, cout, sh, sw, hv, wv, cin, ldo, round, nb, M;
+  bool col;
+  int groups, gk;
+  __device__ const float* src(int m, int g) const {
+    if (m >= M) return nullptr;
+    const int img = m / nb;
     int i, j;
-    crop_border_pixel(b, col, sh, sw, &i, &j);
-    float s = 0.f;
-    for (int vy = 2 * i; vy < 2 * i + 2; ++vy) {
-      for (int vx = 2 * j; vx < 2 * j + 2; ++vx) {
-        if (vy < hv && vx < wv) continue;  // a pixel of u: no excess
-        for (int ky = 0; ky < 3; ++ky) {
-          const int yy = vy - ky + 1;
-          if (yy < 0 || yy >= hv) continue;
-          for (int kx = 0; kx < 3; ++kx) {
-            const int xx = vx - kx + 1;
-            if (xx < 0 || xx >= wv) continue;
-            const float* dp = dy + (((long long)img * hv + yy) * wv + xx) * ldy;
-            const float* wp = wd + ((long long)ci * 9 + ky * 3 + kx) * cout;
-            for (int co = lane; co < cout; co += 32) s += wp[co] * dp[co];
-          }
-        }
-      }
-    }
-#pragma unroll
-    for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-    if (lane == 0) {
-      float* op = dx + (((long long)img * sh + i) * sw + j) * ldo + ci;
-      const float v = *op - s;
-      *op = round ? round_tf32(v) : v;
-    }
+    crop_border_pixel(m - img * nb, col, sh, sw, &i, &j);
+    const int v4 = g / 5, tap = cut_tap(g - 5 * v4);
+    const int vy = 2 * i + (v4 >> 1), vx = 2 * j + (v4 & 1);
+    if (vy < hv && vx < wv) return nullptr;  // a pixel of u: no excess
+    const int yy = vy - tap / 3 + 1, xx = vx - tap % 3 + 1;
+    if (yy < 0 || yy >= hv || xx < 0 || xx >= wv) return nullptr;
+    return dy + (((long long)img * hv + yy) * wv + xx) * ldy;
   }
-}
+  __device__ bool live(int, int m, int g) const { return src(m, g) != nullptr; }
+  __device__ float a(int, int m, int g, int c) const {
+    const float* p = src(m, g);
+    return p ? p[c] : 0.f;
+  }
+  __device__ float b(int, int g, int c, int n) const {
+    return n < cin ? wd[((long long)n * 9 + cut_tap(g % 5)) * cout + c] : 0.f;
+  }
+  __device__ void store(int, int m, int n, float v) const {
+    if (m >= M || n >= cin) return;
+    const int img = m / nb;
+    int i, j;
+    crop_border_pixel(m - img * nb, col, sh, sw, &i, &j);
+    float* op = dx + (((long long)img * sh + i) * sw + j) * ldo + n;
+    const float r = *op - v;
+    *op = round ? round_tf32(r) : r;
+  }
+};
 
 // Filter gradient: dw[co][ky*3+kx][ci] -= sum over images and the output
 // pixels (Y, X) on the cut row / column whose tap source (Y', X') lies in U
-// but not in u of dy[img][Y][X][co] * x[img][Y'/2][X'/2][ci].  Only taps with
-// ky = 2 or kx = 2 reach outside u.  One thread per (co, tap, ci), fixed
-// summation order.
-__global__ void up_crop_fix_wgrad_kernel(const float* __restrict__ dy, int ldy, int cout,
-                                         const float* __restrict__ x, int ps, int cin, int sh,
-                                         int sw, int hv, int wv, int n_img,
-                                         float* __restrict__ dw) {
-  const bool col = wv < 2 * sw, row = hv < 2 * sh;
-  const int nb = crop_border_count(col, row, hv, wv);
-  const long long n = (long long)cout * 9 * cin;
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
-       i += (long long)gridDim.x * blockDim.x) {
-    const int ci = (int)(i % cin);
-    const long long r = i / cin;
-    const int tap = (int)(r % 9), co = (int)(r / 9);
-    const int ky = tap / 3, kx = tap % 3;
-    if (ky != 2 && kx != 2) continue;
-    float s = 0.f;
-    for (int img = 0; img < n_img; ++img) {
-      for (int b = 0; b < nb; ++b) {
-        int Y, X;
-        crop_border_pixel(b, col, hv, wv, &Y, &X);
-        const int yy = Y + ky - 1, xx = X + kx - 1;
-        if (yy < 0 || yy >= 2 * sh || xx < 0 || xx >= 2 * sw || (yy < hv && xx < wv)) continue;
-        s += dy[(((long long)img * hv + Y) * wv + X) * ldy + co] *
-             x[(((long long)img * sh + (yy >> 1)) * sw + (xx >> 1)) * ps + ci];
-      }
-    }
-    dw[i] -= s;
+// but not in u of dy[img][Y][X][co] * x[img][Y'/2][X'/2][ci].  One GEMM per
+// tap that can reach outside u (blockIdx.z): m = co, n = ci, k = (image,
+// border pixel).
+struct CutFixWgrad {
+  static constexpr bool kAKFast = false, kBKFast = false;
+  const float* dy;
+  const float* x;
+  float* dw;
+  int ldy, cout, ps, cin, sh, sw, hv, wv, nb;
+  bool col;
+  int groups, gk;  // one group of n_img * nb pixels
+  __device__ bool pix(int z, int k, long long* dyo, long long* xo) const {
+    if (k >= gk) return false;
+    const int img = k / nb;
+    int Y, X;
+    crop_border_pixel(k - img * nb, col, hv, wv, &Y, &X);
+    const int tap = cut_tap(z), yy = Y + tap / 3 - 1, xx = X + tap % 3 - 1;
+    if (yy < 0 || yy >= 2 * sh || xx < 0 || xx >= 2 * sw || (yy < hv && xx < wv)) return false;
+    *dyo = (((long long)img * hv + Y) * wv + X) * ldy;
+    *xo = (((long long)img * sh + (yy >> 1)) * sw + (xx >> 1)) * ps;
+    return true;
   }
-}
+  __device__ bool live(int, int, int) const { return true; }
+  __device__ float a(int z, int m, int, int c) const {
+    long long dyo, xo;
+    return m < cout && pix(z, c, &dyo, &xo) ? dy[dyo + m] : 0.f;
+  }
+  __device__ float b(int z, int, int c, int n) const {
+    long long dyo, xo;
+    return n < cin && pix(z, c, &dyo, &xo) ? x[xo + n] : 0.f;
+  }
+  __device__ void store(int z, int m, int n, float v) const {
+    if (m < cout && n < cin) dw[((long long)m * 9 + cut_tap(z)) * cin + n] -= v;
+  }
+};
 
 // ------------------------------------------------------------------ host side
 struct View {
@@ -1638,11 +1681,26 @@ yl_status conv_fprop(yl_ctx* ctx, const ConvGather& g, const float* w, int n_row
     ConvEpilogue ec = e;
     ec.gn_mean = ec.gn_rstd = nullptr;
     YL_TRY(run_plan(ctx, &v, 1, wm, 4 * n_rows, 4 * g.cin, p, 4, ec));
-    const long long items =
-        (long long)n_img * crop_border_count(g.wv < 2 * sw, g.hv < 2 * sh, g.hv, g.wv) * e.n_total;
-    up_crop_fix_fprop_kernel<<<grid_1d(items * 32, 256), 256, 0, ctx->stream>>>(
-        g.src, g.ps, sh, sw, g.cin, w, e.n_total, n_img, g.hv, g.wv, e.out, e.ldo, e.round_tf32);
-    YL_TRY(check_launch("up_crop_fix_fprop_kernel"));
+    CutFixFprop f{};
+    f.x = g.src;
+    f.w = w;
+    f.out = e.out;
+    f.ps = g.ps;
+    f.sh = sh;
+    f.sw = sw;
+    f.cin = g.cin;
+    f.cout = e.n_total;
+    f.hv = g.hv;
+    f.wv = g.wv;
+    f.ldo = e.ldo;
+    f.round = e.round_tf32;
+    f.col = g.wv < 2 * sw;
+    f.nb = crop_border_count(f.col, g.hv < 2 * sh, g.hv, g.wv);
+    f.M = n_img * f.nb;
+    f.groups = 5;
+    f.gk = g.cin;
+    cut_fix_gemm_kernel<<<dim3((f.cout + 31) / 32, (f.M + 31) / 32), 256, 0, ctx->stream>>>(f);
+    YL_TRY(check_launch("cut_fix_gemm_kernel<CutFixFprop>"));
     if (!e.gn_mean) return YL_OK;
     return gn_stats(ctx, e.out, n_img, e.n_total, e.gn_groups, (long long)g.oh * g.ow, e.ldo,
                     e.gn_eps, 0, e.gn_mean, e.gn_rstd);
@@ -1717,11 +1775,26 @@ yl_status conv_dgrad_upsampled(yl_ctx* ctx, const float* dy, int ldy, int cout, 
   }
   YL_TRY(run_plan(ctx, v, 4, wm, rows, 16 * cout, p, 1, e));
   if (hv == 2 * sh && wv == 2 * sw) return YL_OK;
-  const long long items =
-      (long long)n * crop_border_count(wv < 2 * sw, hv < 2 * sh, sh, sw) * e.n_total;
-  up_crop_fix_dgrad_kernel<<<grid_1d(items * 32, 256), 256, 0, ctx->stream>>>(
-      dy, ldy, cout, sh, sw, hv, wv, wd, e.n_total, n, e.out, e.ldo, e.round_tf32);
-  return check_launch("up_crop_fix_dgrad_kernel");
+  CutFixDgrad f{};
+  f.dy = dy;
+  f.wd = wd;
+  f.dx = e.out;
+  f.ldy = ldy;
+  f.cout = cout;
+  f.sh = sh;
+  f.sw = sw;
+  f.hv = hv;
+  f.wv = wv;
+  f.cin = e.n_total;
+  f.ldo = e.ldo;
+  f.round = e.round_tf32;
+  f.col = wv < 2 * sw;
+  f.nb = crop_border_count(f.col, hv < 2 * sh, sh, sw);
+  f.M = n * f.nb;
+  f.groups = 20;  // 4 pixels of the 2x2 block x 5 taps
+  f.gk = cout;
+  cut_fix_gemm_kernel<<<dim3((f.cin + 31) / 32, (f.M + 31) / 32), 256, 0, ctx->stream>>>(f);
+  return check_launch("cut_fix_gemm_kernel<CutFixDgrad>");
 }
 
 // Tile shape of the TMA wgrad for a cout x n_total filter gradient
@@ -1973,9 +2046,24 @@ yl_status conv_wgrad_ws(yl_ctx* ctx, const float* dy, int ldy, int cout, const C
                                                                    cout, g.cin, dw, accumulate);
     YL_TRY(check_launch("wgrad_unmerge_kernel"));
     if (g.hv == 2 * sh && g.wv == 2 * sw) return YL_OK;
-    up_crop_fix_wgrad_kernel<<<grid_1d(n, 256), 256, 0, ctx->stream>>>(
-        dy, ldy, cout, g.src, g.ps, g.cin, sh, sw, g.hv, g.wv, n_img, dw);
-    return check_launch("up_crop_fix_wgrad_kernel");
+    CutFixWgrad f{};
+    f.dy = dy;
+    f.x = g.src;
+    f.dw = dw;
+    f.ldy = ldy;
+    f.cout = cout;
+    f.ps = g.ps;
+    f.cin = g.cin;
+    f.sh = sh;
+    f.sw = sw;
+    f.hv = g.hv;
+    f.wv = g.wv;
+    f.col = g.wv < 2 * sw;
+    f.nb = crop_border_count(f.col, g.hv < 2 * sh, g.hv, g.wv);
+    f.groups = 1;
+    f.gk = n_img * f.nb;
+    cut_fix_gemm_kernel<<<dim3((g.cin + 31) / 32, (cout + 31) / 32, 5), 256, 0, ctx->stream>>>(f);
+    return check_launch("cut_fix_gemm_kernel<CutFixWgrad>");
   }
   const long long n = (long long)cout * g.k_total;
   splitk_reduce_kernel<<<grid_1d(n / 4 + 1, 256), 256, 0, ctx->stream>>>(ws, splits, n, dw, n,
