@@ -1147,40 +1147,81 @@ __host__ __device__ __forceinline__ int crop_border_count(bool col, bool row, in
 __device__ __forceinline__ int cut_tap(int t5) { return t5 < 2 ? 2 + 3 * t5 : t5 + 4; }
 
 // The three fixes are small gathered GEMMs, C[m][n] -= sum_k A[m][k] B[k][n],
-// with k in groups of gk (a tap, or a tap and an upsampled pixel) whose
-// entries are zero where the term does not exist.  One 256-thread block per
-// 32 x 32 tile of C (and per tap for dW): k streams through shared memory in
-// 128-deep stages, each thread holding 4 outputs; a group that no row of the
-// tile uses is skipped.  Fixed summation order: the results are deterministic.
+// whose missing terms read as zero.  One 256-thread block per 32 x 32 tile
+// of C: k streams through shared memory in 128-deep stages, each thread
+// holding 4 outputs, and the gather offsets are worked out once per tap group
+// (rows) or per stage (columns) into shared memory.  Fixed summation order:
+// the results are deterministic.
 constexpr int kCutKS = 128;
 
+__device__ __forceinline__ void cut_fix_stage_fma(const float (&As)[kCutKS][33],
+                                                  const float (&Bs)[kCutKS][33], int tx, int ty,
+                                                  float (&acc)[4]) {
+#pragma unroll 8
+  for (int kk = 0; kk < kCutKS; ++kk) {
+    const float bv = Bs[kk][tx];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[j] = fmaf(As[kk][ty + 8 * j], bv, acc[j]);
+  }
+}
+
+// Row gathers: C[m][n] -= sum over groups g and c < gk of
+// A[arow(m, g) + c] * B[brow(n, g) + c] (an offset of -1 is a missing row).
 template <class Op>
-__global__ void __launch_bounds__(256) cut_fix_gemm_kernel(Op op) {
+__global__ void __launch_bounds__(256) cut_fix_rows_kernel(Op op) {
   __shared__ float As[kCutKS][33], Bs[kCutKS][33];
+  __shared__ long long ao[32], bo[32];
   const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
-  const int n0 = blockIdx.x * 32, m0 = blockIdx.y * 32, z = blockIdx.z;
+  const int n0 = blockIdx.x * 32, m0 = blockIdx.y * 32;
   float acc[4] = {0.f, 0.f, 0.f, 0.f};
   for (int g = 0; g < op.groups; ++g) {
-    if (!__syncthreads_or(threadIdx.x < 32 && op.live(z, m0 + (int)threadIdx.x, g))) continue;
+    if (threadIdx.x < 32) ao[threadIdx.x] = op.arow(m0 + (int)threadIdx.x, g);
+    else if (threadIdx.x < 64) bo[threadIdx.x - 32] = op.brow(n0 + (int)threadIdx.x - 32, g);
+    // a group no row of this tile uses is skipped (the barrier publishes ao / bo)
+    if (!__syncthreads_or(threadIdx.x < 32 && ao[threadIdx.x] >= 0)) continue;
     for (int c0 = 0; c0 < op.gk; c0 += kCutKS) {
 #pragma unroll 4
       for (int i = 0; i < kCutKS * 32 / 256; ++i) {
-        const int e = threadIdx.x + 256 * i;
-        int kk = Op::kAKFast ? e % kCutKS : e / 32, r = Op::kAKFast ? e / kCutKS : e % 32;
-        As[kk][r] = c0 + kk < op.gk ? op.a(z, m0 + r, g, c0 + kk) : 0.f;
-        kk = Op::kBKFast ? e % kCutKS : e / 32;
-        r = Op::kBKFast ? e / kCutKS : e % 32;
-        Bs[kk][r] = c0 + kk < op.gk ? op.b(z, g, c0 + kk, n0 + r) : 0.f;
+        const int e = threadIdx.x + 256 * i, kk = e % kCutKS, r = e / kCutKS;
+        const bool in = c0 + kk < op.gk;
+        As[kk][r] = in && ao[r] >= 0 ? op.A[ao[r] + c0 + kk] : 0.f;
+        Bs[kk][r] = in && bo[r] >= 0 ? op.B[bo[r] + c0 + kk] : 0.f;
       }
       __syncthreads();
-#pragma unroll 8
-      for (int kk = 0; kk < kCutKS; ++kk) {
-        const float bv = Bs[kk][tx];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) acc[j] = fmaf(As[kk][ty + 8 * j], bv, acc[j]);
-      }
+      cut_fix_stage_fma(As, Bs, tx, ty, acc);
       __syncthreads();
     }
+  }
+#pragma unroll
+  for (int j = 0; j < 4; ++j) op.store(m0 + ty + 8 * j, n0 + tx, acc[j]);
+}
+
+// Column gathers (one GEMM per tap, blockIdx.z): C[m][n] -= sum over k < gk
+// of A[acol(k) + m] * B[bcol(k) + n] (-1: the term does not exist).
+template <class Op>
+__global__ void __launch_bounds__(256) cut_fix_cols_kernel(Op op) {
+  __shared__ float As[kCutKS][33], Bs[kCutKS][33];
+  __shared__ long long ao[kCutKS], bo[kCutKS];
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  const int n0 = blockIdx.x * 32, m0 = blockIdx.y * 32, z = blockIdx.z;
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int k0 = 0; k0 < op.gk; k0 += kCutKS) {
+    if (threadIdx.x < kCutKS) {
+      long long a = -1, b = -1;
+      op.cols(z, k0 + (int)threadIdx.x, &a, &b);
+      ao[threadIdx.x] = a;
+      bo[threadIdx.x] = b;
+    }
+    if (!__syncthreads_or(threadIdx.x < kCutKS && ao[threadIdx.x] >= 0)) continue;
+#pragma unroll 4
+    for (int i = 0; i < kCutKS * 32 / 256; ++i) {
+      const int e = threadIdx.x + 256 * i, r = e % 32, kk = e / 32;
+      As[kk][r] = ao[kk] >= 0 && m0 + r < op.M ? op.A[ao[kk] + m0 + r] : 0.f;
+      Bs[kk][r] = bo[kk] >= 0 && n0 + r < op.N ? op.B[bo[kk] + n0 + r] : 0.f;
+    }
+    __syncthreads();
+    cut_fix_stage_fma(As, Bs, tx, ty, acc);
+    __syncthreads();
   }
 #pragma unroll
   for (int j = 0; j < 4; ++j) op.store(z, m0 + ty + 8 * j, n0 + tx, acc[j]);
@@ -1189,36 +1230,28 @@ __global__ void __launch_bounds__(256) cut_fix_gemm_kernel(Op op) {
 // Forward: out[img][Y][X][co] -= sum over taps (ky, kx) whose source pixel
 // (Y', X') = (Y + ky - 1, X + kx - 1) lies in U but not in u of
 // w[co][ky*3+kx][:] . x[img][Y'/2][X'/2][:], for the output pixels on the
-// cut row / column.  m = (image, border pixel), n = co, k = (tap, ci).
+// cut row / column.  m = (image, border pixel), n = co, groups = taps,
+// c = ci.  A = x, B = w [cout][9][cin].
 struct CutFixFprop {
-  static constexpr bool kAKFast = true, kBKFast = true;
-  const float* x;
-  const float* w;
+  const float* A;
+  const float* B;
   float* out;
   int ps, sh, sw, cin, cout, hv, wv, ldo, round, nb, M;
   bool col;
   int groups, gk;
-  __device__ const float* src(int m, int g, int* Y, int* X) const {
-    if (m >= M) return nullptr;
+  __device__ long long arow(int m, int g) const {
+    if (m >= M) return -1;
     const int img = m / nb;
-    crop_border_pixel(m - img * nb, col, hv, wv, Y, X);
-    const int tap = cut_tap(g), yy = *Y + tap / 3 - 1, xx = *X + tap % 3 - 1;
-    if (yy < 0 || yy >= 2 * sh || xx < 0 || xx >= 2 * sw || (yy < hv && xx < wv)) return nullptr;
-    return x + (((long long)img * sh + (yy >> 1)) * sw + (xx >> 1)) * ps;
-  }
-  __device__ bool live(int, int m, int g) const {
     int Y, X;
-    return src(m, g, &Y, &X) != nullptr;
+    crop_border_pixel(m - img * nb, col, hv, wv, &Y, &X);
+    const int tap = cut_tap(g), yy = Y + tap / 3 - 1, xx = X + tap % 3 - 1;
+    if (yy < 0 || yy >= 2 * sh || xx < 0 || xx >= 2 * sw || (yy < hv && xx < wv)) return -1;
+    return (((long long)img * sh + (yy >> 1)) * sw + (xx >> 1)) * ps;
   }
-  __device__ float a(int, int m, int g, int c) const {
-    int Y, X;
-    const float* p = src(m, g, &Y, &X);
-    return p ? p[c] : 0.f;
+  __device__ long long brow(int n, int g) const {
+    return n < cout ? ((long long)n * 9 + cut_tap(g)) * cin : -1;
   }
-  __device__ float b(int, int g, int c, int n) const {
-    return n < cout ? w[((long long)n * 9 + cut_tap(g)) * cin + c] : 0.f;
-  }
-  __device__ void store(int, int m, int n, float v) const {
+  __device__ void store(int m, int n, float v) const {
     if (m >= M || n >= cout) return;
     const int img = m / nb;
     int Y, X;
@@ -1233,36 +1266,31 @@ struct CutFixFprop {
 // sum that comes from the upsampled pixels of U outside u, du[Y'][X'] =
 // sum_taps wd[ci][ky*3+kx][:] . dy[img][Y' - ky + 1][X' - kx + 1][:] (dy is
 // hv x wv), over (Y', X') in {2i, 2i+1} x {2j, 2j+1} with Y' >= hv or X' >= wv.
-// m = (image, border source pixel), n = ci, k = (pixel of the 2x2 block, tap, co).
+// m = (image, border source pixel), n = ci, groups = (pixel of the 2x2
+// block, tap), c = co.  A = dy, B = wd [cin][9][cout].
 struct CutFixDgrad {
-  static constexpr bool kAKFast = true, kBKFast = true;
-  const float* dy;
-  const float* wd;
+  const float* A;
+  const float* B;
   float* dx;
   int ldy, cout, sh, sw, hv, wv, cin, ldo, round, nb, M;
   bool col;
   int groups, gk;
-  __device__ const float* src(int m, int g) const {
-    if (m >= M) return nullptr;
+  __device__ long long arow(int m, int g) const {
+    if (m >= M) return -1;
     const int img = m / nb;
     int i, j;
     crop_border_pixel(m - img * nb, col, sh, sw, &i, &j);
     const int v4 = g / 5, tap = cut_tap(g - 5 * v4);
     const int vy = 2 * i + (v4 >> 1), vx = 2 * j + (v4 & 1);
-    if (vy < hv && vx < wv) return nullptr;  // a pixel of u: no excess
+    if (vy < hv && vx < wv) return -1;  // a pixel of u: no excess
     const int yy = vy - tap / 3 + 1, xx = vx - tap % 3 + 1;
-    if (yy < 0 || yy >= hv || xx < 0 || xx >= wv) return nullptr;
-    return dy + (((long long)img * hv + yy) * wv + xx) * ldy;
+    if (yy < 0 || yy >= hv || xx < 0 || xx >= wv) return -1;
+    return (((long long)img * hv + yy) * wv + xx) * ldy;
   }
-  __device__ bool live(int, int m, int g) const { return src(m, g) != nullptr; }
-  __device__ float a(int, int m, int g, int c) const {
-    const float* p = src(m, g);
-    return p ? p[c] : 0.f;
+  __device__ long long brow(int n, int g) const {
+    return n < cin ? ((long long)n * 9 + cut_tap(g % 5)) * cout : -1;
   }
-  __device__ float b(int, int g, int c, int n) const {
-    return n < cin ? wd[((long long)n * 9 + cut_tap(g % 5)) * cout + c] : 0.f;
-  }
-  __device__ void store(int, int m, int n, float v) const {
+  __device__ void store(int m, int n, float v) const {
     if (m >= M || n >= cin) return;
     const int img = m / nb;
     int i, j;
@@ -1277,37 +1305,26 @@ struct CutFixDgrad {
 // pixels (Y, X) on the cut row / column whose tap source (Y', X') lies in U
 // but not in u of dy[img][Y][X][co] * x[img][Y'/2][X'/2][ci].  One GEMM per
 // tap that can reach outside u (blockIdx.z): m = co, n = ci, k = (image,
-// border pixel).
+// border pixel).  A = dy, B = x.
 struct CutFixWgrad {
-  static constexpr bool kAKFast = false, kBKFast = false;
-  const float* dy;
-  const float* x;
+  const float* A;
+  const float* B;
   float* dw;
-  int ldy, cout, ps, cin, sh, sw, hv, wv, nb;
+  int ldy, M, ps, N, sh, sw, hv, wv, nb;  // M = cout, N = cin
   bool col;
-  int groups, gk;  // one group of n_img * nb pixels
-  __device__ bool pix(int z, int k, long long* dyo, long long* xo) const {
-    if (k >= gk) return false;
+  int gk;  // n_img * nb
+  __device__ void cols(int z, int k, long long* ao, long long* bo) const {
+    if (k >= gk) return;
     const int img = k / nb;
     int Y, X;
     crop_border_pixel(k - img * nb, col, hv, wv, &Y, &X);
     const int tap = cut_tap(z), yy = Y + tap / 3 - 1, xx = X + tap % 3 - 1;
-    if (yy < 0 || yy >= 2 * sh || xx < 0 || xx >= 2 * sw || (yy < hv && xx < wv)) return false;
-    *dyo = (((long long)img * hv + Y) * wv + X) * ldy;
-    *xo = (((long long)img * sh + (yy >> 1)) * sw + (xx >> 1)) * ps;
-    return true;
-  }
-  __device__ bool live(int, int, int) const { return true; }
-  __device__ float a(int z, int m, int, int c) const {
-    long long dyo, xo;
-    return m < cout && pix(z, c, &dyo, &xo) ? dy[dyo + m] : 0.f;
-  }
-  __device__ float b(int z, int, int c, int n) const {
-    long long dyo, xo;
-    return n < cin && pix(z, c, &dyo, &xo) ? x[xo + n] : 0.f;
+    if (yy < 0 || yy >= 2 * sh || xx < 0 || xx >= 2 * sw || (yy < hv && xx < wv)) return;
+    *ao = (((long long)img * hv + Y) * wv + X) * ldy;
+    *bo = (((long long)img * sh + (yy >> 1)) * sw + (xx >> 1)) * ps;
   }
   __device__ void store(int z, int m, int n, float v) const {
-    if (m < cout && n < cin) dw[((long long)m * 9 + cut_tap(z)) * cin + n] -= v;
+    if (m < M && n < N) dw[((long long)m * 9 + cut_tap(z)) * N + n] -= v;
   }
 };
 
@@ -1682,8 +1699,8 @@ yl_status conv_fprop(yl_ctx* ctx, const ConvGather& g, const float* w, int n_row
     ec.gn_mean = ec.gn_rstd = nullptr;
     YL_TRY(run_plan(ctx, &v, 1, wm, 4 * n_rows, 4 * g.cin, p, 4, ec));
     CutFixFprop f{};
-    f.x = g.src;
-    f.w = w;
+    f.A = g.src;
+    f.B = w;
     f.out = e.out;
     f.ps = g.ps;
     f.sh = sh;
@@ -1699,8 +1716,8 @@ yl_status conv_fprop(yl_ctx* ctx, const ConvGather& g, const float* w, int n_row
     f.M = n_img * f.nb;
     f.groups = 5;
     f.gk = g.cin;
-    cut_fix_gemm_kernel<<<dim3((f.cout + 31) / 32, (f.M + 31) / 32), 256, 0, ctx->stream>>>(f);
-    YL_TRY(check_launch("cut_fix_gemm_kernel<CutFixFprop>"));
+    cut_fix_rows_kernel<<<dim3((f.cout + 31) / 32, (f.M + 31) / 32), 256, 0, ctx->stream>>>(f);
+    YL_TRY(check_launch("cut_fix_rows_kernel<CutFixFprop>"));
     if (!e.gn_mean) return YL_OK;
     return gn_stats(ctx, e.out, n_img, e.n_total, e.gn_groups, (long long)g.oh * g.ow, e.ldo,
                     e.gn_eps, 0, e.gn_mean, e.gn_rstd);
@@ -1776,8 +1793,8 @@ yl_status conv_dgrad_upsampled(yl_ctx* ctx, const float* dy, int ldy, int cout, 
   YL_TRY(run_plan(ctx, v, 4, wm, rows, 16 * cout, p, 1, e));
   if (hv == 2 * sh && wv == 2 * sw) return YL_OK;
   CutFixDgrad f{};
-  f.dy = dy;
-  f.wd = wd;
+  f.A = dy;
+  f.B = wd;
   f.dx = e.out;
   f.ldy = ldy;
   f.cout = cout;
@@ -1793,8 +1810,8 @@ yl_status conv_dgrad_upsampled(yl_ctx* ctx, const float* dy, int ldy, int cout, 
   f.M = n * f.nb;
   f.groups = 20;  // 4 pixels of the 2x2 block x 5 taps
   f.gk = cout;
-  cut_fix_gemm_kernel<<<dim3((f.cin + 31) / 32, (f.M + 31) / 32), 256, 0, ctx->stream>>>(f);
-  return check_launch("cut_fix_gemm_kernel<CutFixDgrad>");
+  cut_fix_rows_kernel<<<dim3((f.cin + 31) / 32, (f.M + 31) / 32), 256, 0, ctx->stream>>>(f);
+  return check_launch("cut_fix_rows_kernel<CutFixDgrad>");
 }
 
 // Tile shape of the TMA wgrad for a cout x n_total filter gradient
@@ -2047,23 +2064,22 @@ yl_status conv_wgrad_ws(yl_ctx* ctx, const float* dy, int ldy, int cout, const C
     YL_TRY(check_launch("wgrad_unmerge_kernel"));
     if (g.hv == 2 * sh && g.wv == 2 * sw) return YL_OK;
     CutFixWgrad f{};
-    f.dy = dy;
-    f.x = g.src;
+    f.A = dy;
+    f.B = g.src;
     f.dw = dw;
     f.ldy = ldy;
-    f.cout = cout;
+    f.M = cout;
     f.ps = g.ps;
-    f.cin = g.cin;
+    f.N = g.cin;
     f.sh = sh;
     f.sw = sw;
     f.hv = g.hv;
     f.wv = g.wv;
     f.col = g.wv < 2 * sw;
     f.nb = crop_border_count(f.col, g.hv < 2 * sh, g.hv, g.wv);
-    f.groups = 1;
     f.gk = n_img * f.nb;
-    cut_fix_gemm_kernel<<<dim3((g.cin + 31) / 32, (cout + 31) / 32, 5), 256, 0, ctx->stream>>>(f);
-    return check_launch("cut_fix_gemm_kernel<CutFixWgrad>");
+    cut_fix_cols_kernel<<<dim3((g.cin + 31) / 32, (cout + 31) / 32, 5), 256, 0, ctx->stream>>>(f);
+    return check_launch("cut_fix_cols_kernel<CutFixWgrad>");
   }
   const long long n = (long long)cout * g.k_total;
   splitk_reduce_kernel<<<grid_1d(n / 4 + 1, 256), 256, 0, ctx->stream>>>(ws, splits, n, dw, n,
