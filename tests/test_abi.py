@@ -47,3 +47,22 @@ def test_status_text_without_gpu():
     st = L.yl_ctx_create(0, None)
     assert st != 0
     assert len(L.yl_last_error_message()) > 0
+
+
+def test_conv_output_shapes_and_cut_grids_without_gpu():
+    """yl_conv2d_out_shape is host arithmetic: the output extents of plain,
+    stride-2 and upsample convs, and which upsampled sizes an upsample conv
+    accepts -- the x2 grid or one cut by a row and / or column (the decoder's
+    odd-size crop, ConvGPU.swift:393), nothing else."""
+    from yumelayers_b200._lib import YumeError
+    from yumelayers_b200.ops import conv_desc, conv_out_shape
+    assert conv_out_shape(conv_desc((2, 32, 64, 64), 32)) == (64, 64)
+    assert conv_out_shape(conv_desc((1, 16, 15, 17), 24, 3, 2, 1)) == (8, 9)
+    assert conv_out_shape(conv_desc((1, 16, 15, 17), 24, 1, 1, 0)) == (15, 17)
+    assert conv_out_shape(conv_desc((2, 256, 30, 54), 128, up=True)) == (60, 108)
+    assert conv_out_shape(conv_desc((2, 256, 30, 54), 128, up=True, up_hw=(60, 107))) == (60, 107)
+    assert conv_out_shape(conv_desc((1, 32, 1, 5), 32, up=True, up_hw=(1, 9))) == (1, 9)
+    for bad in ((60, 109), (61, 108), (58, 108), (60, 106)):
+        with pytest.raises(YumeError) as ei:
+            conv_out_shape(conv_desc((2, 256, 30, 54), 128, up=True, up_hw=bad))
+        assert ei.value.status == 1  # YL_ERR_SHAPE
