@@ -1,6 +1,10 @@
 """Generates tests/golden/prototype_golden.npz from the reference's own
 PyTorch prototype (src/diffusion.py:6-10 timestep_embedding, src/vae.py:7-15
-ResBlock with SiLU).  Run where the reference checkout is available:
+ResBlock with SiLU, and the decoder's / encoder's stages src/vae.py:44-45
+Decoder._up -- ResBlock, nearest x2 upsample, 3x3 conv, SiLU -- and
+src/vae.py:27-28 Encoder._down -- ResBlock, stride-2 3x3 conv, SiLU -- with
+their autograd gradients for an upstream gradient g).  Run where the
+reference checkout is available:
 
     python tests/golden/make_golden.py /path/to/YumeLayers
 
@@ -17,7 +21,7 @@ import torch
 def main(ref_root: str) -> None:
     sys.path.insert(0, str(Path(ref_root) / "src"))
     from diffusion import timestep_embedding  # noqa: E402  (reference prototype)
-    from vae import ResBlock  # noqa: E402
+    from vae import Decoder, Encoder, ResBlock  # noqa: E402
 
     torch.manual_seed(0)
     rng = np.random.default_rng(0)
@@ -29,12 +33,33 @@ def main(ref_root: str) -> None:
     with torch.no_grad():
         y = block(torch.tensor(x)).numpy()
     conv1, conv2 = block.net[0], block.net[2]
-    out = Path(__file__).resolve().parent / "prototype_golden.npz"
-    np.savez_compressed(
-        out, temb_t=t, temb_out=temb.astype(np.float32), rb_x=x,
+    arrays = dict(
+        temb_t=t, temb_out=temb.astype(np.float32), rb_x=x,
         rb_w1=conv1.weight.detach().numpy(), rb_b1=conv1.bias.detach().numpy(),
         rb_w2=conv2.weight.detach().numpy(), rb_b2=conv2.bias.detach().numpy(),
         rb_y=y.astype(np.float32))
+    # one decoder stage (8 -> 4 channels, 5x6 -> 10x12) and one encoder stage
+    # (8 -> 16 channels, 7x9 -> 4x5), forward and backward
+    stages = (("up", Decoder(base=4)._up(8, 4), (2, 8, 5, 6)),
+              ("down", Encoder(base=4)._down(8, 16), (2, 8, 7, 9)))
+    for name, stage, shape in stages:
+        xs = torch.tensor(rng.standard_normal(shape).astype(np.float32), requires_grad=True)
+        ys = stage(xs)
+        g = torch.tensor(rng.standard_normal(tuple(ys.shape)).astype(np.float32))
+        (ys * g).sum().backward()
+        rb = stage[0].net
+        conv = stage[2] if name == "up" else stage[1]
+        for key, mod in (("rb_w1", rb[0]), ("rb_w2", rb[2]), ("w", conv)):
+            arrays[f"{name}_{key}"] = mod.weight.detach().numpy()
+            arrays[f"{name}_{key.replace('w', 'b')}"] = mod.bias.detach().numpy()
+            arrays[f"{name}_d{key}"] = mod.weight.grad.numpy()
+            arrays[f"{name}_d{key.replace('w', 'b')}"] = mod.bias.grad.numpy()
+        arrays[f"{name}_x"] = xs.detach().numpy()
+        arrays[f"{name}_y"] = ys.detach().numpy()
+        arrays[f"{name}_g"] = g.numpy()
+        arrays[f"{name}_dx"] = xs.grad.numpy()
+    out = Path(__file__).resolve().parent / "prototype_golden.npz"
+    np.savez_compressed(out, **arrays)
     print("wrote", out)
 
 

@@ -374,3 +374,42 @@ def test_resblock_golden(oracle):
     oracle.orc_unary(6, ptr(h), ptr(hs), h.size)
     y = conv2d_fwd(oracle, hs, w2, b2, residual=x)
     assert rel_l2(y, g["rb_y"]) < 1e-5
+
+
+def _silu(oracle, z):
+    out = np.empty_like(z)
+    oracle.orc_unary(6, ptr(z), ptr(out), z.size)
+    return out
+
+
+def _silu_grad(oracle, z, g):
+    out = np.empty_like(z)
+    oracle.orc_binary(5, ptr(f32(z)), ptr(f32(g)), ptr(out), z.size)
+    return out
+
+
+@pytest.mark.parametrize("name", ["up", "down"])
+def test_decoder_and_encoder_stage_golden(oracle, name):
+    """One stage of the prototype's decoder (src/vae.py:44-45: ResBlock, nearest
+    x2 upsample, 3x3 conv, SiLU) or encoder (src/vae.py:27-28: ResBlock,
+    stride-2 3x3 conv, SiLU), forward and backward (torch autograd for an
+    upstream gradient g), against the oracle's conv / SiLU layer math: the
+    upsample conv's dX is the 2x2 sum of the upsampled-input gradient, the
+    stride-2 conv's the col2im gather."""
+    g = np.load(GOLDEN / "prototype_golden.npz")
+    k = lambda s: f32(g[f"{name}_{s}"])  # noqa: E731
+    up, stride = name == "up", 1 if name == "up" else 2
+    x = k("x")
+    h = conv2d_fwd(oracle, x, k("rb_w1"), k("rb_b1"))
+    hs = _silu(oracle, h)
+    r = conv2d_fwd(oracle, hs, k("rb_w2"), k("rb_b2"), residual=x)
+    p = conv2d_fwd(oracle, r, k("w"), k("b"), stride=stride, up=up)
+    y = _silu(oracle, p)
+    assert rel_l2(y, k("y")) < 1e-5
+    dp = _silu_grad(oracle, p, k("g"))
+    dr, dw, db, _ = conv2d_bwd(oracle, r, k("w"), dp, stride=stride, up=up)
+    dhs, dw2, db2, _ = conv2d_bwd(oracle, hs, k("rb_w2"), dr)
+    dx1, dw1, db1, _ = conv2d_bwd(oracle, x, k("rb_w1"), _silu_grad(oracle, h, dhs))
+    for got, key in ((dw, "dw"), (db, "db"), (dw2, "drb_w2"), (db2, "drb_b2"), (dw1, "drb_w1"),
+                     (db1, "drb_b1"), (dx1 + dr, "dx")):
+        assert rel_l2(got, k(key)) < 1e-5, key
