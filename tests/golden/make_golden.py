@@ -3,8 +3,10 @@ PyTorch prototype (src/diffusion.py:6-10 timestep_embedding, src/vae.py:7-15
 ResBlock with SiLU, and the decoder's / encoder's stages src/vae.py:44-45
 Decoder._up -- ResBlock, nearest x2 upsample, 3x3 conv, SiLU -- and
 src/vae.py:27-28 Encoder._down -- ResBlock, stride-2 3x3 conv, SiLU -- with
-their autograd gradients for an upstream gradient g).  Run where the
-reference checkout is available:
+their autograd gradients for an upstream gradient g; and the time
+conditioning of src/diffusion.py:38,49 -- DiT.time_mlp, Linear -> SiLU ->
+Linear, over timestep_embedding -- with its weight gradients).  Run where
+the reference checkout is available:
 
     python tests/golden/make_golden.py /path/to/YumeLayers
 
@@ -20,7 +22,8 @@ import torch
 
 def main(ref_root: str) -> None:
     sys.path.insert(0, str(Path(ref_root) / "src"))
-    from diffusion import timestep_embedding  # noqa: E402  (reference prototype)
+    from config import Config  # noqa: E402  (reference prototype)
+    from diffusion import DiT, timestep_embedding  # noqa: E402
     from vae import Decoder, Encoder, ResBlock  # noqa: E402
 
     torch.manual_seed(0)
@@ -58,6 +61,22 @@ def main(ref_root: str) -> None:
         arrays[f"{name}_y"] = ys.detach().numpy()
         arrays[f"{name}_g"] = g.numpy()
         arrays[f"{name}_dx"] = xs.grad.numpy()
+    # the DiT's time conditioning at its default width (128)
+    cfg = Config()
+    mlp = DiT(cfg).time_mlp
+    tt = torch.tensor(rng.uniform(0, 200, 5).astype(np.float32))
+    emb = timestep_embedding(tt, cfg.dif_dim)
+    ym = mlp(emb)
+    gm = torch.tensor(rng.standard_normal(tuple(ym.shape)).astype(np.float32))
+    (ym * gm).sum().backward()
+    for key, mod in (("w1", mlp[0]), ("w2", mlp[2])):
+        arrays[f"tmlp_{key}"] = mod.weight.detach().numpy()
+        arrays[f"tmlp_{key.replace('w', 'b')}"] = mod.bias.detach().numpy()
+        arrays[f"tmlp_d{key}"] = mod.weight.grad.numpy()
+        arrays[f"tmlp_d{key.replace('w', 'b')}"] = mod.bias.grad.numpy()
+    arrays["tmlp_t"] = tt.numpy()
+    arrays["tmlp_y"] = ym.detach().numpy()
+    arrays["tmlp_g"] = gm.numpy()
     out = Path(__file__).resolve().parent / "prototype_golden.npz"
     np.savez_compressed(out, **arrays)
     print("wrote", out)

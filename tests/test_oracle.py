@@ -413,3 +413,29 @@ def test_decoder_and_encoder_stage_golden(oracle, name):
     for got, key in ((dw, "dw"), (db, "db"), (dw2, "drb_w2"), (db2, "drb_b2"), (dw1, "drb_w1"),
                      (db1, "drb_b1"), (dx1 + dr, "dx")):
         assert rel_l2(got, k(key)) < 1e-5, key
+
+
+def test_time_conditioning_mlp_golden(oracle):
+    """The prototype's time conditioning (src/diffusion.py:38,49: DiT.time_mlp,
+    Linear -> SiLU -> Linear, over timestep_embedding(t, 128)), forward and the
+    weight gradients for an upstream gradient g, from the oracle's embedding,
+    Linear and SiLU."""
+    g = np.load(GOLDEN / "prototype_golden.npz")
+    k = lambda s: f32(g[f"tmlp_{s}"])  # noqa: E731
+    t = k("t")
+    n, d = t.size, 128
+    emb = np.empty((n, d), np.float32)
+    oracle.orc_timestep_embedding_torch(ptr(t), n, d, 10000.0, ptr(emb))
+    h = np.empty((n, d), np.float32)
+    oracle.orc_linear_fwd(ptr(emb), ptr(k("w1")), ptr(k("b1")), ptr(h), n, d, d, 0)
+    hs = _silu(oracle, h)
+    y = np.empty((n, d), np.float32)
+    oracle.orc_linear_fwd(ptr(hs), ptr(k("w2")), ptr(k("b2")), ptr(y), n, d, d, 0)
+    assert rel_l2(y, k("y")) < 1e-5
+    dhs, dw2, db2 = np.empty_like(hs), np.empty((d, d), np.float32), np.empty(d, np.float32)
+    oracle.orc_linear_bwd(ptr(hs), ptr(k("w2")), ptr(k("g")), ptr(dhs), ptr(dw2), ptr(db2), n, d, d)
+    dh = _silu_grad(oracle, h, dhs)
+    dw1, db1 = np.empty((d, d), np.float32), np.empty(d, np.float32)
+    oracle.orc_linear_bwd(ptr(emb), ptr(k("w1")), ptr(dh), None, ptr(dw1), ptr(db1), n, d, d)
+    for got, key in ((dw2, "dw2"), (db2, "db2"), (dw1, "dw1"), (db1, "db1")):
+        assert rel_l2(got, k(key)) < 1e-5, key
