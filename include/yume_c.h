@@ -197,7 +197,8 @@ yl_status yl_adam_update(yl_ctx* ctx, float* param, const float* grad, float* m,
 /* Conv2d geometry.  The input is (n, c, h, w); with up = 1 it is the source
  * of a nearest x2 upsample cropped to (up_h, up_w) (the decoder's
  * "upsample2x + conv", ConvGPU.swift:380-399), read without materialising the
- * upsampled tensor.  Output size: (in + 2*pad - k)/stride + 1 per axis
+ * upsampled tensor; up_h is 2h or 2h - 1 and up_w is 2w or 2w - 1 (anything
+ * else is YL_ERR_SHAPE).  Output size: (in + 2*pad - k)/stride + 1 per axis
  * (ConvGPU.swift:58-59).  Weights are (oc, c, k, k) = the reference's
  * (oc, ic*k*k) (ConvGPU.swift:18); bias has oc entries. */
 typedef struct yl_conv_desc {
