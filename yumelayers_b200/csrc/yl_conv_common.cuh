@@ -31,7 +31,6 @@ __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
   return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
 }
 
-
 // Fixed-order split-K reduction and tensor-map helpers
 // Fixed-order sum of split-K partials: out[i] (+)= sum_s ws[s][i].
 static __global__ void splitk_reduce_kernel(const float* __restrict__ ws, int splits, long long stride,
@@ -90,34 +89,5 @@ static yl_status make_weight_tmap(CUtensorMap* tm, const float* w, int rows, int
   YL_CHECK(r == CUDA_SUCCESS, YL_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
   return YL_OK;
 }
-
-// Tensor map over an NHWC activation {c, w, h, n} with pixel stride ps
-// (floats); box {32 channels, box_w, box_h, 1}; out-of-range reads are zero.
-static yl_status make_act_tmap(CUtensorMap* tm, const float* base, int c, int w, int h, int n,
-                               int ps, int box_w, int box_h, CUtensorMapSwizzle swz) {
-  auto fn = get_encode_fn();
-  YL_CHECK(fn, YL_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
-  YL_CHECK(((uintptr_t)base & 15) == 0 && ps % 4 == 0, YL_ERR_INVALID,
-           "activation tensor map: base/stride alignment");
-  cuuint64_t dims[4] = {(cuuint64_t)c, (cuuint64_t)w, (cuuint64_t)h, (cuuint64_t)n};
-  cuuint64_t strides[3] = {(cuuint64_t)ps * 4, (cuuint64_t)w * ps * 4,
-                           (cuuint64_t)h * w * ps * 4};
-  cuuint32_t box[4] = {32, (cuuint32_t)box_w, (cuuint32_t)box_h, 1};
-  cuuint32_t estr[4] = {1, 1, 1, 1};
-  CUresult r = fn(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, const_cast<float*>(base), dims, strides,
-                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
-                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  YL_CHECK(r == CUDA_SUCCESS, YL_ERR_CUDA, "cuTensorMapEncodeTiled (activation) failed (%d)",
-           (int)r);
-  return YL_OK;
-}
-
-// The source of `g` is a dense NHWC tensor of hv x wv pixels (what the TMA
-// paths need: rectangular boxes, no upsample, stride 1).
-static bool dense_source(const ConvGather& g) {
-  return g.stride == 1 && !g.up && g.row_stride == g.wv * g.ps &&
-         g.img_stride == (long long)g.hv * g.wv * g.ps && ((uintptr_t)g.src & 15) == 0;
-}
-
 
 }  // namespace yl

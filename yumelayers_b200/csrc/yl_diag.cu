@@ -96,7 +96,8 @@ yl_status yl_profile_conv(yl_ctx* ctx, int n, int c, int h, int w, int oc, int k
   const int ih = up ? 2 * h : h, iw = up ? 2 * w : w;
   const int oh = (ih + 2 * pad - k) / stride + 1, ow = (iw + 2 * pad - k) / stride + 1;
   DevBufs b;
-  float *x, *wt, *wd, *y, *dy, *dx, *dw;
+  float *x = nullptr, *wt = nullptr, *wd = nullptr, *y = nullptr, *dy = nullptr, *dx = nullptr,
+        *dw = nullptr;
   YL_TRY(b.get((size_t)n * h * w * c, &x));
   YL_TRY(b.get((size_t)oc * k * k * c, &wt));
   YL_TRY(b.get((size_t)oc * k * k * c, &wd));
@@ -190,7 +191,7 @@ yl_status yl_profile_adam(yl_ctx* ctx, long long n, int tensors, int reps, doubl
   YL_CHECK(ctx && ms_out && reps >= 1 && n > 0 && tensors >= 1 && tensors <= 48, YL_ERR_INVALID,
            "yl_profile_adam: bad argument");
   DevBufs b;
-  float *p, *g, *m, *v;
+  float *p = nullptr, *g = nullptr, *m = nullptr, *v = nullptr;
   YL_TRY(b.get((size_t)n, &p));
   YL_TRY(b.get((size_t)n, &g));
   YL_TRY(b.get((size_t)n, &m));
@@ -229,7 +230,8 @@ yl_status yl_profile_groupnorm(yl_ctx* ctx, int n, int c, int h, int w, int reps
   YL_CHECK(ctx && fwd_ms && bwd_ms && reps >= 1, YL_ERR_INVALID, "yl_profile_groupnorm");
   const long long e = (long long)n * h * w * c;
   DevBufs b;
-  float *x, *y, *dy, *dx, *g, *bt, *dg, *db, *m, *r;
+  float *x = nullptr, *y = nullptr, *dy = nullptr, *dx = nullptr, *g = nullptr, *bt = nullptr,
+        *dg = nullptr, *db = nullptr, *m = nullptr, *r = nullptr;
   YL_TRY(b.get(e, &x));
   YL_TRY(b.get(e, &y));
   YL_TRY(b.get(e, &dy));
@@ -279,7 +281,7 @@ yl_status yl_profile_layered(yl_ctx* ctx, int n, long long plane, int reps, doub
   YL_CHECK(ctx && ms_out && reps >= 1 && n >= 1 && plane >= 1, YL_ERR_INVALID,
            "yl_profile_layered: bad argument");
   DevBufs b;
-  float *r, *t, *c, *g, *l;
+  float *r = nullptr, *t = nullptr, *c = nullptr, *g = nullptr, *l = nullptr;
   const long long e8 = (long long)n * 8 * plane, e3 = (long long)n * 3 * plane;
   YL_TRY(b.get((size_t)e8, &r));
   YL_TRY(b.get((size_t)e8, &t));
